@@ -1,0 +1,225 @@
+/*
+ * speccache_b200.h — C ABI of the B200 (sm_100a) KV-restore library for SpecCache Path-1.
+ *
+ * Library: libspeccache_b200.so (built in-tree next to the Python package).
+ *
+ * Conventions shared by every entry point
+ * ---------------------------------------
+ *  - Plain pointers, sizes and element strides only; no framework types.
+ *  - Device pointers are CUDA device (or managed) addresses on the current device.
+ *    ``stream`` is a ``cudaStream_t`` passed as ``void*`` (NULL = legacy default stream).
+ *  - Work is enqueued on ``stream`` and never synchronised by the library (the pipeline's
+ *    explicit synchronise call excepted).
+ *  - Every call returns an ``sc_status``; nothing throws across the ABI and nothing
+ *    aborts the process.  ``sc_last_error()`` returns a per-thread message for the last
+ *    failing call on that thread.
+ *  - Stride arrays are host arrays, counted in elements.
+ *  - Thread safety: calls on distinct streams may run concurrently from distinct host
+ *    threads; one ``sc_pipeline`` object must be driven by one thread at a time.
+ *
+ * Arithmetic contract (parity with the reference's eager path)
+ * ------------------------------------------------------------
+ *  Keys:    x = fp16(q * s)  [rounded to fp16 first, speccache/kernels/reference.py:257]
+ *           out[i]       = cvt(x[i]      * cos[i] - x[i+D/2] * sin[i])
+ *           out[i + D/2] = cvt(x[i+D/2]  * cos[i] + x[i]     * sin[i])   (fp32 math)
+ *           with SC_FLAG_FP32_INTERMEDIATE the fp16 rounding of x is skipped
+ *           (the arithmetic of speccache/kernels/triton_rope_kv.py:150-158).
+ *  Values:  out = cvt(q * s)                                        (reference.py:302)
+ *  Tables:  cos/sin[i] = fp16(cos|sin(fp32(dp) * inv_freq[i])),
+ *           inv_freq[i] = 1 / theta^(2i/D) in float32             (reference.py:151-164)
+ *  Quantize: scale = fp16(max(amax / 127, eps)) with IEEE division,
+ *            q = clamp(round_half_even(x / scale), -127, 127)       (reference.py:200-204)
+ *  cvt is round-to-nearest-even into the output dtype (fp16, or bf16 as an extension).
+ */
+#ifndef SPECCACHE_B200_H
+#define SPECCACHE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SC_ABI_VERSION 1
+
+/* Every entry point is exported with default visibility; the library is built with
+ * -fvisibility=hidden so that nothing else leaks out of it. */
+#if defined(__GNUC__)
+#define SC_API __attribute__((visibility("default")))
+#else
+#define SC_API
+#endif
+
+/* Status codes.  The Python layer maps them to the reference's exception types. */
+typedef enum sc_status {
+    SC_OK = 0,
+    SC_ERR_INVALID_ARGUMENT = 1, /* shape / size / stride / alignment problem (ValueError) */
+    SC_ERR_INVALID_DTYPE = 2,    /* unsupported dtype code (TypeError)                     */
+    SC_ERR_CUDA = 3,             /* a CUDA runtime call failed (RuntimeError)              */
+    SC_ERR_OUT_OF_RANGE = 4,     /* a device-side index check tripped (page id, length)    */
+    SC_ERR_TIMEOUT = 5,          /* a bounded wait ran out                                 */
+    SC_ERR_HOST_ALLOC = 6,       /* pinned host allocation failed                          */
+    SC_ERR_UNSUPPORTED = 7       /* valid request this build does not implement            */
+} sc_status;
+
+/* Element type codes. */
+typedef enum sc_dtype {
+    SC_DTYPE_F16 = 0,
+    SC_DTYPE_BF16 = 1,
+    SC_DTYPE_F32 = 2
+} sc_dtype;
+
+/* Flags for the restore entry points. */
+#define SC_FLAG_FP32_INTERMEDIATE 0x1u /* keep q*s in fp32 before the rotation            */
+#define SC_FLAG_FORCE_GENERIC 0x2u     /* use the stride-generic kernel (testing aid)      */
+
+/* Device status bits written (atomicOr) by the paged kernels into a caller-given word. */
+#define SC_STATUS_BAD_PAGE_ID 0x1    /* page-table entry outside [0, n_pool_pages)          */
+#define SC_STATUS_BAD_SEQ_LEN 0x2    /* seq_len < 0 or > max_pages * page_size              */
+#define SC_STATUS_BAD_OUT_OFFSET 0x4 /* output offset misaligned or rows beyond out_numel    */
+
+/* Message for the last failing call on this host thread ("" if none). */
+SC_API const char* sc_last_error(void);
+
+/* SC_ABI_VERSION of the loaded library. */
+SC_API int32_t sc_abi_version(void);
+
+/*
+ * cos/sin tables for relative RoPE shifts.
+ * Replaces compute_rope_cos_sin_delta (speccache/kernels/reference.py:122-165).
+ *
+ *  delta_pos  device float32 [n] (the shifts, already converted to float32)
+ *  inv_freq   host float32 [head_dim/2], or NULL to compute 1/theta^(2i/D) here
+ *  cos_out, sin_out  device [n, head_dim/2] contiguous, dtype out_dtype (F16 | BF16 | F32)
+ */
+SC_API int32_t sc_rope_cos_sin_delta(const float* delta_pos, int64_t n, int32_t head_dim,
+                              double theta_base, const float* inv_freq, void* cos_out,
+                              void* sin_out, int32_t out_dtype, void* stream);
+
+/*
+ * Fused INT8 K dequant + relative RoPE shift and INT8 V dequant, one launch for both.
+ * Replaces triton_fused_k_dequant_rope_shift (speccache/kernels/triton_rope_kv.py:243-345),
+ * dequant_value (triton_rope_kv.py:352-411) and dequant_kv_cache (triton_rope_kv.py:414-427).
+ *
+ * Geometry: n_layers x n_tokens x n_heads rows of head_dim (head_dim even).
+ *  k_quant / v_quant  int8, strides [layer, token, head, dim]; either may be NULL to skip it
+ *  k_scale / v_scale  scale_dtype (F16 as in the reference, or F32), strides [layer, token, head]
+ *  cos_delta/sin_delta  fp16 tables, strides [token, dim]; token stride 0 broadcasts one
+ *                     row ([1, D/2]); a non-zero token stride gives one row per token
+ *                     ([T, D/2]).  Pass NULL for both to use delta_p instead.
+ *  delta_p            the shift when no table is given (converted to float32 like the
+ *                     reference); if delta_p_dev (device float32 scalar) is non-NULL it
+ *                     is read on the device instead.
+ *  theta_base, inv_freq  as for sc_rope_cos_sin_delta (only used without tables)
+ *  k_out / v_out      out_dtype (F16 | BF16), strides [layer, token, head, dim]
+ */
+SC_API int32_t sc_dequant_rope_kv(int32_t n_layers, int64_t n_tokens, int32_t n_heads,
+                           int32_t head_dim, const int8_t* k_quant, const int64_t* kq_strides,
+                           const void* k_scale, const int64_t* ks_strides,
+                           const int8_t* v_quant, const int64_t* vq_strides,
+                           const void* v_scale, const int64_t* vs_strides, int32_t scale_dtype,
+                           const void* cos_delta, const void* sin_delta,
+                           const int64_t* cs_strides, double delta_p, const float* delta_p_dev,
+                           double theta_base, const float* inv_freq, void* k_out,
+                           const int64_t* ko_strides, void* v_out, const int64_t* vo_strides,
+                           int32_t out_dtype, uint32_t flags, void* stream);
+
+/*
+ * Per-(token, head) absmax INT8 quantisation (the offload twin).
+ * Replaces quantize_kv_int8 / quantize_symmetric_int8 (speccache/kernels/reference.py:179-209).
+ *
+ *  x        [n_tokens, n_heads, head_dim], dtype x_dtype (F16 | BF16 | F32), strides [t, h, d]
+ *  q_out    int8, strides [t, h, d]
+ *  scale_out  dtype scale_dtype (F16 as in the reference, or F32), strides [t, h]
+ */
+SC_API int32_t sc_quantize_int8(int64_t n_tokens, int32_t n_heads, int32_t head_dim, const void* x,
+                         int32_t x_dtype, const int64_t* x_strides, float eps, int8_t* q_out,
+                         const int64_t* q_strides, void* scale_out, int32_t scale_dtype,
+                         const int64_t* s_strides, uint32_t flags, void* stream);
+
+/*
+ * Ragged, paged restore: gather each request's pages from a device page pool, dequantise,
+ * shift keys by the request's (or page's) delta_p and write contiguous per-request caches.
+ * Replaces the host gather of PinnedKVPool.get_coalesced_views
+ * (speccache/cache/pinned_pool.py:392-464) followed by the per-chunk kernels of
+ * SpecCacheEngine.execute_async_dma_and_rope (speccache/cache/engine.py:441-601).
+ *
+ *  pool_kq / pool_vq   int8  [n_pool_pages, page_size, n_heads, head_dim] contiguous
+ *  pool_ks / pool_vs   fp16  [n_pool_pages, page_size, n_heads] contiguous
+ *  page_table          device int32 [n_requests, page_table_stride] (first max_pages used)
+ *  seq_lens            device int32 [n_requests]
+ *  delta_p             device float32 [n_requests] or, with delta_p_per_page,
+ *                      [n_requests, max_pages]
+ *  out_offsets         device int64 [n_requests]: element offset of request r's token 0
+ *  out_strides         [token, head, dim] of the outputs (dim stride must be 1)
+ *  out_numel           elements in each of k_out / v_out; a request whose rows would
+ *                      fall outside is skipped and flagged (SC_STATUS_BAD_OUT_OFFSET)
+ *  status              device int32 word; SC_STATUS_* bits are OR-ed in when an entry is
+ *                      rejected (the offending page is skipped, nothing faults).  Required.
+ */
+SC_API int32_t sc_restore_paged(int32_t n_requests, int32_t max_pages, int32_t page_size,
+                         int32_t n_heads, int32_t head_dim, int64_t n_pool_pages,
+                         const int8_t* pool_kq, const void* pool_ks, const int8_t* pool_vq,
+                         const void* pool_vs, const int32_t* page_table,
+                         int64_t page_table_stride, const int32_t* seq_lens,
+                         const float* delta_p, int32_t delta_p_per_page, double theta_base,
+                         const float* inv_freq, void* k_out, void* v_out,
+                         const int64_t* out_offsets, const int64_t* out_strides,
+                         int64_t out_numel, int32_t out_dtype, int32_t* status, uint32_t flags,
+                         void* stream);
+
+/*
+ * Multi-layer pinned-host -> GPU restore pipeline.
+ * Replaces the pinned slabs of MultiLayerKVInjector (speccache/serving/kv_injector.py:171-215)
+ * and its reconstruct_and_inject_multi_layer (kv_injector.py:392-498), and the
+ * double-buffered DMA loop of SpecCacheEngine.execute_async_dma_and_rope
+ * (speccache/cache/engine.py:441-601).
+ *
+ * Host slabs (pinned, owned by the pipeline), per layer l and block b:
+ *    k_quant/v_quant  int8 [n_layers, n_blocks, chunk_size, n_heads, head_dim]
+ *    k_scale/v_scale  fp16 [n_layers, n_blocks, chunk_size, n_heads]
+ * A restore copies, for each layer, the requested blocks (one cudaMemcpyAsync per run of
+ * consecutive block ids and tensor) on the pipeline's transfer stream into one of n_slots
+ * device staging slots, and runs the restore kernel for that layer on compute_stream once
+ * its copy event has fired, so layer l+1's copy overlaps layer l's kernel.
+ */
+typedef struct sc_pipeline sc_pipeline;
+
+#define SC_PIPE_NUMA_LOCAL 0x1u /* allocate the slabs from a thread bound to the GPU's NUMA node */
+
+SC_API int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t n_blocks,
+                           int32_t chunk_size, int32_t n_heads, int32_t head_dim,
+                           int64_t max_restore_blocks, int32_t n_slots, uint32_t flags,
+                           sc_pipeline** out);
+
+/* Pinned host slab addresses (see layout above). */
+SC_API int32_t sc_pipeline_host_slabs(const sc_pipeline* p, int8_t** k_quant, void** k_scale,
+                               int8_t** v_quant, void** v_scale);
+
+/*
+ * Enqueue one restore of n_blocks blocks for every layer.
+ *  block_ids, delta_ps  host int32 [n_blocks]; delta_ps[i] shifts block i's keys
+ *  k_out, v_out         host arrays of n_layers device pointers; token i*chunk_size+c of
+ *                       layer l goes to k_out[l] + (i*chunk_size + c)*st + h*sh + d
+ *  out_strides          [token, head, dim] (dim stride 1)
+ *  out_numel            elements of each k_out[l] / v_out[l] buffer (bounds check)
+ * Returns once everything is enqueued; completion is ordered on compute_stream.
+ */
+SC_API int32_t sc_pipeline_restore(sc_pipeline* p, const int32_t* block_ids, const int32_t* delta_ps,
+                            int32_t n_blocks, double theta_base, const float* inv_freq,
+                            void* const* k_out, void* const* v_out, const int64_t* out_strides,
+                            int64_t out_numel, int32_t out_dtype, void* compute_stream);
+
+/* Wait (bounded by timeout_s, polling) for the last restore; SC_ERR_TIMEOUT if it ran out. */
+SC_API int32_t sc_pipeline_synchronize(sc_pipeline* p, double timeout_s);
+
+/* Read and clear the device status word of the pipeline's kernels (synchronises). */
+SC_API int32_t sc_pipeline_status(sc_pipeline* p, int32_t* status_bits);
+
+SC_API int32_t sc_pipeline_destroy(sc_pipeline* p);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPECCACHE_B200_H */

@@ -1,0 +1,151 @@
+"""Pinned-host -> GPU multi-layer KV restore pipeline (C++ in ``libspeccache_b200.so``).
+
+Python face of ``sc_pipeline_*``: it owns pinned host slabs laid out like the
+reference's unified multi-layer slabs (speccache/serving/kv_injector.py:171-192,
+``[L, blocks, chunk, H, D]`` int8 and ``[L, blocks, chunk, H, 1]`` fp16), and restores a
+list of blocks for every layer: per layer, H2D copies (one per run of consecutive block
+ids) on its own transfer stream into a ring of device slots, joined by events to the
+restore kernel on the caller's current stream, so layer l+1's copy overlaps layer l's
+kernel.  This replaces the Python loops of
+``MultiLayerKVInjector.reconstruct_and_inject_multi_layer`` (kv_injector.py:392-498)
+and ``SpecCacheEngine.execute_async_dma_and_rope`` (speccache/cache/engine.py:441-601).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from .. import _lib
+
+
+def _host_view(addr: int, shape: tuple[int, ...], np_dtype, torch_dtype=None) -> torch.Tensor:
+    n = int(np.prod(shape))
+    ctype = {np.int8: ctypes.c_int8, np.int16: ctypes.c_int16}[np_dtype]
+    arr = np.ctypeslib.as_array((ctype * n).from_address(addr)).reshape(shape)
+    t = torch.from_numpy(arr)
+    return t.view(torch_dtype) if torch_dtype is not None else t
+
+
+class KVRestorePipeline:
+    """Multi-layer restore from pinned host slabs into per-layer GPU caches.
+
+    Args:
+        num_layers, num_blocks, chunk_size, num_kv_heads, head_dim: slab geometry.
+        device: CUDA device of the restore.
+        max_restore_blocks: most blocks one restore may ask for (sizes the device slots);
+            default ``num_blocks``.
+        n_slots: device staging slots (2 = double buffering).
+        numa_local: allocate the slabs from a thread bound to the GPU's NUMA node.
+    """
+
+    def __init__(self, num_layers: int, num_blocks: int, chunk_size: int, num_kv_heads: int,
+                 head_dim: int, *, device: torch.device | str | int | None = None,
+                 max_restore_blocks: int | None = None, n_slots: int = 2,
+                 numa_local: bool = True) -> None:
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        device = torch.device(device if not isinstance(device, int) else f"cuda:{device}")
+        if device.type != "cuda":
+            raise RuntimeError(f"KVRestorePipeline needs a CUDA device, got {device}")
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.device = device
+        self.num_layers, self.num_blocks = int(num_layers), int(num_blocks)
+        self.chunk_size, self.num_kv_heads, self.head_dim = int(chunk_size), int(num_kv_heads), int(head_dim)
+        self.max_restore_blocks = int(max_restore_blocks or num_blocks)
+        self._lib = _lib.load()
+        handle = ctypes.c_void_p()
+        flags = _lib.SC_PIPE_NUMA_LOCAL if numa_local else 0
+        rc = self._lib.sc_pipeline_create(device.index, self.num_layers, self.num_blocks,
+                                          self.chunk_size, self.num_kv_heads, self.head_dim,
+                                          self.max_restore_blocks, int(n_slots), flags,
+                                          ctypes.byref(handle))
+        _lib.check(rc, "sc_pipeline_create")
+        self._h = handle
+        ptrs = [ctypes.c_void_p() for _ in range(4)]
+        _lib.check(self._lib.sc_pipeline_host_slabs(self._h, *[ctypes.byref(p) for p in ptrs]),
+                   "sc_pipeline_host_slabs")
+        codes = (self.num_layers, self.num_blocks, self.chunk_size, self.num_kv_heads, self.head_dim)
+        scales = codes[:4] + (1,)
+        self.k_quant = _host_view(ptrs[0].value, codes, np.int8)
+        self.k_scale = _host_view(ptrs[1].value, scales, np.int16, torch.float16)
+        self.v_quant = _host_view(ptrs[2].value, codes, np.int8)
+        self.v_scale = _host_view(ptrs[3].value, scales, np.int16, torch.float16)
+
+    # -- host slab access ---------------------------------------------------------------
+    def write_block(self, layer: int, block_id: int, k_quant: torch.Tensor, k_scale: torch.Tensor,
+                    v_quant: torch.Tensor, v_scale: torch.Tensor) -> None:
+        """Copy one quantised chunk ``[chunk, H, D]`` / ``[chunk, H, 1]`` into the slabs."""
+        self.k_quant[layer, block_id].copy_(k_quant)
+        self.k_scale[layer, block_id].copy_(k_scale)
+        self.v_quant[layer, block_id].copy_(v_quant)
+        self.v_scale[layer, block_id].copy_(v_scale)
+
+    # -- restore --------------------------------------------------------------------------
+    def restore(self, block_ids, delta_ps, k_out: list[torch.Tensor], v_out: list[torch.Tensor],
+                *, theta: float = 10000.0) -> None:
+        """Enqueue the restore of ``block_ids`` (block i shifted by ``delta_ps[i]``) for
+        every layer.  ``k_out[l]`` / ``v_out[l]`` are ``[n*chunk, H, D]`` fp16/bf16 views
+        (any token/head strides, unit dim stride) that all share one layout.  Completion is
+        ordered on the current CUDA stream; nothing blocks."""
+        ids = np.ascontiguousarray(np.asarray(block_ids, dtype=np.int32).reshape(-1))
+        dps = np.ascontiguousarray(np.asarray(delta_ps, dtype=np.int64).reshape(-1))
+        if ids.size != dps.size:
+            raise ValueError(f"{ids.size} block ids but {dps.size} shifts")
+        if np.any(np.abs(dps) >= 2**31):
+            raise ValueError("shifts must fit in int32")
+        dps32 = dps.astype(np.int32)
+        if len(k_out) != self.num_layers or len(v_out) != self.num_layers:
+            raise ValueError(f"need {self.num_layers} K and V outputs")
+        n_tok = ids.size * self.chunk_size
+        ref = k_out[0]
+        if ref.dtype not in (torch.float16, torch.bfloat16):
+            raise TypeError(f"outputs must be float16 or bfloat16, got {ref.dtype}")
+        for o in list(k_out) + list(v_out):
+            if (o.shape != (n_tok, self.num_kv_heads, self.head_dim) or o.stride() != ref.stride()
+                    or o.dtype != ref.dtype or o.device != self.device):
+                raise ValueError(
+                    f"outputs must be [{n_tok}, {self.num_kv_heads}, {self.head_dim}] {ref.dtype} "
+                    f"views on {self.device} sharing one layout")
+        numel = min(o.untyped_storage().nbytes() // o.element_size() - o.storage_offset()
+                    for o in list(k_out) + list(v_out))
+        kp = (ctypes.c_void_p * self.num_layers)(*[o.data_ptr() for o in k_out])
+        vp = (ctypes.c_void_p * self.num_layers)(*[o.data_ptr() for o in v_out])
+        rc = self._lib.sc_pipeline_restore(
+            self._h, ids.ctypes.data, dps32.ctypes.data, int(ids.size), float(theta),
+            _lib.inv_freq_ptr(self.head_dim, theta), kp, vp, _lib.strides(*ref.stride()), numel,
+            _lib.DTYPE_CODE[ref.dtype], _lib.stream_handle(self.device))
+        _lib.check(rc, "sc_pipeline_restore")
+
+    def synchronize(self, timeout: float = 60.0) -> None:
+        """Wait for the last restore, polling; raises TimeoutError after ``timeout`` s."""
+        _lib.check(self._lib.sc_pipeline_synchronize(self._h, float(timeout)), "sc_pipeline_synchronize")
+
+    def status(self) -> int:
+        """Device status bits of the restore kernels (0 = clean); reading clears them."""
+        bits = ctypes.c_int32(0)
+        rc = self._lib.sc_pipeline_status(self._h, ctypes.byref(bits))
+        if rc not in (_lib.SC_OK, _lib.SC_ERR_OUT_OF_RANGE):
+            _lib.check(rc, "sc_pipeline_status")
+        return int(bits.value)
+
+    def close(self) -> None:
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            self._lib.sc_pipeline_destroy(h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self) -> None:  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self) -> "KVRestorePipeline":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()

@@ -1,0 +1,215 @@
+// sc_common.cuh — shared device helpers for the sm_100a KV-restore kernels.
+//
+// Everything here is elementwise, HBM-bound integer/half arithmetic: 16-byte vector
+// loads of INT8 codes, exact int8 -> fp16 conversion by exponent-bias arithmetic,
+// fp16/fp32 dequantisation and the rotate-half RoPE step, packed 16-byte stores.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "sc_internal.h"
+
+namespace sc {
+
+// ---------------------------------------------------------------------------------------
+// Unsigned 32-bit division by a run-time constant (Granlund-Montgomery round-up method).
+// Valid for numerators < 2^31, which every launch guarantees (rows < 2^31).
+// ---------------------------------------------------------------------------------------
+struct FastDiv {
+    uint32_t d;
+    uint32_t m;
+    uint32_t s;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+    FastDiv f{d, 0u, 0u};
+    uint32_t l = 0;
+    while ((1ull << l) < d) ++l;
+    f.s = l;
+    // m = floor(2^32 * (2^l - d) / d) + 1
+    f.m = static_cast<uint32_t>(((1ull << 32) * ((1ull << l) - d)) / d + 1ull);
+    return f;
+}
+
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
+    const uint32_t t = __umulhi(n, f.m);
+    return (t + n) >> f.s;
+}
+
+// ---------------------------------------------------------------------------------------
+// Memory access.  Inputs are read once: non-coherent loads that do not allocate in L1.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ void st_v4(void* p, const uint4& v) {
+    asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ void st_v2(void* p, const uint2& v) {
+    asm volatile("st.global.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ T bit_cast_u32(uint32_t u);
+template <>
+__device__ __forceinline__ __half2 bit_cast_u32<__half2>(uint32_t u) {
+    return *reinterpret_cast<__half2*>(&u);
+}
+__device__ __forceinline__ uint32_t u32_of(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ uint32_t u32_of(__nv_bfloat162 h) {
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// ---------------------------------------------------------------------------------------
+// Exact int8 -> fp16 for four codes packed in one 32-bit word.
+// Flip the sign bit so each byte holds code+128 in [0, 255]; splice each byte under the
+// fp16 exponent pattern 0x64 (0x64XX == 1024 + XX exactly) and subtract 1152 = 1024+128.
+// Three integer/half instructions per two codes, no type-conversion unit involved.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ void i8x4_to_h2(uint32_t w, __half2& lo, __half2& hi) {
+    const uint32_t u = w ^ 0x80808080u;
+    const uint32_t a = __byte_perm(u, 0x64646464u, 0x4140);
+    const uint32_t b = __byte_perm(u, 0x64646464u, 0x4342);
+    const __half2 bias = bit_cast_u32<__half2>(0x64806480u);  // (1152, 1152)
+    lo = __hsub2(bit_cast_u32<__half2>(a), bias);
+    hi = __hsub2(bit_cast_u32<__half2>(b), bias);
+}
+
+// Output packing: two fp32 values -> one 32-bit word of the output dtype (RN-even).
+template <typename OutT>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+    return u32_of(__floats2half2_rn(a, b));
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+    return u32_of(__floats2bfloat162_rn(a, b));
+}
+
+template <typename OutT>
+__device__ __forceinline__ OutT from_float(float a);
+template <>
+__device__ __forceinline__ __half from_float<__half>(float a) {
+    return __float2half_rn(a);
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float a) {
+    return __float2bfloat16_rn(a);
+}
+
+template <typename ScaleT>
+__device__ __forceinline__ float scale_to_float(ScaleT s);
+template <>
+__device__ __forceinline__ float scale_to_float<__half>(__half s) {
+    return __half2float(s);
+}
+template <>
+__device__ __forceinline__ float scale_to_float<float>(float s) {
+    return s;
+}
+
+// cos/sin of one relative shift for frequency f, rounded like the reference's tables:
+// angle = fp32(dp * inv_freq) (one fp32 multiply); cos/sin evaluated in double, rounded
+// to fp32, then to fp16.  Returns the fp16 values widened back to fp32.
+__device__ __forceinline__ void rope_cs(float dp, float inv_freq, float& c, float& s) {
+    const float angle = __fmul_rn(dp, inv_freq);
+    double sd, cd;
+    sincos(static_cast<double>(angle), &sd, &cd);
+    c = __half2float(__float2half_rn(static_cast<float>(cd)));
+    s = __half2float(__float2half_rn(static_cast<float>(sd)));
+}
+
+// ---------------------------------------------------------------------------------------
+// One 16-frequency slice of one row: 16 key codes of the first half (a) and their 16
+// rotate-half partners of the second half (b), the row scale, the slice's cos/sin.
+// Writes 16 outputs at o1 (first half) and 16 at o2 (second half).
+//   X16 = true : x = fp16(q*s) first (reference eager arithmetic; exact because q*s is
+//                exact in fp32 and __hmul2_rn rounds it once)
+//   X16 = false: x = q*s kept in fp32
+// ---------------------------------------------------------------------------------------
+template <typename OutT, typename ScaleT, bool X16>
+__device__ __forceinline__ void rope_slice_store(const uint4& a, const uint4& b, ScaleT scale,
+                                                 const float* __restrict__ cs,
+                                                 const float* __restrict__ sn, void* o1,
+                                                 void* o2) {
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+    const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+    uint32_t r1[8], r2[8];
+    const float sf = scale_to_float<ScaleT>(scale);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        __half2 qa[2], qb[2];
+        i8x4_to_h2(aw[w], qa[0], qa[1]);
+        i8x4_to_h2(bw[w], qb[0], qb[1]);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            float2 x1, x2;
+            if constexpr (X16 && sizeof(ScaleT) == 2) {
+                const __half2 s2 = __half2half2(*reinterpret_cast<const __half*>(&scale));
+                x1 = __half22float2(__hmul2_rn(qa[k], s2));
+                x2 = __half22float2(__hmul2_rn(qb[k], s2));
+            } else {
+                const float2 fa = __half22float2(qa[k]);
+                const float2 fb = __half22float2(qb[k]);
+                x1 = make_float2(__fmul_rn(fa.x, sf), __fmul_rn(fa.y, sf));
+                x2 = make_float2(__fmul_rn(fb.x, sf), __fmul_rn(fb.y, sf));
+                if constexpr (X16) {
+                    x1 = __half22float2(__floats2half2_rn(x1.x, x1.y));
+                    x2 = __half22float2(__floats2half2_rn(x2.x, x2.y));
+                }
+            }
+            const int e = w * 4 + k * 2;
+            const float c0 = cs[e], c1 = cs[e + 1], s0 = sn[e], s1 = sn[e + 1];
+            const float o1a = fmaf(x1.x, c0, -(x2.x * s0));
+            const float o1b = fmaf(x1.y, c1, -(x2.y * s1));
+            const float o2a = fmaf(x2.x, c0, x1.x * s0);
+            const float o2b = fmaf(x2.y, c1, x1.y * s1);
+            r1[w * 2 + k] = pack2<OutT>(o1a, o1b);
+            r2[w * 2 + k] = pack2<OutT>(o2a, o2b);
+        }
+    }
+    st_v4(o1, make_uint4(r1[0], r1[1], r1[2], r1[3]));
+    st_v4(reinterpret_cast<char*>(o1) + 16, make_uint4(r1[4], r1[5], r1[6], r1[7]));
+    st_v4(o2, make_uint4(r2[0], r2[1], r2[2], r2[3]));
+    st_v4(reinterpret_cast<char*>(o2) + 16, make_uint4(r2[4], r2[5], r2[6], r2[7]));
+}
+
+// 16 value codes -> 16 outputs of cvt(q*s).
+template <typename OutT, typename ScaleT>
+__device__ __forceinline__ void value_slice_store(const uint4& a, ScaleT scale, void* o) {
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+    uint32_t r[8];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        __half2 q[2];
+        i8x4_to_h2(aw[w], q[0], q[1]);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            if constexpr (sizeof(ScaleT) == 2 && sizeof(OutT) == 2 &&
+                          std::is_same<OutT, __half>::value) {
+                const __half2 s2 = __half2half2(*reinterpret_cast<const __half*>(&scale));
+                r[w * 2 + k] = u32_of(__hmul2_rn(q[k], s2));
+            } else {
+                const float sf = scale_to_float<ScaleT>(scale);
+                const float2 f = __half22float2(q[k]);
+                r[w * 2 + k] = pack2<OutT>(__fmul_rn(f.x, sf), __fmul_rn(f.y, sf));
+            }
+        }
+    }
+    st_v4(o, make_uint4(r[0], r[1], r[2], r[3]));
+    st_v4(reinterpret_cast<char*>(o) + 16, make_uint4(r[4], r[5], r[6], r[7]));
+}
+
+}  // namespace sc

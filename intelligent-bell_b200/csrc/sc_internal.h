@@ -1,0 +1,63 @@
+// sc_internal.h — host-side internals shared by the library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/speccache_b200.h"
+
+namespace sc {
+
+// Record a message for sc_last_error() on this host thread and return `code`.
+int32_t set_error(int32_t code, const char* fmt, ...)
+#if defined(__GNUC__)
+    __attribute__((format(printf, 2, 3)))
+#endif
+    ;
+
+// Clear the per-thread message (successful call).
+int32_t ok();
+
+// Map a CUDA error to SC_ERR_CUDA with context.
+int32_t cuda_error(cudaError_t e, const char* what);
+
+// Streaming multiprocessor count of the current device (cached per device).
+int sm_count();
+
+// Compute float32 inverse frequencies 1/theta^(2i/D) (double pow rounded to float32)
+// when the caller gives none.  `out` has room for head_dim/2 values.
+void default_inv_freq(int32_t head_dim, double theta, float* out);
+
+// Largest head_dim handled by any kernel (the inverse-frequency table travels as a
+// kernel parameter of head_dim/2 floats).
+constexpr int kMaxHeadDim = 1024;
+
+// Paged restore launch shared by sc_restore_paged and the host pipeline.
+struct PagedArgs {
+    int32_t n_requests, max_pages, page_size, n_heads, head_dim;
+    int64_t n_pool_pages;
+    const int8_t* pool_kq;
+    const void* pool_ks;
+    const int8_t* pool_vq;
+    const void* pool_vs;
+    const int32_t* page_table;
+    int64_t page_table_stride;
+    const int32_t* seq_lens;
+    const float* delta_p;
+    int32_t delta_p_per_page;
+    double theta_base;
+    const float* inv_freq;  // host, may be null
+    void* k_out;
+    void* v_out;
+    const int64_t* out_offsets;
+    int64_t out_strides[3];
+    int64_t out_numel;
+    int32_t out_dtype;
+    int32_t* status;
+    uint32_t flags;
+    cudaStream_t stream;
+};
+
+int32_t launch_paged(const PagedArgs& a);
+
+}  // namespace sc

@@ -1,0 +1,270 @@
+// sc_paged.cu — ragged, paged restore: page-table gather + INT8 dequant + relative RoPE
+// shift, written straight into contiguous per-request caches.
+//
+// Work unit: one (request, page) task.  A persistent grid walks the tasks interleaved
+// (task = block + k * grid), which balances ragged requests without a host-side prefix
+// sum.  Per task the block builds the page's cos/sin slice table in shared memory from
+// the request's (or page's) shift, then every thread streams 16-frequency slices of the
+// page's rows exactly as the dense kernel does (two 16-byte loads per tensor per row,
+// rotate-half partner in the same thread).
+//
+// Device-side checks never fault: a page id outside the pool, a bad sequence length or an
+// output range outside out_numel makes the block skip the work and OR a status bit into
+// the caller's status word.
+#include "sc_common.cuh"
+
+namespace sc {
+namespace {
+
+constexpr int kPThreads = 256;
+
+struct PagedParams {
+    int32_t R, max_pages, page, H, D, P;
+    int64_t n_pool_pages;
+    FastDiv divH;
+    const int8_t* kq;
+    const __half* ks;
+    const int8_t* vq;
+    const __half* vs;
+    const int32_t* table;
+    int64_t table_stride;
+    const int32_t* seq_lens;
+    const float* dp;
+    int32_t dp_per_page;
+    void* ko;
+    void* vo;
+    const int64_t* out_off;
+    int64_t o_t, o_h;
+    int64_t out_numel;
+    int32_t* status;
+    float inv_freq[kMaxHeadDim / 2];
+};
+
+template <typename OutT, bool X16>
+__global__ void __launch_bounds__(kPThreads) paged_restore(const __grid_constant__ PagedParams p) {
+    __shared__ float s_cos[kMaxHeadDim / 2];
+    __shared__ float s_sin[kMaxHeadDim / 2];
+    const int P = p.P;
+    const int j = threadIdx.x % P;
+    const int rl = threadIdx.x / P;
+    const int RB = blockDim.x / P;
+    const int half = p.D >> 1;
+    const int64_t page_elems = static_cast<int64_t>(p.page) * p.H * p.D;
+    const int64_t page_rows = static_cast<int64_t>(p.page) * p.H;
+    const int64_t n_tasks = static_cast<int64_t>(p.R) * p.max_pages;
+    const bool has_k = p.kq != nullptr, has_v = p.vq != nullptr;
+
+    for (int64_t task = blockIdx.x; task < n_tasks; task += gridDim.x) {
+        const int r = static_cast<int>(task / p.max_pages);
+        const int pg = static_cast<int>(task - static_cast<int64_t>(r) * p.max_pages);
+        const int len = p.seq_lens[r];
+        if (len < 0 || static_cast<int64_t>(len) > static_cast<int64_t>(p.max_pages) * p.page) {
+            if (pg == 0 && threadIdx.x == 0) atomicOr(p.status, SC_STATUS_BAD_SEQ_LEN);
+            continue;
+        }
+        const int tok0 = pg * p.page;
+        if (tok0 >= len) continue;
+        const int n_tok = min(p.page, len - tok0);
+        const int32_t page_id = p.table[static_cast<int64_t>(r) * p.table_stride + pg];
+        if (page_id < 0 || page_id >= p.n_pool_pages) {
+            if (threadIdx.x == 0) atomicOr(p.status, SC_STATUS_BAD_PAGE_ID);
+            continue;
+        }
+        const int64_t off = p.out_off[r];
+        {
+            // Output range of this page: rows tok0 .. tok0+n_tok-1, heads 0 .. H-1.
+            const int64_t first = off + static_cast<int64_t>(tok0) * p.o_t;
+            const int64_t last = first + static_cast<int64_t>(n_tok - 1) * p.o_t +
+                                 static_cast<int64_t>(p.H - 1) * p.o_h + p.D;
+            if ((off & 7) != 0 || first < 0 || last > p.out_numel || p.o_t < 0 || p.o_h < 0) {
+                if (threadIdx.x == 0) atomicOr(p.status, SC_STATUS_BAD_OUT_OFFSET);
+                continue;
+            }
+        }
+        float c[16], s[16];
+        if (has_k) {
+            const float dp = p.dp[p.dp_per_page ? task : r];
+            __syncthreads();  // previous task's readers are done with the table
+            for (int f = threadIdx.x; f < half; f += blockDim.x) rope_cs(dp, p.inv_freq[f], s_cos[f], s_sin[f]);
+            __syncthreads();
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                c[k] = s_cos[j * 16 + k];
+                s[k] = s_sin[j * 16 + k];
+            }
+        }
+        const int64_t rows = static_cast<int64_t>(n_tok) * p.H;
+        const int64_t pbase = static_cast<int64_t>(page_id) * page_elems;
+        const int64_t sbase = static_cast<int64_t>(page_id) * page_rows;
+        for (int64_t row0 = rl; row0 < rows; row0 += 2 * RB) {
+            uint4 ka[2], kb[2], va[2], vb[2];
+            __half ksc[2], vsc[2];
+            int64_t oo[2];
+            bool valid[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int64_t row = row0 + u * RB;
+                valid[u] = row < rows;
+                if (!valid[u]) continue;
+                const uint32_t cidx = fdiv(static_cast<uint32_t>(row), p.divH);
+                const int64_t h = row - static_cast<int64_t>(cidx) * p.H;
+                oo[u] = off + (tok0 + static_cast<int64_t>(cidx)) * p.o_t + h * p.o_h + j * 16;
+                const int64_t src = pbase + row * p.D + j * 16;
+                if (has_k) {
+                    ka[u] = ld_stream_v4(p.kq + src);
+                    kb[u] = ld_stream_v4(p.kq + src + half);
+                    ksc[u] = p.ks[sbase + row];
+                }
+                if (has_v) {
+                    va[u] = ld_stream_v4(p.vq + src);
+                    vb[u] = ld_stream_v4(p.vq + src + half);
+                    vsc[u] = p.vs[sbase + row];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                if (!valid[u]) continue;
+                if (has_k) {
+                    OutT* o = reinterpret_cast<OutT*>(p.ko) + oo[u];
+                    rope_slice_store<OutT, __half, X16>(ka[u], kb[u], ksc[u], c, s, o, o + half);
+                }
+                if (has_v) {
+                    OutT* o = reinterpret_cast<OutT*>(p.vo) + oo[u];
+                    value_slice_store<OutT, __half>(va[u], vsc[u], o);
+                    value_slice_store<OutT, __half>(vb[u], vsc[u], o + half);
+                }
+            }
+        }
+    }
+}
+
+template <typename OutT, bool X16>
+cudaError_t launch(const PagedParams& p, cudaStream_t stream) {
+    auto kern = paged_restore<OutT, X16>;
+    const int threads = (kPThreads / p.P) * p.P;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0) != cudaSuccess ||
+        per_sm <= 0)
+        per_sm = 1;
+    const int64_t n_tasks = static_cast<int64_t>(p.R) * p.max_pages;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm;
+    const int grid = static_cast<int>(n_tasks < cap ? n_tasks : cap);
+    kern<<<grid, threads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+int32_t launch_paged(const PagedArgs& a) {
+    if (a.n_requests < 0 || a.max_pages < 0 || a.page_size <= 0 || a.n_heads <= 0 ||
+        a.n_pool_pages < 0)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "invalid paged geometry");
+    if (a.head_dim <= 0 || a.head_dim % 32 != 0 || a.head_dim > kMaxHeadDim)
+        return set_error(SC_ERR_UNSUPPORTED,
+                         "paged restore needs head_dim a multiple of 32 up to %d, got %d",
+                         kMaxHeadDim, a.head_dim);
+    if (a.out_dtype != SC_DTYPE_F16 && a.out_dtype != SC_DTYPE_BF16)
+        return set_error(SC_ERR_INVALID_DTYPE, "output dtype code %d: float16 or bfloat16 only",
+                         a.out_dtype);
+    if (a.n_requests == 0 || a.max_pages == 0) return ok();
+    const bool has_k = a.pool_kq != nullptr, has_v = a.pool_vq != nullptr;
+    if (!has_k && !has_v) return set_error(SC_ERR_INVALID_ARGUMENT, "neither K nor V given");
+    if ((has_k && (!a.pool_ks || !a.k_out)) || (has_v && (!a.pool_vs || !a.v_out)))
+        return set_error(SC_ERR_INVALID_ARGUMENT, "pool tensor given without scale or output");
+    if (!a.page_table || !a.seq_lens || !a.out_offsets || !a.status || (has_k && !a.delta_p))
+        return set_error(SC_ERR_INVALID_ARGUMENT, "null page table / lengths / offsets / status");
+    if (a.page_table_stride < a.max_pages)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "page_table_stride %lld < max_pages %d",
+                         (long long)a.page_table_stride, a.max_pages);
+    if (a.out_strides[2] != 1 || a.out_strides[0] % 8 != 0 || a.out_strides[1] % 8 != 0)
+        return set_error(SC_ERR_INVALID_ARGUMENT,
+                         "output strides must be [t, h, 1] with t, h multiples of 8 elements");
+    auto al = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+    if ((has_k && (!al(a.pool_kq) || !al(a.k_out))) || (has_v && (!al(a.pool_vq) || !al(a.v_out))))
+        return set_error(SC_ERR_INVALID_ARGUMENT, "pool and output base pointers must be 16-byte aligned");
+    if (static_cast<int64_t>(a.page_size) * a.n_heads >= (int64_t(1) << 31))
+        return set_error(SC_ERR_INVALID_ARGUMENT, "page_size * n_heads too large");
+
+    PagedParams p{};
+    p.R = a.n_requests;
+    p.max_pages = a.max_pages;
+    p.page = a.page_size;
+    p.H = a.n_heads;
+    p.D = a.head_dim;
+    p.P = a.head_dim / 32;
+    p.n_pool_pages = a.n_pool_pages;
+    p.divH = make_fastdiv(static_cast<uint32_t>(a.n_heads));
+    p.kq = a.pool_kq;
+    p.ks = static_cast<const __half*>(a.pool_ks);
+    p.vq = a.pool_vq;
+    p.vs = static_cast<const __half*>(a.pool_vs);
+    p.table = a.page_table;
+    p.table_stride = a.page_table_stride;
+    p.seq_lens = a.seq_lens;
+    p.dp = a.delta_p;
+    p.dp_per_page = a.delta_p_per_page;
+    p.ko = a.k_out;
+    p.vo = a.v_out;
+    p.out_off = a.out_offsets;
+    p.o_t = a.out_strides[0];
+    p.o_h = a.out_strides[1];
+    p.out_numel = a.out_numel;
+    p.status = a.status;
+    if (a.inv_freq)
+        for (int i = 0; i < a.head_dim / 2; ++i) p.inv_freq[i] = a.inv_freq[i];
+    else
+        default_inv_freq(a.head_dim, a.theta_base, p.inv_freq);
+    const bool x16 = !(a.flags & SC_FLAG_FP32_INTERMEDIATE);
+    cudaError_t e;
+    if (a.out_dtype == SC_DTYPE_F16)
+        e = x16 ? launch<__half, true>(p, a.stream) : launch<__half, false>(p, a.stream);
+    else
+        e = x16 ? launch<__nv_bfloat16, true>(p, a.stream)
+                : launch<__nv_bfloat16, false>(p, a.stream);
+    if (e != cudaSuccess) return cuda_error(e, "paged restore launch");
+    return ok();
+}
+
+}  // namespace sc
+
+extern "C" int32_t sc_restore_paged(int32_t n_requests, int32_t max_pages, int32_t page_size,
+                                    int32_t n_heads, int32_t head_dim, int64_t n_pool_pages,
+                                    const int8_t* pool_kq, const void* pool_ks,
+                                    const int8_t* pool_vq, const void* pool_vs,
+                                    const int32_t* page_table, int64_t page_table_stride,
+                                    const int32_t* seq_lens, const float* delta_p,
+                                    int32_t delta_p_per_page, double theta_base,
+                                    const float* inv_freq, void* k_out, void* v_out,
+                                    const int64_t* out_offsets, const int64_t* out_strides,
+                                    int64_t out_numel, int32_t out_dtype, int32_t* status,
+                                    uint32_t flags, void* stream) {
+    if (!out_strides) return sc::set_error(SC_ERR_INVALID_ARGUMENT, "null out_strides");
+    sc::PagedArgs a{};
+    a.n_requests = n_requests;
+    a.max_pages = max_pages;
+    a.page_size = page_size;
+    a.n_heads = n_heads;
+    a.head_dim = head_dim;
+    a.n_pool_pages = n_pool_pages;
+    a.pool_kq = pool_kq;
+    a.pool_ks = pool_ks;
+    a.pool_vq = pool_vq;
+    a.pool_vs = pool_vs;
+    a.page_table = page_table;
+    a.page_table_stride = page_table_stride;
+    a.seq_lens = seq_lens;
+    a.delta_p = delta_p;
+    a.delta_p_per_page = delta_p_per_page;
+    a.theta_base = theta_base;
+    a.inv_freq = inv_freq;
+    a.k_out = k_out;
+    a.v_out = v_out;
+    a.out_offsets = out_offsets;
+    for (int i = 0; i < 3; ++i) a.out_strides[i] = out_strides[i];
+    a.out_numel = out_numel;
+    a.out_dtype = out_dtype;
+    a.status = status;
+    a.flags = flags;
+    a.stream = static_cast<cudaStream_t>(stream);
+    return sc::launch_paged(a);
+}

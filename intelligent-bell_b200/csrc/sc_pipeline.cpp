@@ -1,0 +1,396 @@
+// sc_pipeline.cpp — multi-layer pinned-host -> GPU KV restore pipeline.
+//
+// Host side of the restore path (the reference drives the same steps from Python:
+// speccache/serving/kv_injector.py:392-498 and speccache/cache/engine.py:441-601):
+//   * pinned slabs [L, B, chunk, H, D] int8 and [L, B, chunk, H] fp16 (cudaHostAlloc,
+//     optionally from a thread bound to the GPU's NUMA node);
+//   * per layer, one cudaMemcpyAsync per run of consecutive block ids and tensor on the
+//     pipeline's own transfer stream into a ring of device staging slots;
+//   * an event per slot joins the transfer stream to the caller's compute stream, where
+//     the paged restore kernel (identity page table, one shift per block) writes the
+//     layer's K and V; a second event per slot releases the slot for layer l + n_slots.
+// Nothing on the host waits during a restore; sc_pipeline_synchronize polls an event
+// with a deadline.
+#include <errno.h>
+#include <sched.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+#include <unistd.h>
+
+#include <vector>
+
+#include "sc_internal.h"
+
+namespace {
+
+struct Meta {  // one upload per restore: identity-table length and per-block shifts
+    int32_t seq_len;
+    int32_t pad;
+    int64_t out_offset;
+    float delta_p[1];  // [max_restore_blocks]
+};
+
+size_t meta_bytes(int64_t max_blocks) {
+    return sizeof(Meta) + sizeof(float) * static_cast<size_t>(max_blocks > 1 ? max_blocks - 1 : 0);
+}
+
+// Bind the calling thread to the CPUs local to `device` (best effort); returns true and
+// the previous mask in `old` if the binding was changed.
+bool bind_to_device_numa(int device, cpu_set_t* old) {
+    char bus[32] = {0};
+    if (cudaDeviceGetPCIBusId(bus, sizeof(bus), device) != cudaSuccess) return false;
+    for (char* c = bus; *c; ++c)
+        if (*c >= 'A' && *c <= 'F') *c = static_cast<char>(*c - 'A' + 'a');
+    char path[160];
+    snprintf(path, sizeof(path), "/sys/bus/pci/devices/%s/local_cpulist", bus);
+    FILE* f = fopen(path, "r");
+    if (!f) {
+        // sysfs uses a 4-digit domain; the runtime may print 8 digits.
+        if (strlen(bus) > 12) {
+            snprintf(path, sizeof(path), "/sys/bus/pci/devices/%s/local_cpulist", bus + 4);
+            f = fopen(path, "r");
+        }
+        if (!f) return false;
+    }
+    char list[1024] = {0};
+    const bool got = fgets(list, sizeof(list), f) != nullptr;
+    fclose(f);
+    if (!got) return false;
+    cpu_set_t set;
+    CPU_ZERO(&set);
+    int count = 0;
+    for (char* tok = strtok(list, ",\n"); tok; tok = strtok(nullptr, ",\n")) {
+        int a = 0, b = 0;
+        if (sscanf(tok, "%d-%d", &a, &b) == 2) {
+            for (int c = a; c <= b && c < CPU_SETSIZE; ++c) CPU_SET(c, &set), ++count;
+        } else if (sscanf(tok, "%d", &a) == 1 && a < CPU_SETSIZE) {
+            CPU_SET(a, &set), ++count;
+        }
+    }
+    if (count == 0) return false;
+    if (sched_getaffinity(0, sizeof(cpu_set_t), old) != 0) return false;
+    return sched_setaffinity(0, sizeof(cpu_set_t), &set) == 0;
+}
+
+double now_s() {
+    timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec + ts.tv_nsec * 1e-9;
+}
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+struct sc_pipeline {
+    int device = 0;
+    int32_t L = 0, chunk = 0, H = 0, D = 0, n_slots = 0;
+    int64_t B = 0, max_blocks = 0;
+    uint32_t flags = 0;
+    int8_t* h_kq = nullptr;
+    uint16_t* h_ks = nullptr;
+    int8_t* h_vq = nullptr;
+    uint16_t* h_vs = nullptr;
+    Meta* h_meta = nullptr;
+    std::vector<int8_t*> d_kq, d_vq;
+    std::vector<uint16_t*> d_ks, d_vs;
+    int32_t* d_table = nullptr;
+    Meta* d_meta = nullptr;
+    int32_t* d_status = nullptr;
+    cudaStream_t transfer = nullptr;
+    std::vector<cudaEvent_t> ready, slot_free;
+    std::vector<bool> slot_used;
+    cudaEvent_t meta_uploaded = nullptr, done = nullptr;
+    bool any_restore = false;
+};
+
+namespace {
+
+void release(sc_pipeline* p) {
+    if (!p) return;
+    DeviceGuard g(p->device);
+    if (p->transfer) cudaStreamSynchronize(p->transfer);
+    if (p->done && p->any_restore) cudaEventSynchronize(p->done);
+    for (auto e : p->ready) cudaEventDestroy(e);
+    for (auto e : p->slot_free) cudaEventDestroy(e);
+    if (p->meta_uploaded) cudaEventDestroy(p->meta_uploaded);
+    if (p->done) cudaEventDestroy(p->done);
+    if (p->transfer) cudaStreamDestroy(p->transfer);
+    for (auto x : p->d_kq) cudaFree(x);
+    for (auto x : p->d_vq) cudaFree(x);
+    for (auto x : p->d_ks) cudaFree(x);
+    for (auto x : p->d_vs) cudaFree(x);
+    cudaFree(p->d_table);
+    cudaFree(p->d_meta);
+    cudaFree(p->d_status);
+    cudaFreeHost(p->h_kq);
+    cudaFreeHost(p->h_ks);
+    cudaFreeHost(p->h_vq);
+    cudaFreeHost(p->h_vs);
+    cudaFreeHost(p->h_meta);
+    delete p;
+}
+
+}  // namespace
+
+using sc::cuda_error;
+using sc::set_error;
+
+extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t n_blocks,
+                                      int32_t chunk_size, int32_t n_heads, int32_t head_dim,
+                                      int64_t max_restore_blocks, int32_t n_slots,
+                                      uint32_t flags, sc_pipeline** out) {
+    if (!out) return set_error(SC_ERR_INVALID_ARGUMENT, "null output handle");
+    *out = nullptr;
+    if (n_layers <= 0 || n_blocks <= 0 || chunk_size <= 0 || n_heads <= 0 || n_slots <= 0 ||
+        max_restore_blocks <= 0 || max_restore_blocks > n_blocks)
+        return set_error(SC_ERR_INVALID_ARGUMENT,
+                         "invalid pipeline geometry (layers=%d blocks=%lld chunk=%d heads=%d "
+                         "slots=%d max_restore=%lld)",
+                         n_layers, (long long)n_blocks, chunk_size, n_heads, n_slots,
+                         (long long)max_restore_blocks);
+    if (head_dim <= 0 || head_dim % 32 != 0 || head_dim > sc::kMaxHeadDim)
+        return set_error(SC_ERR_UNSUPPORTED, "head_dim must be a multiple of 32 up to %d",
+                         sc::kMaxHeadDim);
+    if (max_restore_blocks >= (int64_t(1) << 31) / chunk_size)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "max_restore_blocks too large");
+    auto* p = new sc_pipeline();
+    p->device = device;
+    p->L = n_layers;
+    p->B = n_blocks;
+    p->chunk = chunk_size;
+    p->H = n_heads;
+    p->D = head_dim;
+    p->max_blocks = max_restore_blocks;
+    p->n_slots = n_slots;
+    p->flags = flags;
+    DeviceGuard g(device);
+    if (!g.ok) {
+        delete p;
+        return set_error(SC_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    }
+    const size_t row = static_cast<size_t>(chunk_size) * n_heads;
+    const size_t slab_codes = static_cast<size_t>(n_layers) * n_blocks * row * head_dim;
+    const size_t slab_scales = static_cast<size_t>(n_layers) * n_blocks * row;
+    cpu_set_t old;
+    const bool bound = (flags & SC_PIPE_NUMA_LOCAL) && bind_to_device_numa(device, &old);
+    cudaError_t e = cudaSuccess;
+    void* ptr = nullptr;
+    auto halloc = [&](size_t bytes, void** dst) {
+        if (e != cudaSuccess) return;
+        e = cudaHostAlloc(dst, bytes, cudaHostAllocPortable);
+        if (e == cudaSuccess) memset(*dst, 0, bytes);  // first touch on the bound thread
+    };
+    halloc(slab_codes, &ptr), p->h_kq = static_cast<int8_t*>(ptr);
+    halloc(slab_scales * 2, &ptr), p->h_ks = static_cast<uint16_t*>(ptr);
+    halloc(slab_codes, &ptr), p->h_vq = static_cast<int8_t*>(ptr);
+    halloc(slab_scales * 2, &ptr), p->h_vs = static_cast<uint16_t*>(ptr);
+    halloc(meta_bytes(max_restore_blocks), &ptr), p->h_meta = static_cast<Meta*>(ptr);
+    if (bound) sched_setaffinity(0, sizeof(cpu_set_t), &old);
+    if (e != cudaSuccess) {
+        const int32_t rc = set_error(SC_ERR_HOST_ALLOC, "cudaHostAlloc of %zu-byte slabs failed: %s",
+                                     slab_codes, cudaGetErrorString(e));
+        cudaGetLastError();
+        release(p);
+        return rc;
+    }
+    const size_t stage_codes = static_cast<size_t>(max_restore_blocks) * row * head_dim;
+    const size_t stage_scales = static_cast<size_t>(max_restore_blocks) * row;
+    for (int s = 0; s < n_slots && e == cudaSuccess; ++s) {
+        int8_t *kq = nullptr, *vq = nullptr;
+        uint16_t *ks = nullptr, *vs = nullptr;
+        e = cudaMalloc(&kq, stage_codes);
+        if (e == cudaSuccess) e = cudaMalloc(&vq, stage_codes);
+        if (e == cudaSuccess) e = cudaMalloc(&ks, stage_scales * 2);
+        if (e == cudaSuccess) e = cudaMalloc(&vs, stage_scales * 2);
+        p->d_kq.push_back(kq), p->d_vq.push_back(vq), p->d_ks.push_back(ks), p->d_vs.push_back(vs);
+    }
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_table, sizeof(int32_t) * max_restore_blocks);
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_meta, meta_bytes(max_restore_blocks));
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_status, sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMemset(p->d_status, 0, sizeof(int32_t));
+    if (e == cudaSuccess) {
+        std::vector<int32_t> ident(static_cast<size_t>(max_restore_blocks));
+        for (int64_t i = 0; i < max_restore_blocks; ++i) ident[i] = static_cast<int32_t>(i);
+        e = cudaMemcpy(p->d_table, ident.data(), sizeof(int32_t) * ident.size(),
+                       cudaMemcpyHostToDevice);
+    }
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->transfer, cudaStreamNonBlocking);
+    for (int s = 0; s < n_slots && e == cudaSuccess; ++s) {
+        cudaEvent_t a = nullptr, b = nullptr;
+        e = cudaEventCreateWithFlags(&a, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&b, cudaEventDisableTiming);
+        p->ready.push_back(a), p->slot_free.push_back(b), p->slot_used.push_back(false);
+    }
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->meta_uploaded, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->done, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+        const int32_t rc = cuda_error(e, "pipeline device set-up");
+        release(p);
+        return rc;
+    }
+    *out = p;
+    return sc::ok();
+}
+
+extern "C" int32_t sc_pipeline_host_slabs(const sc_pipeline* p, int8_t** k_quant, void** k_scale,
+                                          int8_t** v_quant, void** v_scale) {
+    if (!p) return set_error(SC_ERR_INVALID_ARGUMENT, "null pipeline");
+    if (k_quant) *k_quant = p->h_kq;
+    if (k_scale) *k_scale = p->h_ks;
+    if (v_quant) *v_quant = p->h_vq;
+    if (v_scale) *v_scale = p->h_vs;
+    return sc::ok();
+}
+
+extern "C" int32_t sc_pipeline_restore(sc_pipeline* p, const int32_t* block_ids,
+                                       const int32_t* delta_ps, int32_t n_blocks,
+                                       double theta_base, const float* inv_freq,
+                                       void* const* k_out, void* const* v_out,
+                                       const int64_t* out_strides, int64_t out_numel,
+                                       int32_t out_dtype, void* compute_stream) {
+    if (!p) return set_error(SC_ERR_INVALID_ARGUMENT, "null pipeline");
+    if (n_blocks == 0) return sc::ok();
+    if (n_blocks < 0 || n_blocks > p->max_blocks)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "n_blocks %d outside [0, %lld]", n_blocks,
+                         (long long)p->max_blocks);
+    if (!block_ids || !delta_ps || !k_out || !v_out || !out_strides)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "null argument");
+    for (int32_t i = 0; i < n_blocks; ++i)
+        if (block_ids[i] < 0 || block_ids[i] >= p->B)
+            return set_error(SC_ERR_INVALID_ARGUMENT, "block id %d outside [0, %lld)",
+                             block_ids[i], (long long)p->B);
+    for (int32_t l = 0; l < p->L; ++l)
+        if (!k_out[l] || !v_out[l])
+            return set_error(SC_ERR_INVALID_ARGUMENT, "null output pointer for layer %d", l);
+    DeviceGuard g(p->device);
+    if (!g.ok) return set_error(SC_ERR_CUDA, "cudaSetDevice(%d) failed", p->device);
+    cudaStream_t cs = static_cast<cudaStream_t>(compute_stream);
+    cudaError_t e = cudaSuccess;
+
+    // Metadata: the host buffer may still feed the previous restore's upload.
+    if (p->any_restore) e = cudaEventSynchronize(p->meta_uploaded);
+    if (e != cudaSuccess) return cuda_error(e, "waiting for the previous metadata upload");
+    p->h_meta->seq_len = n_blocks * p->chunk;
+    p->h_meta->out_offset = 0;
+    for (int32_t i = 0; i < n_blocks; ++i) p->h_meta->delta_p[i] = static_cast<float>(delta_ps[i]);
+    // The device copy may still be read by the previous restore's last kernels.
+    if (p->any_restore) e = cudaStreamWaitEvent(p->transfer, p->done, 0);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(p->d_meta, p->h_meta, meta_bytes(n_blocks), cudaMemcpyHostToDevice,
+                            p->transfer);
+    if (e == cudaSuccess) e = cudaEventRecord(p->meta_uploaded, p->transfer);
+    if (e != cudaSuccess) return cuda_error(e, "metadata upload");
+
+    const size_t row = static_cast<size_t>(p->chunk) * p->H;
+    const size_t blk_codes = row * p->D, blk_scales = row;
+    for (int32_t l = 0; l < p->L && e == cudaSuccess; ++l) {
+        const int s = l % p->n_slots;
+        if (p->slot_used[s]) e = cudaStreamWaitEvent(p->transfer, p->slot_free[s], 0);
+        const size_t lay_codes = static_cast<size_t>(l) * p->B * blk_codes;
+        const size_t lay_scales = static_cast<size_t>(l) * p->B * blk_scales;
+        for (int32_t i = 0; i < n_blocks && e == cudaSuccess;) {
+            int32_t n = 1;
+            while (i + n < n_blocks && block_ids[i + n] == block_ids[i] + n) ++n;
+            const size_t b0 = static_cast<size_t>(block_ids[i]);
+            const size_t dst = static_cast<size_t>(i);
+            e = cudaMemcpyAsync(p->d_kq[s] + dst * blk_codes, p->h_kq + lay_codes + b0 * blk_codes,
+                                n * blk_codes, cudaMemcpyHostToDevice, p->transfer);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(p->d_vq[s] + dst * blk_codes,
+                                    p->h_vq + lay_codes + b0 * blk_codes, n * blk_codes,
+                                    cudaMemcpyHostToDevice, p->transfer);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(p->d_ks[s] + dst * blk_scales,
+                                    p->h_ks + lay_scales + b0 * blk_scales, n * blk_scales * 2,
+                                    cudaMemcpyHostToDevice, p->transfer);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(p->d_vs[s] + dst * blk_scales,
+                                    p->h_vs + lay_scales + b0 * blk_scales, n * blk_scales * 2,
+                                    cudaMemcpyHostToDevice, p->transfer);
+            i += n;
+        }
+        if (e == cudaSuccess) e = cudaEventRecord(p->ready[s], p->transfer);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, p->ready[s], 0);
+        if (e != cudaSuccess) break;
+        sc::PagedArgs a{};
+        a.n_requests = 1;
+        a.max_pages = n_blocks;
+        a.page_size = p->chunk;
+        a.n_heads = p->H;
+        a.head_dim = p->D;
+        a.n_pool_pages = n_blocks;
+        a.pool_kq = p->d_kq[s];
+        a.pool_ks = p->d_ks[s];
+        a.pool_vq = p->d_vq[s];
+        a.pool_vs = p->d_vs[s];
+        a.page_table = p->d_table;
+        a.page_table_stride = p->max_blocks;
+        a.seq_lens = &p->d_meta->seq_len;
+        a.delta_p = p->d_meta->delta_p;
+        a.delta_p_per_page = 1;
+        a.theta_base = theta_base;
+        a.inv_freq = inv_freq;
+        a.k_out = k_out[l];
+        a.v_out = v_out[l];
+        a.out_offsets = &p->d_meta->out_offset;
+        for (int i = 0; i < 3; ++i) a.out_strides[i] = out_strides[i];
+        a.out_numel = out_numel;
+        a.out_dtype = out_dtype;
+        a.status = p->d_status;
+        a.flags = 0;
+        a.stream = cs;
+        const int32_t rc = sc::launch_paged(a);
+        if (rc != SC_OK) return rc;
+        e = cudaEventRecord(p->slot_free[s], cs);
+        p->slot_used[s] = true;
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(p->done, cs);
+    if (e != cudaSuccess) return cuda_error(e, "restore enqueue");
+    p->any_restore = true;
+    return sc::ok();
+}
+
+extern "C" int32_t sc_pipeline_synchronize(sc_pipeline* p, double timeout_s) {
+    if (!p) return set_error(SC_ERR_INVALID_ARGUMENT, "null pipeline");
+    if (!p->any_restore) return sc::ok();
+    DeviceGuard g(p->device);
+    const double deadline = now_s() + (timeout_s > 0 ? timeout_s : 0);
+    for (;;) {
+        const cudaError_t e = cudaEventQuery(p->done);
+        if (e == cudaSuccess) return sc::ok();
+        if (e != cudaErrorNotReady) return cuda_error(e, "restore completion");
+        if (now_s() >= deadline)
+            return set_error(SC_ERR_TIMEOUT, "restore not complete after %.3f s", timeout_s);
+        usleep(50);
+    }
+}
+
+extern "C" int32_t sc_pipeline_status(sc_pipeline* p, int32_t* status_bits) {
+    if (!p || !status_bits) return set_error(SC_ERR_INVALID_ARGUMENT, "null argument");
+    DeviceGuard g(p->device);
+    int32_t v = 0;
+    cudaError_t e = cudaMemcpy(&v, p->d_status, sizeof(int32_t), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemset(p->d_status, 0, sizeof(int32_t));
+    if (e != cudaSuccess) return cuda_error(e, "reading pipeline status");
+    *status_bits = v;
+    return v == 0 ? sc::ok() : set_error(SC_ERR_OUT_OF_RANGE, "device status bits 0x%x", v);
+}
+
+extern "C" int32_t sc_pipeline_destroy(sc_pipeline* p) {
+    release(p);
+    return sc::ok();
+}

@@ -1,0 +1,473 @@
+// sc_restore.cu — fused INT8 K dequant + relative RoPE shift and V dequant (dense layout),
+// plus the cos/sin table kernel.
+//
+// Vector path (head_dim % 32 == 0, 16-byte aligned rows, unit dim stride):
+//   a row is one (layer, token, head) vector of head_dim int8 codes.  Thread j of a row
+//   owns the 16-frequency slice j: it loads bytes [16j, 16j+16) of the first half and
+//   their rotate-half partners [D/2+16j, D/2+16j+16) with two 16-byte loads, so the
+//   rotation needs no data from other lanes.  The same thread does the V row slice.
+//   The slice's 16 cos/sin values stay in registers for the whole grid-stride loop
+//   (one shift per launch) or are read per token from the caller's table.
+//   Two rows are in flight per thread per iteration (4-8 independent 16-byte loads).
+// Generic path: any strides, any even head_dim <= 1024, one thread per (row, frequency).
+#include <type_traits>
+
+#include "sc_common.cuh"
+
+namespace sc {
+namespace {
+
+constexpr int kThreads = 256;
+
+struct DenseParams {
+    int32_t rows;  // n_layers * n_tokens * n_heads  (< 2^31)
+    int32_t D;
+    int32_t P;  // 16-frequency slices per half row: D / 32 (vector path)
+    int32_t has_k, has_v;
+    int32_t cs_kind;  // 0: from delta_p, 1: one table row, 2: one table row per token
+    FastDiv divH, divT;
+    int32_t H, T;
+    const int8_t* kq;
+    const void* ks;
+    const int8_t* vq;
+    const void* vs;
+    void* ko;
+    void* vo;
+    int64_t kq_s[4], ks_s[3], vq_s[4], vs_s[3], ko_s[4], vo_s[4];  // [l, t, h(, d)]
+    const __half* cos;
+    const __half* sin;
+    int64_t cs_t, cs_d;
+    float dp;
+    const float* dp_dev;
+    float inv_freq[kMaxHeadDim / 2];
+};
+
+__device__ __forceinline__ void row_coords(const DenseParams& p, uint32_t row, int64_t& l,
+                                           int64_t& t, int64_t& h) {
+    const uint32_t lt = fdiv(row, p.divH);
+    h = static_cast<int64_t>(row - lt * static_cast<uint32_t>(p.H));
+    const uint32_t li = fdiv(lt, p.divT);
+    t = static_cast<int64_t>(lt - li * static_cast<uint32_t>(p.T));
+    l = static_cast<int64_t>(li);
+}
+
+// Fill the block's shared cos/sin table for a single shift (cs_kind 0 or 1).
+__device__ __forceinline__ void fill_shared_table(const DenseParams& p, float* s_cos,
+                                                  float* s_sin) {
+    const int half = p.D >> 1;
+    if (p.cs_kind == 1) {
+        for (int f = threadIdx.x; f < half; f += blockDim.x) {
+            s_cos[f] = __half2float(p.cos[f * p.cs_d]);
+            s_sin[f] = __half2float(p.sin[f * p.cs_d]);
+        }
+    } else {
+        const float dp = p.dp_dev != nullptr ? *p.dp_dev : p.dp;
+        for (int f = threadIdx.x; f < half; f += blockDim.x) {
+            float c, s;
+            rope_cs(dp, p.inv_freq[f], c, s);
+            s_cos[f] = c;
+            s_sin[f] = s;
+        }
+    }
+    __syncthreads();
+}
+
+template <typename ScaleT>
+struct RowLoad {
+    uint4 ka, kb, va, vb;
+    ScaleT ksc, vsc;
+    int64_t ko_off, vo_off;
+    int64_t t;
+    bool valid;
+};
+
+template <typename ScaleT>
+__device__ __forceinline__ void load_row(const DenseParams& p, int64_t row, int j,
+                                         RowLoad<ScaleT>& r) {
+    r.valid = row < p.rows;
+    if (!r.valid) return;
+    int64_t l, t, h;
+    row_coords(p, static_cast<uint32_t>(row), l, t, h);
+    r.t = t;
+    const int half = p.D >> 1;
+    if (p.has_k) {
+        const int8_t* base = p.kq + l * p.kq_s[0] + t * p.kq_s[1] + h * p.kq_s[2] + j * 16;
+        r.ka = ld_stream_v4(base);
+        r.kb = ld_stream_v4(base + half);
+        r.ksc = reinterpret_cast<const ScaleT*>(p.ks)[l * p.ks_s[0] + t * p.ks_s[1] + h * p.ks_s[2]];
+        r.ko_off = l * p.ko_s[0] + t * p.ko_s[1] + h * p.ko_s[2] + j * 16;
+    }
+    if (p.has_v) {
+        const int8_t* base = p.vq + l * p.vq_s[0] + t * p.vq_s[1] + h * p.vq_s[2] + j * 16;
+        r.va = ld_stream_v4(base);
+        r.vb = ld_stream_v4(base + half);
+        r.vsc = reinterpret_cast<const ScaleT*>(p.vs)[l * p.vs_s[0] + t * p.vs_s[1] + h * p.vs_s[2]];
+        r.vo_off = l * p.vo_s[0] + t * p.vo_s[1] + h * p.vo_s[2] + j * 16;
+    }
+}
+
+__device__ __forceinline__ void load_token_cs(const DenseParams& p, int64_t t, int j, float* c,
+                                              float* s) {
+    const __half* cp = p.cos + t * p.cs_t + j * 16;
+    const __half* sp = p.sin + t * p.cs_t + j * 16;
+    const uint4 c0 = ld_stream_v4(cp), c1 = ld_stream_v4(cp + 8);
+    const uint4 s0 = ld_stream_v4(sp), s1 = ld_stream_v4(sp + 8);
+    const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const float2 cf = __half22float2(bit_cast_u32<__half2>(cw[k]));
+        const float2 sf = __half22float2(bit_cast_u32<__half2>(sw[k]));
+        c[2 * k] = cf.x;
+        c[2 * k + 1] = cf.y;
+        s[2 * k] = sf.x;
+        s[2 * k + 1] = sf.y;
+    }
+}
+
+template <typename OutT, typename ScaleT, bool X16, bool PER_TOKEN>
+__device__ __forceinline__ void store_row(const DenseParams& p, const RowLoad<ScaleT>& r, int j,
+                                          const float* c, const float* s) {
+    if (!r.valid) return;
+    const int half = p.D >> 1;
+    if (p.has_k) {
+        OutT* o = reinterpret_cast<OutT*>(p.ko) + r.ko_off;
+        if constexpr (PER_TOKEN) {
+            float ct[16], st[16];
+            load_token_cs(p, r.t, j, ct, st);
+            rope_slice_store<OutT, ScaleT, X16>(r.ka, r.kb, r.ksc, ct, st, o, o + half);
+        } else {
+            rope_slice_store<OutT, ScaleT, X16>(r.ka, r.kb, r.ksc, c, s, o, o + half);
+        }
+    }
+    if (p.has_v) {
+        OutT* o = reinterpret_cast<OutT*>(p.vo) + r.vo_off;
+        value_slice_store<OutT, ScaleT>(r.va, r.vsc, o);
+        value_slice_store<OutT, ScaleT>(r.vb, r.vsc, o + half);
+    }
+}
+
+template <typename OutT, typename ScaleT, bool X16, bool PER_TOKEN>
+__global__ void __launch_bounds__(kThreads) dense_restore_vec(const __grid_constant__ DenseParams p) {
+    __shared__ float s_cos[kMaxHeadDim / 2];
+    __shared__ float s_sin[kMaxHeadDim / 2];
+    const int P = p.P;
+    const int j = threadIdx.x % P;
+    const int rl = threadIdx.x / P;
+    const int RB = blockDim.x / P;
+    float c[16], s[16];
+    if constexpr (!PER_TOKEN) {
+        fill_shared_table(p, s_cos, s_sin);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            c[k] = s_cos[j * 16 + k];
+            s[k] = s_sin[j * 16 + k];
+        }
+    }
+    if (rl >= RB) return;
+    const int64_t step = static_cast<int64_t>(gridDim.x) * RB;
+    for (int64_t row0 = static_cast<int64_t>(blockIdx.x) * RB + rl; row0 < p.rows; row0 += 2 * step) {
+        RowLoad<ScaleT> r0, r1;
+        load_row<ScaleT>(p, row0, j, r0);
+        load_row<ScaleT>(p, row0 + step, j, r1);
+        store_row<OutT, ScaleT, X16, PER_TOKEN>(p, r0, j, c, s);
+        store_row<OutT, ScaleT, X16, PER_TOKEN>(p, r1, j, c, s);
+    }
+}
+
+// Stride-generic path: one thread per (row, frequency f), both halves of the pair.
+struct GenericStrides {
+    int64_t rows;
+    int64_t kq_d, vq_d, ko_d, vo_d;
+};
+
+template <typename OutT, typename ScaleT, bool X16>
+__global__ void __launch_bounds__(kThreads)
+    dense_restore_generic(const __grid_constant__ DenseParams p, const GenericStrides g) {
+    __shared__ float s_cos[kMaxHeadDim / 2];
+    __shared__ float s_sin[kMaxHeadDim / 2];
+    if (p.cs_kind != 2) fill_shared_table(p, s_cos, s_sin);
+    const int half = p.D >> 1;
+    const int64_t total = g.rows * half;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t row = i / half;
+        const int f = static_cast<int>(i - row * half);
+        const int64_t h = row % p.H;
+        const int64_t lt = row / p.H;
+        const int64_t t = lt % p.T;
+        const int64_t l = lt / p.T;
+        if (p.has_k) {
+            const int8_t* kb = p.kq + l * p.kq_s[0] + t * p.kq_s[1] + h * p.kq_s[2];
+            const float sf = scale_to_float<ScaleT>(
+                reinterpret_cast<const ScaleT*>(p.ks)[l * p.ks_s[0] + t * p.ks_s[1] + h * p.ks_s[2]]);
+            float x1 = __fmul_rn(static_cast<float>(kb[f * g.kq_d]), sf);
+            float x2 = __fmul_rn(static_cast<float>(kb[(f + half) * g.kq_d]), sf);
+            if constexpr (X16) {
+                x1 = __half2float(__float2half_rn(x1));
+                x2 = __half2float(__float2half_rn(x2));
+            }
+            float c, s;
+            if (p.cs_kind == 2) {
+                c = __half2float(p.cos[t * p.cs_t + f * p.cs_d]);
+                s = __half2float(p.sin[t * p.cs_t + f * p.cs_d]);
+            } else {
+                c = s_cos[f];
+                s = s_sin[f];
+            }
+            OutT* o = reinterpret_cast<OutT*>(p.ko) + l * p.ko_s[0] + t * p.ko_s[1] + h * p.ko_s[2];
+            o[f * g.ko_d] = from_float<OutT>(fmaf(x1, c, -(x2 * s)));
+            o[(f + half) * g.ko_d] = from_float<OutT>(fmaf(x2, c, x1 * s));
+        }
+        if (p.has_v) {
+            const int8_t* vb = p.vq + l * p.vq_s[0] + t * p.vq_s[1] + h * p.vq_s[2];
+            const float sf = scale_to_float<ScaleT>(
+                reinterpret_cast<const ScaleT*>(p.vs)[l * p.vs_s[0] + t * p.vs_s[1] + h * p.vs_s[2]]);
+            OutT* o = reinterpret_cast<OutT*>(p.vo) + l * p.vo_s[0] + t * p.vo_s[1] + h * p.vo_s[2];
+            o[f * g.vo_d] = from_float<OutT>(__fmul_rn(static_cast<float>(vb[f * g.vq_d]), sf));
+            o[(f + half) * g.vo_d] =
+                from_float<OutT>(__fmul_rn(static_cast<float>(vb[(f + half) * g.vq_d]), sf));
+        }
+    }
+}
+
+template <typename OutT>
+__global__ void __launch_bounds__(kThreads)
+    rope_table_kernel(const float* __restrict__ dp, int64_t n, int half,
+                      const __grid_constant__ DenseParams p, OutT* cos_out, OutT* sin_out) {
+    const int64_t total = n * half;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / half;
+        const int f = static_cast<int>(i - r * half);
+        const float angle = __fmul_rn(dp[r], p.inv_freq[f]);
+        double sd, cd;
+        sincos(static_cast<double>(angle), &sd, &cd);
+        const float c = static_cast<float>(cd), s = static_cast<float>(sd);
+        if constexpr (std::is_same<OutT, float>::value) {
+            cos_out[i] = c;
+            sin_out[i] = s;
+        } else {
+            cos_out[i] = from_float<OutT>(c);
+            sin_out[i] = from_float<OutT>(s);
+        }
+    }
+}
+
+template <typename K>
+int blocks_per_sm(K kernel, int threads) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static int cache[64] = {0};
+    if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, 0) != cudaSuccess ||
+        n <= 0)
+        n = 1;
+    if (dev >= 0 && dev < 64) cache[dev] = n;
+    return n;
+}
+
+inline bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+inline bool stride_ok(int64_t stride, int64_t size, int64_t align) {
+    return size <= 1 || (stride % align) == 0;
+}
+
+template <typename OutT, typename ScaleT, bool X16, bool PER_TOKEN>
+cudaError_t launch_vec(const DenseParams& p, cudaStream_t stream) {
+    auto kern = dense_restore_vec<OutT, ScaleT, X16, PER_TOKEN>;
+    const int threads = (kThreads / p.P) * p.P;
+    const int rb = threads / p.P;
+    const int64_t need = (static_cast<int64_t>(p.rows) + 2 * rb - 1) / (2 * rb);
+    const int64_t cap = static_cast<int64_t>(sm_count()) * blocks_per_sm(kern, threads);
+    const int grid = static_cast<int>(need < cap ? (need > 0 ? need : 1) : cap);
+    kern<<<grid, threads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+template <typename OutT, typename ScaleT, bool X16>
+cudaError_t launch_generic(const DenseParams& p, const GenericStrides& g, cudaStream_t stream) {
+    auto kern = dense_restore_generic<OutT, ScaleT, X16>;
+    const int64_t total = g.rows * (p.D / 2);
+    const int64_t need = (total + kThreads - 1) / kThreads;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * blocks_per_sm(kern, kThreads);
+    const int grid = static_cast<int>(need < cap ? (need > 0 ? need : 1) : cap);
+    kern<<<grid, kThreads, 0, stream>>>(p, g);
+    return cudaGetLastError();
+}
+
+template <typename OutT, typename ScaleT>
+cudaError_t dispatch(const DenseParams& p, const GenericStrides& g, bool vec, bool x16,
+                     cudaStream_t stream) {
+    if (vec) {
+        if (p.cs_kind == 2)
+            return x16 ? launch_vec<OutT, ScaleT, true, true>(p, stream)
+                       : launch_vec<OutT, ScaleT, false, true>(p, stream);
+        return x16 ? launch_vec<OutT, ScaleT, true, false>(p, stream)
+                   : launch_vec<OutT, ScaleT, false, false>(p, stream);
+    }
+    return x16 ? launch_generic<OutT, ScaleT, true>(p, g, stream)
+               : launch_generic<OutT, ScaleT, false>(p, g, stream);
+}
+
+}  // namespace
+}  // namespace sc
+
+using namespace sc;
+
+extern "C" int32_t sc_rope_cos_sin_delta(const float* delta_pos, int64_t n, int32_t head_dim,
+                                         double theta_base, const float* inv_freq,
+                                         void* cos_out, void* sin_out, int32_t out_dtype,
+                                         void* stream) {
+    if (head_dim <= 0 || (head_dim & 1))
+        return set_error(SC_ERR_INVALID_ARGUMENT, "head_dim must be even, got %d", head_dim);
+    if (head_dim > kMaxHeadDim)
+        return set_error(SC_ERR_UNSUPPORTED, "head_dim %d exceeds %d", head_dim, kMaxHeadDim);
+    if (n < 0) return set_error(SC_ERR_INVALID_ARGUMENT, "n must be >= 0, got %lld", (long long)n);
+    if (n == 0) return ok();
+    if (!delta_pos || !cos_out || !sin_out)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "null pointer argument");
+    DenseParams p{};
+    p.D = head_dim;
+    if (inv_freq)
+        for (int i = 0; i < head_dim / 2; ++i) p.inv_freq[i] = inv_freq[i];
+    else
+        default_inv_freq(head_dim, theta_base, p.inv_freq);
+    const int half = head_dim / 2;
+    const int64_t total = n * half;
+    const int64_t need = (total + kThreads - 1) / kThreads;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+    const int grid = static_cast<int>(need < cap ? need : cap);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (out_dtype) {
+        case SC_DTYPE_F16:
+            rope_table_kernel<__half><<<grid, kThreads, 0, s>>>(
+                delta_pos, n, half, p, static_cast<__half*>(cos_out), static_cast<__half*>(sin_out));
+            break;
+        case SC_DTYPE_BF16:
+            rope_table_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(
+                delta_pos, n, half, p, static_cast<__nv_bfloat16*>(cos_out),
+                static_cast<__nv_bfloat16*>(sin_out));
+            break;
+        case SC_DTYPE_F32:
+            rope_table_kernel<float><<<grid, kThreads, 0, s>>>(
+                delta_pos, n, half, p, static_cast<float*>(cos_out), static_cast<float*>(sin_out));
+            break;
+        default:
+            return set_error(SC_ERR_INVALID_DTYPE, "unsupported table dtype code %d", out_dtype);
+    }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "rope_table_kernel launch");
+    return ok();
+}
+
+extern "C" int32_t sc_dequant_rope_kv(
+    int32_t n_layers, int64_t n_tokens, int32_t n_heads, int32_t head_dim, const int8_t* k_quant,
+    const int64_t* kq_strides, const void* k_scale, const int64_t* ks_strides,
+    const int8_t* v_quant, const int64_t* vq_strides, const void* v_scale,
+    const int64_t* vs_strides, int32_t scale_dtype, const void* cos_delta, const void* sin_delta,
+    const int64_t* cs_strides, double delta_p, const float* delta_p_dev, double theta_base,
+    const float* inv_freq, void* k_out, const int64_t* ko_strides, void* v_out,
+    const int64_t* vo_strides, int32_t out_dtype, uint32_t flags, void* stream) {
+    if (n_layers < 0 || n_tokens < 0 || n_heads < 0)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "negative size (layers=%d tokens=%lld heads=%d)",
+                         n_layers, (long long)n_tokens, n_heads);
+    if (head_dim <= 0 || (head_dim & 1))
+        return set_error(SC_ERR_INVALID_ARGUMENT,
+                         "head_dim must be even for RoPE half-pairing, got head_dim=%d", head_dim);
+    if (head_dim > kMaxHeadDim)
+        return set_error(SC_ERR_UNSUPPORTED, "head_dim %d exceeds %d", head_dim, kMaxHeadDim);
+    if (out_dtype != SC_DTYPE_F16 && out_dtype != SC_DTYPE_BF16)
+        return set_error(SC_ERR_INVALID_DTYPE, "output dtype code %d: float16 or bfloat16 only",
+                         out_dtype);
+    if (scale_dtype != SC_DTYPE_F16 && scale_dtype != SC_DTYPE_F32)
+        return set_error(SC_ERR_INVALID_DTYPE, "scale dtype code %d: float16 or float32 only",
+                         scale_dtype);
+    const bool has_k = k_quant != nullptr, has_v = v_quant != nullptr;
+    if (!has_k && !has_v) return set_error(SC_ERR_INVALID_ARGUMENT, "neither K nor V given");
+    if (has_k && (!k_scale || !k_out || !kq_strides || !ks_strides || !ko_strides))
+        return set_error(SC_ERR_INVALID_ARGUMENT, "K given without its scale/output/strides");
+    if (has_v && (!v_scale || !v_out || !vq_strides || !vs_strides || !vo_strides))
+        return set_error(SC_ERR_INVALID_ARGUMENT, "V given without its scale/output/strides");
+    if ((cos_delta == nullptr) != (sin_delta == nullptr))
+        return set_error(SC_ERR_INVALID_ARGUMENT, "cos_delta and sin_delta must both be given");
+    if (cos_delta && !cs_strides)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "cos/sin tables given without strides");
+    const int64_t rows = static_cast<int64_t>(n_layers) * n_tokens * n_heads;
+    if (rows >= (int64_t(1) << 31))
+        return set_error(SC_ERR_INVALID_ARGUMENT,
+                         "%lld rows in one call; split the call below 2^31 rows", (long long)rows);
+    if (rows == 0) return ok();
+
+    DenseParams p{};
+    p.rows = static_cast<int32_t>(rows);
+    p.D = head_dim;
+    p.P = head_dim / 32;
+    p.has_k = has_k;
+    p.has_v = has_v;
+    p.H = n_heads;
+    p.T = static_cast<int32_t>(n_tokens);
+    p.divH = make_fastdiv(static_cast<uint32_t>(n_heads));
+    p.divT = make_fastdiv(static_cast<uint32_t>(n_tokens));
+    p.kq = k_quant;
+    p.ks = k_scale;
+    p.vq = v_quant;
+    p.vs = v_scale;
+    p.ko = k_out;
+    p.vo = v_out;
+    GenericStrides g{};
+    g.rows = rows;
+    if (has_k) {
+        for (int i = 0; i < 4; ++i) p.kq_s[i] = kq_strides[i], p.ko_s[i] = ko_strides[i];
+        for (int i = 0; i < 3; ++i) p.ks_s[i] = ks_strides[i];
+        g.kq_d = kq_strides[3];
+        g.ko_d = ko_strides[3];
+    }
+    if (has_v) {
+        for (int i = 0; i < 4; ++i) p.vq_s[i] = vq_strides[i], p.vo_s[i] = vo_strides[i];
+        for (int i = 0; i < 3; ++i) p.vs_s[i] = vs_strides[i];
+        g.vq_d = vq_strides[3];
+        g.vo_d = vo_strides[3];
+    }
+    if (cos_delta) {
+        p.cos = static_cast<const __half*>(cos_delta);
+        p.sin = static_cast<const __half*>(sin_delta);
+        p.cs_t = cs_strides[0];
+        p.cs_d = cs_strides[1];
+        p.cs_kind = (p.cs_t == 0 || n_tokens == 1) ? 1 : 2;
+    } else {
+        p.cs_kind = 0;
+        p.dp = static_cast<float>(delta_p);
+        p.dp_dev = delta_p_dev;
+        if (inv_freq)
+            for (int i = 0; i < head_dim / 2; ++i) p.inv_freq[i] = inv_freq[i];
+        else
+            default_inv_freq(head_dim, theta_base, p.inv_freq);
+    }
+
+    // Vector path eligibility: 16-byte aligned row starts, unit dim stride, D % 32 == 0.
+    bool vec = !(flags & SC_FLAG_FORCE_GENERIC) && (head_dim % 32 == 0);
+    const int64_t sizes[3] = {n_layers, n_tokens, n_heads};
+    auto rows_ok = [&](const void* base, const int64_t* st, int64_t align_elems) {
+        if (!aligned16(base) || st[3] != 1) return false;
+        for (int i = 0; i < 3; ++i)
+            if (!stride_ok(st[i], sizes[i], align_elems)) return false;
+        return true;
+    };
+    if (vec && has_k) vec = rows_ok(k_quant, kq_strides, 16) && rows_ok(k_out, ko_strides, 8);
+    if (vec && has_v) vec = rows_ok(v_quant, vq_strides, 16) && rows_ok(v_out, vo_strides, 8);
+    if (vec && p.cs_kind == 2)
+        vec = aligned16(cos_delta) && aligned16(sin_delta) && p.cs_d == 1 && (p.cs_t % 8) == 0;
+
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool x16 = !(flags & SC_FLAG_FP32_INTERMEDIATE);
+    cudaError_t e;
+    if (out_dtype == SC_DTYPE_F16)
+        e = scale_dtype == SC_DTYPE_F16 ? dispatch<__half, __half>(p, g, vec, x16, s)
+                                        : dispatch<__half, float>(p, g, vec, x16, s);
+    else
+        e = scale_dtype == SC_DTYPE_F16 ? dispatch<__nv_bfloat16, __half>(p, g, vec, x16, s)
+                                        : dispatch<__nv_bfloat16, float>(p, g, vec, x16, s);
+    if (e != cudaSuccess) return cuda_error(e, "dense restore launch");
+    return ok();
+}

@@ -1,0 +1,393 @@
+"""GPU parity of the restore kernels against the CPU oracle and the reference's goldens.
+
+Tolerances: where the cos/sin tables are given, K is compared bit for bit with the
+reference's eager arithmetic (fp16-rounded dequant, fp32 rotation); V always bit for
+bit.  Where the kernel builds cos/sin itself from delta_p, each table entry may differ
+from torch's by one fp16 ulp in rare cases (torch's float32 cos/sin is not correctly
+rounded), so K is checked with the reference's own tolerance, rtol = atol = 1e-2
+(reference tests/test_correctness.py:169), plus an exact-match fraction.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import as_tensor, bits_equal
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0) if torch.cuda.is_available() else None
+
+
+def _quantized(oracle, t, h, d, seed, dtype=torch.float32):
+    g = torch.Generator().manual_seed(seed)
+    raw = torch.randn((t, h, d), generator=g, dtype=torch.float32).to(dtype)
+    return oracle.quantize_kv_int8(raw)
+
+
+@pytest.mark.parametrize("t", [1, 17, 128, 511, 2048, 4096])
+@pytest.mark.parametrize("h", [4, 8, 32])
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("delta_p", [-512, 0, 1024])
+def test_k_shift_grid_matches_eager_bitwise(scb, oracle, t, h, d, delta_p):
+    # the reference's 108-case grid (tests/test_correctness.py:142-169)
+    kq, ks = _quantized(oracle, t, h, d, 42)
+    cos, sin = oracle.compute_rope_cos_sin_delta(delta_p, d)
+    ref = oracle.dequant_rope_shift(kq, ks, cos, sin)
+    out = scb.triton_fused_k_dequant_rope_shift(kq.to(DEV), ks.to(DEV), cos.to(DEV), sin.to(DEV))
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float16 and out.shape == (t, h, d)
+    torch.testing.assert_close(out.cpu(), ref, rtol=1e-2, atol=1e-2)
+    assert bits_equal(out.cpu(), ref)
+
+
+def test_golden_vectors(scb, golden):
+    for name in golden["sh_cases"]:
+        p = f"sh_{name}_"
+        kq, ks = as_tensor(golden[p + "kq"]).to(DEV), as_tensor(golden[p + "ks"]).to(DEV)
+        cos, sin = as_tensor(golden[p + "cos"]).to(DEV), as_tensor(golden[p + "sin"]).to(DEV)
+        vq, vs = as_tensor(golden[p + "vq"]).to(DEV), as_tensor(golden[p + "vs"]).to(DEV)
+        k, v = scb.dequant_kv_cache(kq, ks, vq, vs, cos, sin)
+        torch.cuda.synchronize()
+        assert bits_equal(k.cpu(), as_tensor(golden[p + "k"])), name
+        assert bits_equal(v.cpu(), as_tensor(golden[p + "v"])), name
+
+
+@pytest.mark.parametrize("theta", [10000.0, 500000.0, 1000000.0])
+@pytest.mark.parametrize("delta_p", [-4096, -350, 1, 2048, 4095, 8192, 32768])
+def test_delta_p_path_in_kernel_tables(scb, oracle, theta, delta_p):
+    t, h, d = 257, 8, 128
+    kq, ks = _quantized(oracle, t, h, d, 7)
+    cos, sin = oracle.compute_rope_cos_sin_delta(delta_p, d, theta)
+    ref = oracle.dequant_rope_shift(kq, ks, cos, sin)
+    out = scb.triton_fused_k_dequant_rope_shift(kq.to(DEV), ks.to(DEV), delta_p=delta_p, theta=theta)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out.cpu(), ref, rtol=1e-2, atol=1e-2)
+    same = (out.cpu().view(torch.int16) == ref.view(torch.int16)).float().mean().item()
+    assert same > 0.99, same
+
+
+def test_delta_p_device_scalar_and_per_token(scb, oracle):
+    t, h, d = 100, 4, 64
+    kq, ks = _quantized(oracle, t, h, d, 11)
+    cos, sin = oracle.compute_rope_cos_sin_delta(-77, d)
+    ref = oracle.dequant_rope_shift(kq, ks, cos, sin)
+    out = scb.triton_fused_k_dequant_rope_shift(kq.to(DEV), ks.to(DEV),
+                                                delta_p=torch.tensor([-77], device=DEV))
+    torch.testing.assert_close(out.cpu(), ref, rtol=1e-2, atol=1e-2)
+    dps = torch.randint(-3000, 3000, (t,), generator=torch.Generator().manual_seed(1))
+    cos_t, sin_t = oracle.compute_rope_cos_sin_delta(dps, d)
+    ref_t = oracle.dequant_rope_shift(kq, ks, cos_t, sin_t)
+    out_t = scb.triton_fused_k_dequant_rope_shift(kq.to(DEV), ks.to(DEV), delta_p=dps)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out_t.cpu(), ref_t, rtol=1e-2, atol=1e-2)
+
+
+def test_rope_table_kernel(scb, oracle, golden):
+    dps = torch.from_numpy(golden["tab_dps"])
+    for d in (64, 128):
+        for theta in (10000.0, 500000.0, 1000000.0):
+            key = f"tab_d{d}_th{int(theta)}"
+            c, s = scb.compute_rope_cos_sin_delta(dps, d, theta, device=DEV)
+            torch.cuda.synchronize()
+            for got, want in ((c.cpu(), as_tensor(golden[key + "_cos"])),
+                              (s.cpu(), as_tensor(golden[key + "_sin"]))):
+                diff = (got.float() - want.float()).abs()
+                assert diff.max().item() <= 2 ** -10, key  # at most one fp16 ulp near 1
+                assert (diff == 0).float().mean().item() > 0.99, key
+    c32, _ = scb.compute_rope_cos_sin_delta(torch.arange(-5, 5), 128, device=DEV, dtype=torch.float32)
+    ref32 = torch.cos(torch.arange(-5, 5, dtype=torch.float32)[:, None] * oracle.inv_freq(128)[None])
+    torch.testing.assert_close(c32.cpu(), ref32, rtol=0, atol=2e-7)
+
+
+def test_value_and_bf16_outputs(scb, oracle):
+    t, h, d = 333, 8, 128
+    kq, ks = _quantized(oracle, t, h, d, 3)
+    vq, vs = _quantized(oracle, t, h, d, 4)
+    cos, sin = oracle.compute_rope_cos_sin_delta(555, d, 500000.0)
+    k, v = scb.dequant_kv_cache(kq.to(DEV), ks.to(DEV), vq.to(DEV), vs.to(DEV), cos.to(DEV),
+                                sin.to(DEV), out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16
+    assert bits_equal(k.cpu(), oracle.dequant_rope_shift(kq, ks, cos, sin, torch.bfloat16))
+    assert bits_equal(v.cpu(), oracle.dequant_value(vq, vs, torch.bfloat16))
+    v16 = scb.dequant_value(vq.to(DEV), vs.to(DEV))
+    torch.cuda.synchronize()
+    assert bits_equal(v16.cpu(), oracle.dequant_value(vq, vs))
+
+
+def test_fp32_intermediate_mode(scb, oracle):
+    t, h, d = 64, 8, 128
+    kq, ks = _quantized(oracle, t, h, d, 5)
+    cos, sin = oracle.compute_rope_cos_sin_delta(900, d)
+    ref = oracle.dequant_rope_shift(kq, ks, cos, sin, fp16_intermediate=False)
+    out = scb.triton_fused_k_dequant_rope_shift(kq.to(DEV), ks.to(DEV), cos.to(DEV), sin.to(DEV),
+                                                fp32_intermediate=True)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out.cpu(), ref, rtol=1e-3, atol=1e-3)
+
+
+def test_preallocated_out_is_written_in_place(scb, oracle):
+    # reference tests/test_correctness.py:238-256
+    t, h, d = 64, 8, 128
+    kq, ks = _quantized(oracle, t, h, d, 42)
+    cos, sin = oracle.compute_rope_cos_sin_delta(12, d)
+    pre = torch.empty((t, h, d), dtype=torch.float16, device=DEV)
+    ret = scb.triton_fused_k_dequant_rope_shift(kq.to(DEV), ks.to(DEV), cos.to(DEV), sin.to(DEV),
+                                                out=pre)
+    assert ret.data_ptr() == pre.data_ptr()
+    torch.cuda.synchronize()
+    assert bits_equal(ret.cpu(), oracle.dequant_rope_shift(kq, ks, cos, sin))
+
+
+@pytest.mark.parametrize("force_generic", [False, True])
+def test_strided_views_and_multi_layer(scb, oracle, force_generic):
+    n_l, t, h, d, dp, theta = 3, 77, 4, 128, 321, 500000.0
+    codes = [_quantized(oracle, t, h, d, 100 + i) for i in range(2 * n_l)]
+    kq = torch.stack([c[0] for c in codes[:n_l]])
+    ks = torch.stack([c[1] for c in codes[:n_l]])
+    vq = torch.stack([c[0] for c in codes[n_l:]])
+    vs = torch.stack([c[1] for c in codes[n_l:]])
+    # outputs written straight into model-layout caches [L, 1, H, Tmax, D]
+    t_max = 96
+    k_cache = torch.zeros((n_l, 1, h, t_max, d), dtype=torch.bfloat16, device=DEV)
+    v_cache = torch.zeros_like(k_cache)
+    k_view = k_cache[:, 0, :, :t, :].permute(0, 2, 1, 3)
+    v_view = v_cache[:, 0, :, :t, :].permute(0, 2, 1, 3)
+    scb.restore_layers(kq.to(DEV), ks.to(DEV), vq.to(DEV), vs.to(DEV), delta_p=dp, theta=theta,
+                       k_out=k_view, v_out=v_view, force_generic=force_generic)
+    torch.cuda.synchronize()
+    cos, sin = oracle.compute_rope_cos_sin_delta(dp, d, theta)
+    for layer in range(n_l):
+        k_ref = oracle.dequant_rope_shift(kq[layer], ks[layer], cos, sin, torch.bfloat16)
+        v_ref = oracle.dequant_value(vq[layer], vs[layer], torch.bfloat16)
+        torch.testing.assert_close(k_cache[layer, 0, :, :t].permute(1, 0, 2).cpu().float(),
+                                   k_ref.float(), rtol=1e-2, atol=1e-2)
+        assert bits_equal(v_cache[layer, 0, :, :t].permute(1, 0, 2).contiguous().cpu(), v_ref)
+    assert k_cache[:, :, :, t:].abs().sum().item() == 0  # nothing written past T
+
+
+def test_generic_path_odd_strides(scb, oracle):
+    # a dim stride of 2 (every other byte of a wider buffer) forces the generic kernel;
+    # head_dim 96 with head-major storage goes through the vector path with 3 slices/row
+    t, h, d = 19, 3, 96
+    kq, ks = _quantized(oracle, t, h, d, 9)
+    vq, vs = _quantized(oracle, t, h, d, 10)
+    wide = torch.zeros((t, h, 2 * d), dtype=torch.int8)
+    wide[..., ::2] = kq
+    kq_strided = wide.to(DEV)[..., ::2]
+    kq_hm = kq.permute(1, 0, 2).contiguous().to(DEV).permute(1, 0, 2)
+    cos, sin = oracle.compute_rope_cos_sin_delta(-99, d)
+    k_ref = oracle.dequant_rope_shift(kq, ks, cos, sin)
+    for k_in in (kq_strided, kq_hm):
+        k, v = scb.dequant_kv_cache(k_in, ks.to(DEV), vq.to(DEV), vs.to(DEV), cos.to(DEV),
+                                    sin.to(DEV))
+        torch.cuda.synchronize()
+        assert bits_equal(k.cpu(), k_ref)
+        assert bits_equal(v.cpu(), oracle.dequant_value(vq, vs))
+    # odd head_dim is rejected like the reference; head_dim 34 (even, not a multiple of 32)
+    # runs on the generic kernel
+    kq34, ks34 = _quantized(oracle, 5, 2, 34, 12)
+    c34, s34 = oracle.compute_rope_cos_sin_delta(7, 34)
+    k34 = scb.triton_fused_k_dequant_rope_shift(kq34.to(DEV), ks34.to(DEV), c34.to(DEV), s34.to(DEV))
+    torch.cuda.synchronize()
+    assert bits_equal(k34.cpu(), oracle.dequant_rope_shift(kq34, ks34, c34, s34))
+
+
+def test_end_to_end_rotational_equivalence(scb, oracle):
+    # reference tests/test_correctness.py:172-235 with the quantize twin on the GPU
+    g = torch.Generator().manual_seed(999)
+    t, h, d = 256, 8, 128
+    raw = torch.randn((t, h, d), generator=g).to(torch.float16)
+    c600, s600 = oracle.compute_rope_cos_sin_delta(600, d)
+    c250, s250 = oracle.compute_rope_cos_sin_delta(250, d)
+
+    def rot(x, c, s):
+        cf = torch.cat([c, c], -1)[:, None, :].float()
+        sf = torch.cat([s, s], -1)[:, None, :].float()
+        xf = x.float()
+        return (xf * cf + oracle.rotate_half(xf) * sf).to(torch.float16)
+
+    kq, ks = scb.quantize_kv_int8(rot(raw, c600, s600).to(DEV))
+    shifted = scb.triton_fused_k_dequant_rope_shift(kq, ks, delta_p=-350)
+    q250, s250_ = oracle.quantize_kv_int8(rot(raw, c250, s250))
+    direct = oracle.dequant_value(q250, s250_)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(shifted.cpu(), direct, rtol=5e-2, atol=5e-2)
+    sim = torch.nn.functional.cosine_similarity(shifted.cpu().float().view(-1, d),
+                                                direct.float().view(-1, d), dim=-1)
+    assert sim.min().item() > 0.99
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(1, 1, 128), (17, 4, 64), (513, 8, 128), (33, 2, 32), (5, 3, 96)])
+def test_quantize_bit_exact(scb, oracle, dtype, shape):
+    g = torch.Generator().manual_seed(sum(shape))
+    x = torch.randn(shape, generator=g, dtype=torch.float32)
+    x[..., : max(1, shape[-1] // 50)] *= 10.0  # outlier channels
+    x[0, 0] = 0.0  # all-zero row -> eps scale
+    x = x.to(dtype)
+    q, s = scb.quantize_kv_int8(x.to(DEV))
+    q_ref, s_ref = oracle.quantize_kv_int8(x)
+    torch.cuda.synchronize()
+    assert torch.equal(q.cpu(), q_ref)
+    assert bits_equal(s.cpu(), s_ref)
+
+
+def test_quantize_golden_and_strided(scb, oracle, golden):
+    for name in golden["q_cases"]:
+        name = str(name)
+        x = as_tensor(golden[f"q_{name}_x"], str(golden[f"q_{name}_xdtype"]))
+        q, s = scb.quantize_kv_int8(x.to(DEV))
+        torch.cuda.synchronize()
+        assert torch.equal(q.cpu(), as_tensor(golden[f"q_{name}_q"])), name
+        assert bits_equal(s.cpu(), as_tensor(golden[f"q_{name}_s"])), name
+    # head-major (non-contiguous) input: strided rows on the vector kernel
+    x = torch.randn((40, 6, 128), generator=torch.Generator().manual_seed(2)).to(torch.float16)
+    xs = x.permute(1, 0, 2).contiguous().to(DEV).permute(1, 0, 2)
+    q, s = scb.quantize_kv_int8(xs)
+    q_ref, s_ref = oracle.quantize_kv_int8(x)
+    torch.cuda.synchronize()
+    assert torch.equal(q.cpu(), q_ref) and bits_equal(s.cpu(), s_ref)
+
+
+def _paged_case(oracle, n_req, page, h, d, seed, max_len):
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(1, max_len + 1, (n_req,), generator=g).tolist()
+    lens[0] = max_len  # one request fills its pages exactly when max_len % page == 0
+    pages_per = [(n + page - 1) // page for n in lens]
+    n_pool = sum(pages_per) + 3
+    pool_kq = torch.randint(-127, 128, (n_pool, page, h, d), generator=g, dtype=torch.int8)
+    pool_vq = torch.randint(-127, 128, (n_pool, page, h, d), generator=g, dtype=torch.int8)
+    pool_ks = (torch.rand((n_pool, page, h, 1), generator=g) * 0.05 + 1e-3).to(torch.float16)
+    pool_vs = (torch.rand((n_pool, page, h, 1), generator=g) * 0.05 + 1e-3).to(torch.float16)
+    perm = torch.randperm(n_pool, generator=g)
+    max_pages = max(pages_per)
+    table = torch.zeros((n_req, max_pages), dtype=torch.int32)
+    k = 0
+    for r, n in enumerate(pages_per):
+        table[r, :n] = perm[k:k + n].to(torch.int32)
+        k += n
+    dps = torch.randint(0, 4097, (n_req,), generator=g).tolist()
+    return pool_kq, pool_ks, pool_vq, pool_vs, table, lens, dps
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
+def test_paged_ragged_restore(scb, oracle, out_dtype):
+    pkq, pks, pvq, pvs, table, lens, dps = _paged_case(oracle, 9, 64, 8, 128, 1, 700)
+    theta = 500000.0
+    k, v, cu = scb.restore_paged(pkq.to(DEV), pks.to(DEV), pvq.to(DEV), pvs.to(DEV), table, lens,
+                                 dps, theta=theta, out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    assert scb.paged_status(DEV) == 0
+    ref = oracle.restore_paged(pkq, pks, pvq, pvs, table, lens, dps, theta, out_dtype=out_dtype)
+    for r, (kr, vr) in enumerate(ref):
+        kg = k[cu[r]:cu[r + 1]].cpu()
+        vg = v[cu[r]:cu[r + 1]].cpu()
+        torch.testing.assert_close(kg.float(), kr.float(), rtol=1e-2, atol=1e-2)
+        assert bits_equal(vg, vr)
+
+
+def test_paged_per_page_shifts_bitwise_with_tables(scb, oracle):
+    # per-page shifts (the pipeline's mode); compare against per-block oracle restore
+    pkq, pks, pvq, pvs, table, lens, _ = _paged_case(oracle, 1, 16, 4, 64, 2, 16 * 7)
+    n = (lens[0] + 15) // 16
+    dps = [int(x) for x in torch.randint(-2000, 2000, (n,), generator=torch.Generator().manual_seed(3))]
+    k, v, cu = scb.restore_paged(pkq.to(DEV), pks.to(DEV), pvq.to(DEV), pvs.to(DEV), table, lens,
+                                 torch.tensor(dps, dtype=torch.float32).view(1, -1),
+                                 delta_p_per_page=True, out_dtype=torch.float16)
+    torch.cuda.synchronize()
+    kr, vr = oracle.restore_blocks(pkq, pks, pvq, pvs, table[0, :n].tolist(), dps)
+    torch.testing.assert_close(k.cpu(), kr[: lens[0]], rtol=1e-2, atol=1e-2)
+    assert bits_equal(v.cpu(), vr[: lens[0]])
+
+
+def test_paged_bad_entries_are_flagged_not_faulted(scb, oracle):
+    pkq, pks, pvq, pvs, table, lens, dps = _paged_case(oracle, 3, 16, 2, 64, 4, 40)
+    bad = table.clone()
+    bad[1, 0] = 10_000  # page id outside the pool
+    k, v, cu = scb.restore_paged(pkq.to(DEV), pks.to(DEV), pvq.to(DEV), pvs.to(DEV), bad, lens, dps,
+                                 out_dtype=torch.float16)
+    torch.cuda.synchronize()
+    assert scb.paged_status(DEV) & scb._lib.SC_STATUS_BAD_PAGE_ID
+    # the good requests are restored all the same
+    ref = oracle.restore_paged(pkq, pks, pvq, pvs, table, lens, dps)
+    assert bits_equal(v[cu[0]:cu[1]].cpu(), ref[0][1])
+    assert bits_equal(v[cu[2]:cu[3]].cpu(), ref[2][1])
+    # device-side lengths beyond the table, and offsets outside the output
+    lens_dev = torch.tensor([lens[0], 16 * table.shape[1] + 1, lens[2]], dtype=torch.int32, device=DEV)
+    out = torch.zeros((sum(lens) + 64, 2, 64), dtype=torch.float16, device=DEV)
+    offs = torch.tensor([0, 0, 10**9], dtype=torch.int64)
+    scb.restore_paged(pkq.to(DEV), pks.to(DEV), pvq.to(DEV), pvs.to(DEV), table, lens_dev, dps,
+                      k_out=out, v_out=out.clone(), out_offsets=offs)
+    torch.cuda.synchronize()
+    bits = scb.paged_status(DEV)
+    assert bits & scb._lib.SC_STATUS_BAD_SEQ_LEN and bits & scb._lib.SC_STATUS_BAD_OUT_OFFSET
+    assert scb.paged_status(DEV) == 0  # reading cleared it
+
+
+def test_pipeline_restore_matches_oracle(scb, oracle):
+    from speccache_b200.cache import KVRestorePipeline
+
+    n_l, n_blocks, chunk, h, d, theta = 3, 12, 32, 4, 128, 500000.0
+    g = torch.Generator().manual_seed(8)
+    with KVRestorePipeline(n_l, n_blocks, chunk, h, d, device=DEV, max_restore_blocks=8,
+                           n_slots=2) as pipe:
+        pipe.k_quant.copy_(torch.randint(-127, 128, pipe.k_quant.shape, generator=g, dtype=torch.int8))
+        pipe.v_quant.copy_(torch.randint(-127, 128, pipe.v_quant.shape, generator=g, dtype=torch.int8))
+        pipe.k_scale.copy_((torch.rand(pipe.k_scale.shape, generator=g) * 0.05 + 1e-3).half())
+        pipe.v_scale.copy_((torch.rand(pipe.v_scale.shape, generator=g) * 0.05 + 1e-3).half())
+        for blocks, dps in (([3, 4, 5, 0, 11, 7], [-256] * 6), ([9, 2, 10, 1], [100, -7, 4000, 0])):
+            n_tok = len(blocks) * chunk
+            k_out = [torch.empty((n_tok, h, d), dtype=torch.float16, device=DEV) for _ in range(n_l)]
+            v_out = [torch.empty_like(x) for x in k_out]
+            pipe.restore(blocks, dps, k_out, v_out, theta=theta)
+            pipe.synchronize(timeout=30.0)
+            assert pipe.status() == 0
+            for layer in range(n_l):
+                kr, vr = oracle.restore_blocks(pipe.k_quant[layer], pipe.k_scale[layer],
+                                               pipe.v_quant[layer], pipe.v_scale[layer], blocks,
+                                               dps, theta)
+                torch.testing.assert_close(k_out[layer].cpu(), kr, rtol=1e-2, atol=1e-2)
+                assert bits_equal(v_out[layer].cpu(), vr)
+
+
+def test_pipeline_back_to_back_restores_reuse_slots(scb, oracle):
+    from speccache_b200.cache import KVRestorePipeline
+
+    n_l, n_blocks, chunk, h, d = 5, 6, 64, 8, 128
+    g = torch.Generator().manual_seed(12)
+    with KVRestorePipeline(n_l, n_blocks, chunk, h, d, device=DEV, n_slots=2) as pipe:
+        pipe.k_quant.copy_(torch.randint(-127, 128, pipe.k_quant.shape, generator=g, dtype=torch.int8))
+        pipe.v_quant.copy_(torch.randint(-127, 128, pipe.v_quant.shape, generator=g, dtype=torch.int8))
+        pipe.k_scale.fill_(0.01)
+        pipe.v_scale.fill_(0.02)
+        outs = []
+        for rep in range(4):  # enqueue four restores without waiting in between
+            blocks = [(rep + i) % n_blocks for i in range(n_blocks)]
+            k_out = [torch.empty((n_blocks * chunk, h, d), dtype=torch.bfloat16, device=DEV)
+                     for _ in range(n_l)]
+            v_out = [torch.empty_like(x) for x in k_out]
+            pipe.restore(blocks, [rep * 10] * n_blocks, k_out, v_out)
+            outs.append((blocks, rep * 10, k_out, v_out))
+        pipe.synchronize(timeout=30.0)
+        for blocks, dp, k_out, v_out in outs:
+            for layer in range(n_l):
+                kr, vr = oracle.restore_blocks(pipe.k_quant[layer], pipe.k_scale[layer],
+                                               pipe.v_quant[layer], pipe.v_scale[layer], blocks,
+                                               [dp] * len(blocks), out_dtype=torch.bfloat16)
+                torch.testing.assert_close(k_out[layer].cpu().float(), kr.float(), rtol=1e-2, atol=1e-2)
+                assert bits_equal(v_out[layer].cpu(), vr)
+
+
+def test_validation_on_device(scb):
+    k = torch.zeros((4, 2, 64), dtype=torch.int8, device=DEV)
+    s = torch.ones((4, 2, 1), dtype=torch.float16, device=DEV)
+    with pytest.raises(ValueError, match="k_scale must have shape"):
+        scb.triton_fused_k_dequant_rope_shift(k, s[:3], delta_p=1)
+    with pytest.raises(TypeError, match="out tensor must be torch.float16"):
+        scb.triton_fused_k_dequant_rope_shift(k, s, delta_p=1,
+                                              out=torch.empty((4, 2, 64), device=DEV))
+    with pytest.raises(ValueError, match="must have shape"):
+        scb.dequant_value(k, s, out=torch.empty((4, 2, 63), dtype=torch.float16, device=DEV))

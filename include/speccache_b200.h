@@ -76,7 +76,7 @@ typedef enum sc_dtype {
 /* Device status bits written (atomicOr) by the paged kernels into a caller-given word. */
 #define SC_STATUS_BAD_PAGE_ID 0x1    /* page-table entry outside [0, n_pool_pages)          */
 #define SC_STATUS_BAD_SEQ_LEN 0x2    /* seq_len < 0 or > max_pages * page_size              */
-#define SC_STATUS_BAD_OUT_OFFSET 0x4 /* output offset misaligned or rows beyond out_numel    */
+#define SC_STATUS_BAD_OUT_OFFSET 0x4 /* offset not a multiple of 16 or rows beyond out_numel */
 
 /* Message for the last failing call on this host thread ("" if none). */
 SC_API const char* sc_last_error(void);
@@ -151,7 +151,9 @@ SC_API int32_t sc_quantize_int8(int64_t n_tokens, int32_t n_heads, int32_t head_
  *  delta_p             device float32 [n_requests] or, with delta_p_per_page,
  *                      [n_requests, max_pages]
  *  out_offsets         device int64 [n_requests]: element offset of request r's token 0
- *  out_strides         [token, head, dim] of the outputs (dim stride must be 1)
+ *                      (a multiple of 16 elements: rows are written 32 bytes at a time)
+ *  out_strides         [token, head, dim] of the outputs (dim stride 1, others multiples
+ *                      of 16 elements; outputs 32-byte aligned)
  *  out_numel           elements in each of k_out / v_out; a request whose rows would
  *                      fall outside is skipped and flagged (SC_STATUS_BAD_OUT_OFFSET)
  *  status              device int32 word; SC_STATUS_* bits are OR-ed in when an entry is

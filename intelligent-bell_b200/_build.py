@@ -43,9 +43,15 @@ def _stale() -> bool:
     return any(os.path.getmtime(d) > built for d in deps)
 
 
-def build_library(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> str:
-    """Compile every CUDA/C++ source into the shared library; returns its path."""
-    if not force and not _stale():
+def build_library(force: bool = False, verbose: bool = False, ptxas_info: bool = False,
+                  out_path: str | None = None, defines: dict | None = None) -> str:
+    """Compile every CUDA/C++ source into the shared library; returns its path.
+
+    ``out_path`` / ``defines`` build a variant elsewhere with tuning macros set
+    (e.g. ``{"SC_DENSE_MIN_BLOCKS": 4}``); the default is the in-tree library.
+    """
+    target = out_path or LIB_PATH
+    if out_path is None and not force and not _stale():
         return LIB_PATH
     cmd = [
         _nvcc(),
@@ -57,8 +63,9 @@ def build_library(force: bool = False, verbose: bool = False, ptxas_info: bool =
         "-fPIC,-O3,-fvisibility=hidden",
         "-shared",
         f"-I{INCLUDE}",
+        *[f"-D{k}={v}" for k, v in (defines or {}).items()],
         "-o",
-        LIB_PATH + ".tmp",
+        target + ".tmp",
         *sources(),
     ]
     if ptxas_info:
@@ -70,8 +77,8 @@ def build_library(force: bool = False, verbose: bool = False, ptxas_info: bool =
         raise RuntimeError(f"nvcc failed ({proc.returncode}):\n{proc.stderr}")
     if verbose or ptxas_info:
         print(proc.stderr, file=sys.stderr)
-    os.replace(LIB_PATH + ".tmp", LIB_PATH)
-    return LIB_PATH
+    os.replace(target + ".tmp", target)
+    return target
 
 
 if __name__ == "__main__":

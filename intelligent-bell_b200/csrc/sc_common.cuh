@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "sc_internal.h"
 
 namespace sc {
@@ -41,19 +43,53 @@ __device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
 
 // ---------------------------------------------------------------------------------------
 // Memory access.  Inputs are read once: non-coherent loads that do not allocate in L1.
+// Tuning knobs (compile-time): SC_LOAD_L2_PREFETCH adds a 256-byte L2 prefetch hint to
+// the input loads; SC_STORE_STREAMING marks output stores evict-first.
 // ---------------------------------------------------------------------------------------
+#ifndef SC_LOAD_L2_PREFETCH
+#define SC_LOAD_L2_PREFETCH 0
+#endif
+#ifndef SC_STORE_STREAMING
+#define SC_STORE_STREAMING 0
+#endif
+
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
     uint4 r;
+#if SC_LOAD_L2_PREFETCH
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+#else
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                  : "l"(p));
+#endif
     return r;
 }
 
 __device__ __forceinline__ void st_v4(void* p, const uint4& v) {
+#if SC_STORE_STREAMING
+    asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+#else
     asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
                  "r"(v.w)
                  : "memory");
+#endif
+}
+
+// One 32-byte store (a full L2 sector per lane); the address must be 32-byte aligned.
+__device__ __forceinline__ void st_v8(void* p, const uint32_t (&v)[8]) {
+#if SC_STORE_STREAMING
+    asm volatile("st.global.cs.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+#else
+    asm volatile("st.global.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+#endif
 }
 
 __device__ __forceinline__ void st_v2(void* p, const uint2& v) {
@@ -131,28 +167,51 @@ __device__ __forceinline__ void rope_cs(float dp, float inv_freq, float& c, floa
     s = __half2float(__float2half_rn(static_cast<float>(sd)));
 }
 
+// cos/sin of a 16-frequency slice, read four at a time.
+//   CsShared: the block's table in shared memory (16-byte aligned float4 reads).
+//   CsRegs:   values the thread holds itself (per-token tables).
+struct CsShared {
+    const float4* c;
+    const float4* s;
+    __device__ __forceinline__ float4 cos4(int w) const { return c[w]; }
+    __device__ __forceinline__ float4 sin4(int w) const { return s[w]; }
+};
+struct CsRegs {
+    const float* c;
+    const float* s;
+    __device__ __forceinline__ float4 cos4(int w) const {
+        return make_float4(c[4 * w], c[4 * w + 1], c[4 * w + 2], c[4 * w + 3]);
+    }
+    __device__ __forceinline__ float4 sin4(int w) const {
+        return make_float4(s[4 * w], s[4 * w + 1], s[4 * w + 2], s[4 * w + 3]);
+    }
+};
+
 // ---------------------------------------------------------------------------------------
 // One 16-frequency slice of one row: 16 key codes of the first half (a) and their 16
 // rotate-half partners of the second half (b), the row scale, the slice's cos/sin.
-// Writes 16 outputs at o1 (first half) and 16 at o2 (second half).
+// Writes 16 outputs at o1 (first half) and 16 at o2 (second half), one 32-byte store
+// each (o1 and o2 must be 32-byte aligned).
 //   X16 = true : x = fp16(q*s) first (reference eager arithmetic; exact because q*s is
 //                exact in fp32 and __hmul2_rn rounds it once)
 //   X16 = false: x = q*s kept in fp32
 // ---------------------------------------------------------------------------------------
-template <typename OutT, typename ScaleT, bool X16>
+template <typename OutT, typename ScaleT, bool X16, typename CS>
 __device__ __forceinline__ void rope_slice_store(const uint4& a, const uint4& b, ScaleT scale,
-                                                 const float* __restrict__ cs,
-                                                 const float* __restrict__ sn, void* o1,
-                                                 void* o2) {
+                                                 const CS& cs, void* o1, void* o2) {
     const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
     const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
-    uint32_t r1[8], r2[8];
     const float sf = scale_to_float<ScaleT>(scale);
+    uint32_t r1[8], r2[8];
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
         __half2 qa[2], qb[2];
         i8x4_to_h2(aw[w], qa[0], qa[1]);
         i8x4_to_h2(bw[w], qb[0], qb[1]);
+        const float4 c4 = cs.cos4(w);
+        const float4 s4 = cs.sin4(w);
+        const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+        const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
             float2 x1, x2;
@@ -170,8 +229,7 @@ __device__ __forceinline__ void rope_slice_store(const uint4& a, const uint4& b,
                     x2 = __half22float2(__floats2half2_rn(x2.x, x2.y));
                 }
             }
-            const int e = w * 4 + k * 2;
-            const float c0 = cs[e], c1 = cs[e + 1], s0 = sn[e], s1 = sn[e + 1];
+            const float c0 = cv[2 * k], c1 = cv[2 * k + 1], s0 = sv[2 * k], s1 = sv[2 * k + 1];
             const float o1a = fmaf(x1.x, c0, -(x2.x * s0));
             const float o1b = fmaf(x1.y, c1, -(x2.y * s1));
             const float o2a = fmaf(x2.x, c0, x1.x * s0);
@@ -180,13 +238,11 @@ __device__ __forceinline__ void rope_slice_store(const uint4& a, const uint4& b,
             r2[w * 2 + k] = pack2<OutT>(o2a, o2b);
         }
     }
-    st_v4(o1, make_uint4(r1[0], r1[1], r1[2], r1[3]));
-    st_v4(reinterpret_cast<char*>(o1) + 16, make_uint4(r1[4], r1[5], r1[6], r1[7]));
-    st_v4(o2, make_uint4(r2[0], r2[1], r2[2], r2[3]));
-    st_v4(reinterpret_cast<char*>(o2) + 16, make_uint4(r2[4], r2[5], r2[6], r2[7]));
+    st_v8(o1, r1);
+    st_v8(o2, r2);
 }
 
-// 16 value codes -> 16 outputs of cvt(q*s).
+// 16 value codes -> 16 outputs of cvt(q*s), one 32-byte store.
 template <typename OutT, typename ScaleT>
 __device__ __forceinline__ void value_slice_store(const uint4& a, ScaleT scale, void* o) {
     const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
@@ -197,8 +253,7 @@ __device__ __forceinline__ void value_slice_store(const uint4& a, ScaleT scale, 
         i8x4_to_h2(aw[w], q[0], q[1]);
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
-            if constexpr (sizeof(ScaleT) == 2 && sizeof(OutT) == 2 &&
-                          std::is_same<OutT, __half>::value) {
+            if constexpr (sizeof(ScaleT) == 2 && std::is_same<OutT, __half>::value) {
                 const __half2 s2 = __half2half2(*reinterpret_cast<const __half*>(&scale));
                 r[w * 2 + k] = u32_of(__hmul2_rn(q[k], s2));
             } else {
@@ -208,8 +263,7 @@ __device__ __forceinline__ void value_slice_store(const uint4& a, ScaleT scale, 
             }
         }
     }
-    st_v4(o, make_uint4(r[0], r[1], r[2], r[3]));
-    st_v4(reinterpret_cast<char*>(o) + 16, make_uint4(r[4], r[5], r[6], r[7]));
+    st_v8(o, r);
 }
 
 }  // namespace sc

@@ -4,7 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/speccache_b200.h"
+#include "speccache_b200.h"
 
 namespace sc {
 

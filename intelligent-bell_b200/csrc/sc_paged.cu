@@ -6,7 +6,8 @@
 // sum.  Per task the block builds the page's cos/sin slice table in shared memory from
 // the request's (or page's) shift, then every thread streams 16-frequency slices of the
 // page's rows exactly as the dense kernel does (two 16-byte loads per tensor per row,
-// rotate-half partner in the same thread).
+// rotate-half partner in the same thread, the next row's loads in flight while the
+// current row is converted and stored).
 //
 // Device-side checks never fault: a page id outside the pool, a bad sequence length or an
 // output range outside out_numel makes the block skip the work and OR a status bit into
@@ -17,6 +18,9 @@ namespace sc {
 namespace {
 
 constexpr int kPThreads = 256;
+#ifndef SC_PAGED_MIN_BLOCKS
+#define SC_PAGED_MIN_BLOCKS 2
+#endif
 
 struct PagedParams {
     int32_t R, max_pages, page, H, D, P;
@@ -40,10 +44,39 @@ struct PagedParams {
     float inv_freq[kMaxHeadDim / 2];
 };
 
+struct PageRow {
+    uint4 ka, kb, va, vb;
+    __half ksc, vsc;
+    int64_t oo;
+    bool valid;
+};
+
+__device__ __forceinline__ void load_page_row(const PagedParams& p, int64_t row, int64_t rows,
+                                              int j, int half, int64_t pbase, int64_t sbase,
+                                              int64_t off, int tok0, bool has_k, bool has_v,
+                                              PageRow& r) {
+    r.valid = row < rows;
+    if (!r.valid) return;
+    const uint32_t cidx = fdiv(static_cast<uint32_t>(row), p.divH);
+    const int64_t h = row - static_cast<int64_t>(cidx) * p.H;
+    r.oo = off + (tok0 + static_cast<int64_t>(cidx)) * p.o_t + h * p.o_h + j * 16;
+    const int64_t src = pbase + row * p.D + j * 16;
+    if (has_k) {
+        r.ka = ld_stream_v4(p.kq + src);
+        r.kb = ld_stream_v4(p.kq + src + half);
+        r.ksc = p.ks[sbase + row];
+    }
+    if (has_v) {
+        r.va = ld_stream_v4(p.vq + src);
+        r.vb = ld_stream_v4(p.vq + src + half);
+        r.vsc = p.vs[sbase + row];
+    }
+}
+
 template <typename OutT, bool X16>
-__global__ void __launch_bounds__(kPThreads) paged_restore(const __grid_constant__ PagedParams p) {
-    __shared__ float s_cos[kMaxHeadDim / 2];
-    __shared__ float s_sin[kMaxHeadDim / 2];
+__global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS) paged_restore(const __grid_constant__ PagedParams p) {
+    __shared__ __align__(16) float s_cos[kMaxHeadDim / 2];
+    __shared__ __align__(16) float s_sin[kMaxHeadDim / 2];
     const int P = p.P;
     const int j = threadIdx.x % P;
     const int rl = threadIdx.x / P;
@@ -76,64 +109,40 @@ __global__ void __launch_bounds__(kPThreads) paged_restore(const __grid_constant
             const int64_t first = off + static_cast<int64_t>(tok0) * p.o_t;
             const int64_t last = first + static_cast<int64_t>(n_tok - 1) * p.o_t +
                                  static_cast<int64_t>(p.H - 1) * p.o_h + p.D;
-            if ((off & 7) != 0 || first < 0 || last > p.out_numel || p.o_t < 0 || p.o_h < 0) {
+            if ((off & 15) != 0 || first < 0 || last > p.out_numel || p.o_t < 0 || p.o_h < 0) {
                 if (threadIdx.x == 0) atomicOr(p.status, SC_STATUS_BAD_OUT_OFFSET);
                 continue;
             }
         }
-        float c[16], s[16];
         if (has_k) {
             const float dp = p.dp[p.dp_per_page ? task : r];
             __syncthreads();  // previous task's readers are done with the table
             for (int f = threadIdx.x; f < half; f += blockDim.x) rope_cs(dp, p.inv_freq[f], s_cos[f], s_sin[f]);
             __syncthreads();
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {
-                c[k] = s_cos[j * 16 + k];
-                s[k] = s_sin[j * 16 + k];
-            }
         }
+        const CsShared cs{reinterpret_cast<const float4*>(s_cos + j * 16),
+                          reinterpret_cast<const float4*>(s_sin + j * 16)};
         const int64_t rows = static_cast<int64_t>(n_tok) * p.H;
         const int64_t pbase = static_cast<int64_t>(page_id) * page_elems;
         const int64_t sbase = static_cast<int64_t>(page_id) * page_rows;
-        for (int64_t row0 = rl; row0 < rows; row0 += 2 * RB) {
-            uint4 ka[2], kb[2], va[2], vb[2];
-            __half ksc[2], vsc[2];
-            int64_t oo[2];
-            bool valid[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int64_t row = row0 + u * RB;
-                valid[u] = row < rows;
-                if (!valid[u]) continue;
-                const uint32_t cidx = fdiv(static_cast<uint32_t>(row), p.divH);
-                const int64_t h = row - static_cast<int64_t>(cidx) * p.H;
-                oo[u] = off + (tok0 + static_cast<int64_t>(cidx)) * p.o_t + h * p.o_h + j * 16;
-                const int64_t src = pbase + row * p.D + j * 16;
+        // one row-slice in flight ahead of the one being converted and stored
+        PageRow cur, nxt;
+        int64_t row = rl;
+        load_page_row(p, row, rows, j, half, pbase, sbase, off, tok0, has_k, has_v, cur);
+        for (; row < rows; row += RB) {
+            load_page_row(p, row + RB, rows, j, half, pbase, sbase, off, tok0, has_k, has_v, nxt);
+            if (cur.valid) {
                 if (has_k) {
-                    ka[u] = ld_stream_v4(p.kq + src);
-                    kb[u] = ld_stream_v4(p.kq + src + half);
-                    ksc[u] = p.ks[sbase + row];
+                    OutT* o = reinterpret_cast<OutT*>(p.ko) + cur.oo;
+                    rope_slice_store<OutT, __half, X16>(cur.ka, cur.kb, cur.ksc, cs, o, o + half);
                 }
                 if (has_v) {
-                    va[u] = ld_stream_v4(p.vq + src);
-                    vb[u] = ld_stream_v4(p.vq + src + half);
-                    vsc[u] = p.vs[sbase + row];
+                    OutT* o = reinterpret_cast<OutT*>(p.vo) + cur.oo;
+                    value_slice_store<OutT, __half>(cur.va, cur.vsc, o);
+                    value_slice_store<OutT, __half>(cur.vb, cur.vsc, o + half);
                 }
             }
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                if (!valid[u]) continue;
-                if (has_k) {
-                    OutT* o = reinterpret_cast<OutT*>(p.ko) + oo[u];
-                    rope_slice_store<OutT, __half, X16>(ka[u], kb[u], ksc[u], c, s, o, o + half);
-                }
-                if (has_v) {
-                    OutT* o = reinterpret_cast<OutT*>(p.vo) + oo[u];
-                    value_slice_store<OutT, __half>(va[u], vsc[u], o);
-                    value_slice_store<OutT, __half>(vb[u], vsc[u], o + half);
-                }
-            }
+            cur = nxt;
         }
     }
 }
@@ -176,12 +185,14 @@ int32_t launch_paged(const PagedArgs& a) {
     if (a.page_table_stride < a.max_pages)
         return set_error(SC_ERR_INVALID_ARGUMENT, "page_table_stride %lld < max_pages %d",
                          (long long)a.page_table_stride, a.max_pages);
-    if (a.out_strides[2] != 1 || a.out_strides[0] % 8 != 0 || a.out_strides[1] % 8 != 0)
+    if (a.out_strides[2] != 1 || a.out_strides[0] % 16 != 0 || a.out_strides[1] % 16 != 0)
         return set_error(SC_ERR_INVALID_ARGUMENT,
-                         "output strides must be [t, h, 1] with t, h multiples of 8 elements");
-    auto al = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
-    if ((has_k && (!al(a.pool_kq) || !al(a.k_out))) || (has_v && (!al(a.pool_vq) || !al(a.v_out))))
-        return set_error(SC_ERR_INVALID_ARGUMENT, "pool and output base pointers must be 16-byte aligned");
+                         "output strides must be [t, h, 1] with t, h multiples of 16 elements");
+    auto al = [](const void* ptr, uintptr_t n) { return (reinterpret_cast<uintptr_t>(ptr) % n) == 0; };
+    if ((has_k && (!al(a.pool_kq, 16) || !al(a.k_out, 32))) ||
+        (has_v && (!al(a.pool_vq, 16) || !al(a.v_out, 32))))
+        return set_error(SC_ERR_INVALID_ARGUMENT,
+                         "pools must be 16-byte and outputs 32-byte aligned");
     if (static_cast<int64_t>(a.page_size) * a.n_heads >= (int64_t(1) << 31))
         return set_error(SC_ERR_INVALID_ARGUMENT, "page_size * n_heads too large");
 

@@ -1,14 +1,17 @@
 // sc_restore.cu — fused INT8 K dequant + relative RoPE shift and V dequant (dense layout),
 // plus the cos/sin table kernel.
 //
-// Vector path (head_dim % 32 == 0, 16-byte aligned rows, unit dim stride):
+// Vector path (head_dim % 32 == 0, unit dim stride, 16-byte aligned input rows and
+// 32-byte aligned output rows):
 //   a row is one (layer, token, head) vector of head_dim int8 codes.  Thread j of a row
 //   owns the 16-frequency slice j: it loads bytes [16j, 16j+16) of the first half and
 //   their rotate-half partners [D/2+16j, D/2+16j+16) with two 16-byte loads, so the
 //   rotation needs no data from other lanes.  The same thread does the V row slice.
-//   The slice's 16 cos/sin values stay in registers for the whole grid-stride loop
-//   (one shift per launch) or are read per token from the caller's table.
-//   Two rows are in flight per thread per iteration (4-8 independent 16-byte loads).
+//   Each 16-output run is written with one 32-byte store, i.e. one full L2 sector.
+//   The cos/sin table of a single shift is built once per block in shared memory and read
+//   as float4 (per-token tables are read from global memory per row).  Each thread keeps
+//   the next row's four 16-byte loads in flight while it converts and stores the current
+//   row, so the load queue never drains during the arithmetic.
 // Generic path: any strides, any even head_dim <= 1024, one thread per (row, frequency).
 #include <type_traits>
 
@@ -18,6 +21,14 @@ namespace sc {
 namespace {
 
 constexpr int kThreads = 256;
+// Resident blocks per SM the register allocation aims for (vector kernels).
+#ifndef SC_DENSE_MIN_BLOCKS
+#define SC_DENSE_MIN_BLOCKS 2
+#endif
+// Row-slices whose loads a thread keeps in flight ahead of the one it stores.
+#ifndef SC_PREFETCH_ROWS
+#define SC_PREFETCH_ROWS 2
+#endif
 
 struct DenseParams {
     int32_t rows;  // n_layers * n_tokens * n_heads  (< 2^31)
@@ -72,37 +83,37 @@ __device__ __forceinline__ void fill_shared_table(const DenseParams& p, float* s
     __syncthreads();
 }
 
+// What one thread carries from the load of a row-slice to its store: the codes and
+// scales only (store addresses are recomputed from the row index).
 template <typename ScaleT>
 struct RowLoad {
     uint4 ka, kb, va, vb;
     ScaleT ksc, vsc;
-    int64_t ko_off, vo_off;
-    int64_t t;
-    bool valid;
+    int32_t row;  // -1 when past the end
 };
 
 template <typename ScaleT>
 __device__ __forceinline__ void load_row(const DenseParams& p, int64_t row, int j,
                                          RowLoad<ScaleT>& r) {
-    r.valid = row < p.rows;
-    if (!r.valid) return;
+    if (row >= p.rows) {
+        r.row = -1;
+        return;
+    }
+    r.row = static_cast<int32_t>(row);
     int64_t l, t, h;
     row_coords(p, static_cast<uint32_t>(row), l, t, h);
-    r.t = t;
     const int half = p.D >> 1;
     if (p.has_k) {
         const int8_t* base = p.kq + l * p.kq_s[0] + t * p.kq_s[1] + h * p.kq_s[2] + j * 16;
         r.ka = ld_stream_v4(base);
         r.kb = ld_stream_v4(base + half);
         r.ksc = reinterpret_cast<const ScaleT*>(p.ks)[l * p.ks_s[0] + t * p.ks_s[1] + h * p.ks_s[2]];
-        r.ko_off = l * p.ko_s[0] + t * p.ko_s[1] + h * p.ko_s[2] + j * 16;
     }
     if (p.has_v) {
         const int8_t* base = p.vq + l * p.vq_s[0] + t * p.vq_s[1] + h * p.vq_s[2] + j * 16;
         r.va = ld_stream_v4(base);
         r.vb = ld_stream_v4(base + half);
         r.vsc = reinterpret_cast<const ScaleT*>(p.vs)[l * p.vs_s[0] + t * p.vs_s[1] + h * p.vs_s[2]];
-        r.vo_off = l * p.vo_s[0] + t * p.vo_s[1] + h * p.vo_s[2] + j * 16;
     }
 }
 
@@ -127,51 +138,52 @@ __device__ __forceinline__ void load_token_cs(const DenseParams& p, int64_t t, i
 
 template <typename OutT, typename ScaleT, bool X16, bool PER_TOKEN>
 __device__ __forceinline__ void store_row(const DenseParams& p, const RowLoad<ScaleT>& r, int j,
-                                          const float* c, const float* s) {
-    if (!r.valid) return;
+                                          const CsShared& cs) {
+    if (r.row < 0) return;
+    int64_t l, t, h;
+    row_coords(p, static_cast<uint32_t>(r.row), l, t, h);
     const int half = p.D >> 1;
     if (p.has_k) {
-        OutT* o = reinterpret_cast<OutT*>(p.ko) + r.ko_off;
+        OutT* o = reinterpret_cast<OutT*>(p.ko) + (l * p.ko_s[0] + t * p.ko_s[1] + h * p.ko_s[2] + j * 16);
         if constexpr (PER_TOKEN) {
             float ct[16], st[16];
-            load_token_cs(p, r.t, j, ct, st);
-            rope_slice_store<OutT, ScaleT, X16>(r.ka, r.kb, r.ksc, ct, st, o, o + half);
+            load_token_cs(p, t, j, ct, st);
+            rope_slice_store<OutT, ScaleT, X16>(r.ka, r.kb, r.ksc, CsRegs{ct, st}, o, o + half);
         } else {
-            rope_slice_store<OutT, ScaleT, X16>(r.ka, r.kb, r.ksc, c, s, o, o + half);
+            rope_slice_store<OutT, ScaleT, X16>(r.ka, r.kb, r.ksc, cs, o, o + half);
         }
     }
     if (p.has_v) {
-        OutT* o = reinterpret_cast<OutT*>(p.vo) + r.vo_off;
+        OutT* o = reinterpret_cast<OutT*>(p.vo) + (l * p.vo_s[0] + t * p.vo_s[1] + h * p.vo_s[2] + j * 16);
         value_slice_store<OutT, ScaleT>(r.va, r.vsc, o);
         value_slice_store<OutT, ScaleT>(r.vb, r.vsc, o + half);
     }
 }
 
+// Grid-stride over rows; each thread keeps the next row's loads in flight while it
+// converts and stores the current one.
 template <typename OutT, typename ScaleT, bool X16, bool PER_TOKEN>
-__global__ void __launch_bounds__(kThreads) dense_restore_vec(const __grid_constant__ DenseParams p) {
-    __shared__ float s_cos[kMaxHeadDim / 2];
-    __shared__ float s_sin[kMaxHeadDim / 2];
+__global__ void __launch_bounds__(kThreads, SC_DENSE_MIN_BLOCKS) dense_restore_vec(const __grid_constant__ DenseParams p) {
+    __shared__ __align__(16) float s_cos[kMaxHeadDim / 2];
+    __shared__ __align__(16) float s_sin[kMaxHeadDim / 2];
     const int P = p.P;
     const int j = threadIdx.x % P;
     const int rl = threadIdx.x / P;
     const int RB = blockDim.x / P;
-    float c[16], s[16];
-    if constexpr (!PER_TOKEN) {
-        fill_shared_table(p, s_cos, s_sin);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            c[k] = s_cos[j * 16 + k];
-            s[k] = s_sin[j * 16 + k];
-        }
-    }
+    if constexpr (!PER_TOKEN) fill_shared_table(p, s_cos, s_sin);
+    const CsShared cs{reinterpret_cast<const float4*>(s_cos + j * 16),
+                      reinterpret_cast<const float4*>(s_sin + j * 16)};
     if (rl >= RB) return;
     const int64_t step = static_cast<int64_t>(gridDim.x) * RB;
-    for (int64_t row0 = static_cast<int64_t>(blockIdx.x) * RB + rl; row0 < p.rows; row0 += 2 * step) {
-        RowLoad<ScaleT> r0, r1;
-        load_row<ScaleT>(p, row0, j, r0);
-        load_row<ScaleT>(p, row0 + step, j, r1);
-        store_row<OutT, ScaleT, X16, PER_TOKEN>(p, r0, j, c, s);
-        store_row<OutT, ScaleT, X16, PER_TOKEN>(p, r1, j, c, s);
+    int64_t row = static_cast<int64_t>(blockIdx.x) * RB + rl;
+    RowLoad<ScaleT> buf[SC_PREFETCH_ROWS + 1];
+#pragma unroll
+    for (int k = 0; k < SC_PREFETCH_ROWS; ++k) load_row<ScaleT>(p, row + k * step, j, buf[k]);
+    for (; row < p.rows; row += step) {
+        load_row<ScaleT>(p, row + SC_PREFETCH_ROWS * step, j, buf[SC_PREFETCH_ROWS]);
+        store_row<OutT, ScaleT, X16, PER_TOKEN>(p, buf[0], j, cs);
+#pragma unroll
+        for (int k = 0; k < SC_PREFETCH_ROWS; ++k) buf[k] = buf[k + 1];
     }
 }
 
@@ -278,7 +290,7 @@ cudaError_t launch_vec(const DenseParams& p, cudaStream_t stream) {
     auto kern = dense_restore_vec<OutT, ScaleT, X16, PER_TOKEN>;
     const int threads = (kThreads / p.P) * p.P;
     const int rb = threads / p.P;
-    const int64_t need = (static_cast<int64_t>(p.rows) + 2 * rb - 1) / (2 * rb);
+    const int64_t need = (static_cast<int64_t>(p.rows) + rb - 1) / rb;
     const int64_t cap = static_cast<int64_t>(sm_count()) * blocks_per_sm(kern, threads);
     const int grid = static_cast<int>(need < cap ? (need > 0 ? need : 1) : cap);
     kern<<<grid, threads, 0, stream>>>(p);
@@ -448,14 +460,15 @@ extern "C" int32_t sc_dequant_rope_kv(
     // Vector path eligibility: 16-byte aligned row starts, unit dim stride, D % 32 == 0.
     bool vec = !(flags & SC_FLAG_FORCE_GENERIC) && (head_dim % 32 == 0);
     const int64_t sizes[3] = {n_layers, n_tokens, n_heads};
-    auto rows_ok = [&](const void* base, const int64_t* st, int64_t align_elems) {
-        if (!aligned16(base) || st[3] != 1) return false;
+    // Inputs: 16-byte row starts.  Outputs: 32-byte row starts (one 32-byte store per lane).
+    auto rows_ok = [&](const void* base, const int64_t* st, int64_t align_elems, uintptr_t align_bytes) {
+        if ((reinterpret_cast<uintptr_t>(base) % align_bytes) != 0 || st[3] != 1) return false;
         for (int i = 0; i < 3; ++i)
             if (!stride_ok(st[i], sizes[i], align_elems)) return false;
         return true;
     };
-    if (vec && has_k) vec = rows_ok(k_quant, kq_strides, 16) && rows_ok(k_out, ko_strides, 8);
-    if (vec && has_v) vec = rows_ok(v_quant, vq_strides, 16) && rows_ok(v_out, vo_strides, 8);
+    if (vec && has_k) vec = rows_ok(k_quant, kq_strides, 16, 16) && rows_ok(k_out, ko_strides, 16, 32);
+    if (vec && has_v) vec = rows_ok(v_quant, vq_strides, 16, 16) && rows_ok(v_out, vo_strides, 16, 32);
     if (vec && p.cs_kind == 2)
         vec = aligned16(cos_delta) && aligned16(sin_delta) && p.cs_d == 1 && (p.cs_t % 8) == 0;
 

@@ -1,26 +1,37 @@
 """Benchmark of the SpecCache Path-1 KV restore on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload llama8b|paged|roundtrip|llama70b]
 
-Workload (default, one GPU): Llama-3-8B KV geometry — 32 layers x (K, V), 8 KV heads x
-head_dim 128, T = 8192 tokens, per-(token, head) absmax INT8 codes with fp16 scales made
-from fp16 N(0,1) values (seeded, synthetic), RoPE theta 5e5, one shift drawn uniformly
-in [1, 4096] from the seed, bf16 output written into contiguous per-layer caches.
+Workloads (synthetic, seeded data with the shapes and value distributions below):
 
-* ``value``: algorithmic HBM bytes of the fused restore (int8 K+V in, fp16 scales in,
-  bf16 K+V out: 6*T*H*D + 4*T*H per layer) per second, inputs resident in HBM, one
-  launch restoring all 32 layers per step.  1.62 GB per step exceeds the 126 MB L2, so
-  no flush is needed between steps.
-* ``e2e``: the same metric through the pinned-host restore pipeline
-  (``sc_pipeline_restore``): every step copies the 32 layers' INT8 codes and scales
-  from pinned host slabs (545 MB) and restores them, then reads back the last cache row
-  of K and V.  ``restore_ms`` is the T=8192 restore time.
-* ``cpu_baseline``: the reference's eager CPU arithmetic (the oracle port) on the host
-  cores over a bounded sample (one layer).
-
-With N > 1 (torchrun, one process per GPU) every rank restores its own 8-head shard of
-an N x 8-head model (weak scaling, no collective on the data path); ``value`` is the
-bytes of all ranks over the slowest rank's time.
+* ``llama8b`` (default, the headline): Llama-3-8B KV geometry - 32 layers x (K, V),
+  8 KV heads x head_dim 128, T = 8192 tokens, per-(token, head) absmax INT8 codes with
+  fp16 scales made from fp16 N(0,1) values, RoPE theta 5e5, one shift drawn uniformly in
+  [1, 4096] from the seed, bf16 output into contiguous per-layer caches.
+  - ``value``: algorithmic HBM bytes of the fused restore per second (int8 K+V in, fp16
+    scales in, bf16 K+V out: 6*T*H*D + 4*T*H per layer), inputs resident in HBM, one
+    launch restoring all 32 layers per step.  Inputs + outputs are 1.62 GB per step, far
+    above the 126 MB L2, so no flush is needed between steps.
+  - ``e2e``: the same metric through the pinned-host restore pipeline
+    (``sc_pipeline_restore``, the C ABI): each step copies the 32 layers' codes and
+    scales from pinned host slabs (545 MB), restores them, and reads back the last cache
+    row of K and V.  ``restore_ms`` is the T = 8192 restore time.
+  - ``cpu_baseline``: the reference's eager CPU arithmetic (the oracle port) on the host
+    cores over a bounded sample (one layer).
+  - N > 1 (torchrun): every rank restores its own 8-head shard of an N x 8-head model
+    (weak scaling, no collective on the data path); ``value`` = bytes of all ranks over
+    the slowest rank's time.
+* ``paged``: ragged paged batch, Llama-3-8B geometry - 64 requests with lengths uniform
+  in [256, 8192] and shifts uniform in [0, 4096] from the seed, INT8 pool of 64-token
+  pages addressed by a shuffled page table, restored into packed bf16 caches in one
+  launch.
+* ``roundtrip``: Qwen-2.5-7B-like - 28 layers, 4 KV heads x 128, T = 16384, theta 1e6,
+  fp16 N(0,1) K/V with 2% of channels scaled x10; quantize (bit-exact twin) then restore
+  with shift 2048 into fp16.
+* ``llama70b``: Llama-3-70B KV geometry - 80 layers, 8 KV heads x 128, T = 32768, shift
+  8192, theta 5e5; pinned host slab -> GPU pipeline; with N GPUs each rank restores 8/N
+  heads (strong scaling).  ``value`` is end-to-end (H2D-bound).
 """
 
 from __future__ import annotations
@@ -42,19 +53,33 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 if REPO not in sys.path:
     sys.path.insert(0, REPO)
 
-L_LAYERS, T_TOKENS, H_HEADS, D_HEAD = 32, 8192, 8, 128
-THETA = 500000.0
-CHUNK = 64
 SEED = 0
+CHUNK = 64
+
+WORKLOADS = {
+    "llama8b": dict(layers=32, tokens=8192, heads=8, head_dim=128, theta=500000.0,
+                    out=torch.bfloat16),
+    "paged": dict(requests=64, min_len=256, max_len=8192, heads=8, head_dim=128, page=64,
+                  theta=500000.0, out=torch.bfloat16),
+    "roundtrip": dict(layers=28, tokens=16384, heads=4, head_dim=128, theta=1000000.0,
+                      delta_p=2048, out=torch.float16),
+    "llama70b": dict(layers=80, tokens=32768, heads=8, head_dim=128, theta=500000.0,
+                     delta_p=8192, out=torch.bfloat16),
+}
 
 
-def algorithmic_bytes(layers: int, tokens: int, heads: int, head_dim: int) -> int:
-    """int8 K,V in + fp16 K,V scales in + bf16 K,V out."""
-    return layers * (6 * tokens * heads * head_dim + 4 * tokens * heads)
+def restore_bytes(rows: int, head_dim: int) -> int:
+    """Algorithmic bytes of a restore: int8 K,V in + 2-byte K,V scales + 2-byte K,V out."""
+    return rows * (6 * head_dim + 4)
 
 
-def h2d_bytes(layers: int, tokens: int, heads: int, head_dim: int) -> int:
-    return layers * (2 * tokens * heads * head_dim + 2 * 2 * tokens * heads)
+def quantize_bytes(rows: int, head_dim: int) -> int:
+    """Algorithmic bytes of quantizing K and V: 2-byte in, int8 + 2-byte scale out."""
+    return 2 * rows * (3 * head_dim + 2)
+
+
+def h2d_bytes(rows: int, head_dim: int) -> int:
+    return rows * (2 * head_dim + 4)
 
 
 def draw_shift(seed: int) -> int:
@@ -62,19 +87,22 @@ def draw_shift(seed: int) -> int:
 
 
 def read_peaks() -> tuple[float, str]:
-    path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
-        with open(path) as f:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
             return float(json.load(f)["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
 
 
-def read_profiled_traffic() -> float | None:
-    """Per-launch DRAM bytes of the dense restore kernel from the committed ncu summary."""
-    path = os.path.join(REPO, "profiles", "dense_restore_llama8b_t8192_ncu.txt")
+def read_profiled_traffic(workload: str) -> float | None:
+    """Per-launch DRAM bytes of the workload's dominant kernel, from the committed ncu
+    summary (line ``dram_bytes_per_launch_full: <bytes>``); None if not profiled."""
+    name = {"llama8b": "dense_restore_llama8b_t8192_ncu.txt",
+            "paged": "paged_restore_ragged64_ncu.txt"}.get(workload)
+    if name is None:
+        return None
     try:
-        with open(path) as f:
+        with open(os.path.join(REPO, "profiles", name)) as f:
             for line in f:
                 if line.startswith("dram_bytes_per_launch_full:"):
                     return float(line.split(":", 1)[1].split()[0])
@@ -89,19 +117,20 @@ class ClockSampler:
     QUERY = ("index,clocks.sm,clocks.max.sm,utilization.gpu,power.draw,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, gpu_index: int) -> None:
         self.gpu = gpu_index
         self.proc = None
-        self.file = None
+        self.path = None
 
     def __enter__(self):
         try:
-            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu)],
-                stdout=self.file, stderr=subprocess.DEVNULL)
+                 "-lms", "200", "-i", str(self.gpu)], stdout=fd, stderr=subprocess.DEVNULL)
+            os.close(fd)
         except Exception:
             self.proc = None
         return self
@@ -115,17 +144,15 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
-        if self.file is None:
+        if self.path is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        self.file.flush()
-        with open(self.file.name) as f:
+        with open(self.path) as f:
             rows = [r.strip().split(",") for r in f if r.strip()]
-        os.unlink(self.file.name)
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        os.unlink(self.path)
         sm, smax, reasons, loaded = [], None, set(), []
         for r in rows:
+            vals = [v.strip() for v in r]
             try:
-                vals = [v.strip() for v in r]
                 mhz, mx, util = float(vals[1]), float(vals[2]), float(vals[3])
             except (ValueError, IndexError):
                 continue
@@ -133,7 +160,7 @@ class ClockSampler:
             sm.append(mhz)
             if util >= 50:
                 loaded.append(mhz)
-                for name, v in zip(names, vals[5:9]):
+                for name, v in zip(self.NAMES, vals[5:9]):
                     if v.lower() == "active":
                         reasons.add(name)
         pick = loaded or sm
@@ -141,264 +168,488 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm), "samples_under_load": len(loaded)}
 
 
-def dist_setup(n_gpus: int):
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        import datetime
+class Dist:
+    """One process per GPU (torchrun env); barrier and max-over-ranks on NCCL."""
 
+    def __init__(self) -> None:
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.device = torch.device("cuda", self.local)
+        torch.cuda.set_device(self.device)
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=self.device)
+
+    def barrier(self) -> None:
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max(self, x: float) -> float:
+        if self.world == 1:
+            return x
         import torch.distributed as dist
 
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    return world, rank, local
+        t = torch.tensor([x], dtype=torch.float64, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self) -> None:
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
 
 
-def barrier(world: int) -> None:
-    if world > 1:
-        import torch.distributed as dist
+def time_steps(fn, steps: int, warmup: int, dist: Dist, per_step_events: bool = True):
+    """W untimed steps, then K timed steps bracketed by barrier + synchronize; returns
+    (max-over-ranks total ms, per-step ms list of this rank)."""
+    stream = torch.cuda.current_stream(dist.device)
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(dist.device)
+    dist.barrier()
+    torch.cuda.synchronize(dist.device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    ev[0].record(stream)
+    for i in range(steps):
+        fn()
+        if per_step_events or i == steps - 1:
+            ev[i + 1].record(stream)
+    torch.cuda.synchronize(dist.device)
+    dist.barrier()
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)] if per_step_events else []
+    total = ev[0].elapsed_time(ev[steps])
+    return dist.max(total), per
 
-        dist.barrier()
 
-
-def max_over_ranks(x: float, world: int, device) -> float:
-    if world == 1:
-        return x
-    import torch.distributed as dist
-
-    t = torch.tensor([x], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
-
-
-def make_inputs(scb, device, layers, tokens, heads, head_dim, seed):
-    """Seeded fp16 N(0,1) K/V per layer, quantised on the GPU into [L, T, H, D] codes."""
+# ---------------------------------------------------------------------------------------
+# Synthetic inputs
+# ---------------------------------------------------------------------------------------
+def make_dense_inputs(scb, device, layers, tokens, heads, head_dim, seed, outlier_frac=0.0):
+    """Seeded fp16 N(0,1) K/V per layer (optionally a fraction of channels x10),
+    quantised on the GPU into [L, T, H, D] codes and [L, T, H, 1] fp16 scales."""
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
     kq = torch.empty((layers, tokens, heads, head_dim), dtype=torch.int8, device=device)
     vq = torch.empty_like(kq)
     ks = torch.empty((layers, tokens, heads, 1), dtype=torch.float16, device=device)
     vs = torch.empty_like(ks)
+    n_out = int(round(outlier_frac * head_dim))
     for layer in range(layers):
         for q, s in ((kq, ks), (vq, vs)):
-            x = torch.randn((tokens, heads, head_dim), generator=gen, device=device,
-                            dtype=torch.float32).to(torch.float16)
-            scb.quantize_kv_int8(x, q_out=q[layer], scale_out=s[layer])
+            x = torch.randn((tokens, heads, head_dim), generator=gen, device=device)
+            if n_out:
+                ch = torch.randperm(head_dim, generator=gen, device=device)[:n_out]
+                x[..., ch] *= 10.0
+            scb.quantize_kv_int8(x.to(torch.float16), q_out=q[layer], scale_out=s[layer])
     torch.cuda.synchronize(device)
     return kq, ks, vq, vs
 
 
-def cpu_baseline_sample(layers_total: int, tokens: int, heads: int, head_dim: int, dp: int,
-                        budget_s: float = 10.0) -> dict:
-    """Time the oracle (the reference's eager CPU arithmetic) on one layer, host cores."""
-    oracle = importlib.import_module("oracle.speccache_oracle")
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    g = torch.Generator().manual_seed(SEED)
+def make_paged_case(cfg, seed):
+    """Host-side description of the ragged batch: lengths, shifts, shuffled page table."""
+    rng = np.random.default_rng(seed)
+    n_req, page = cfg["requests"], cfg["page"]
+    lens = rng.integers(cfg["min_len"], cfg["max_len"] + 1, n_req).astype(np.int64)
+    shifts = rng.integers(0, 4097, n_req).astype(np.float32)
+    pages = [(int(n) + page - 1) // page for n in lens]
+    n_pool = int(sum(pages))
+    perm = rng.permutation(n_pool).astype(np.int32)
+    table = np.zeros((n_req, max(pages)), dtype=np.int32)
+    k = 0
+    for r, n in enumerate(pages):
+        table[r, :n] = perm[k:k + n]
+        k += n
+    return lens, shifts, table, n_pool
+
+
+# ---------------------------------------------------------------------------------------
+# CPU baselines (the oracle: the reference's eager arithmetic restated on torch-CPU)
+# ---------------------------------------------------------------------------------------
+def _cpu_layer(tokens, heads, head_dim, seed):
+    g = torch.Generator().manual_seed(seed)
     kq = torch.randint(-127, 128, (tokens, heads, head_dim), generator=g, dtype=torch.int8)
     vq = torch.randint(-127, 128, (tokens, heads, head_dim), generator=g, dtype=torch.int8)
     ks = (torch.rand((tokens, heads, 1), generator=g) * 0.03 + 1e-3).to(torch.float16)
     vs = (torch.rand((tokens, heads, 1), generator=g) * 0.03 + 1e-3).to(torch.float16)
+    return kq, ks, vq, vs
+
+
+def cpu_step_fn(workload: str, cfg: dict):
+    """One bounded CPU sample of the workload; returns (callable, bytes, description)."""
+    oracle = importlib.import_module("oracle.speccache_oracle")
+    h, d = cfg["heads"], cfg["head_dim"]
+    if workload == "paged":
+        t = 4224  # the mean request length of the batch
+        kq, ks, vq, vs = _cpu_layer(t, h, d, SEED)
+        dp = 2048
+
+        def fn():
+            c, s = oracle.compute_rope_cos_sin_delta(dp, d, cfg["theta"])
+            oracle.dequant_rope_shift(kq, ks, c, s, out_dtype=cfg["out"])
+            oracle.dequant_value(vq, vs, out_dtype=cfg["out"])
+
+        return fn, restore_bytes(t * h, d), (
+            f"1 request of mean length {t} of the {cfg['requests']}-request batch "
+            f"(H={h}, D={d}, K shift + V dequant)")
+    t = cfg["tokens"]
+    if workload == "roundtrip":
+        g = torch.Generator().manual_seed(SEED)
+        xk = torch.randn((t, h, d), generator=g).to(torch.float16)
+        xv = torch.randn((t, h, d), generator=g).to(torch.float16)
+
+        def fn():
+            kq, ks = oracle.quantize_kv_int8(xk)
+            vq, vs = oracle.quantize_kv_int8(xv)
+            c, s = oracle.compute_rope_cos_sin_delta(cfg["delta_p"], d, cfg["theta"])
+            oracle.dequant_rope_shift(kq, ks, c, s, out_dtype=cfg["out"])
+            oracle.dequant_value(vq, vs, out_dtype=cfg["out"])
+
+        return fn, quantize_bytes(t * h, d) + restore_bytes(t * h, d), (
+            f"1 of {cfg['layers']} layers (T={t}, H={h}, D={d}: quantize K,V then restore)")
+    kq, ks, vq, vs = _cpu_layer(t, h, d, SEED)
+    dp = cfg.get("delta_p", draw_shift(SEED))
+
+    def fn():
+        c, s = oracle.compute_rope_cos_sin_delta(dp, d, cfg["theta"])
+        oracle.dequant_rope_shift(kq, ks, c, s, out_dtype=cfg["out"])
+        oracle.dequant_value(vq, vs, out_dtype=cfg["out"])
+
+    return fn, restore_bytes(t * h, d), (
+        f"1 of {cfg['layers']} layers (T={t}, H={h}, D={d}, K shift + V dequant)")
+
+
+def cpu_baseline(workload: str, cfg: dict, budget_s: float = 10.0) -> dict:
+    torch.set_num_threads(os.cpu_count() or 1)
+    fn, nbytes, what = cpu_step_fn(workload, cfg)
     times = []
     t_end = time.perf_counter() + budget_s
     while len(times) < 5 or (time.perf_counter() < t_end and len(times) < 200):
         t0 = time.perf_counter()
-        cos, sin = oracle.compute_rope_cos_sin_delta(dp, head_dim, THETA)
-        oracle.dequant_rope_shift(kq, ks, cos, sin, out_dtype=torch.bfloat16)
-        oracle.dequant_value(vq, vs, out_dtype=torch.bfloat16)
+        fn()
         times.append(time.perf_counter() - t0)
     med = statistics.median(times)
-    per_layer = algorithmic_bytes(1, tokens, heads, head_dim)
-    return {"value": per_layer / med / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
-            "kind": "port",
-            "sample": f"1 of {layers_total} layers (T={tokens}, H={heads}, D={head_dim}, K shift "
-                      f"+ V dequant, bf16 out), median of {len(times)} runs; scales linearly per layer",
-            "restore_ms_extrapolated": med * 1e3 * layers_total}
+    return {"value": nbytes / med / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{what}; median of {len(times)} runs; per-layer cost "
+                                      "is independent of the layer, so it scales linearly"}
 
 
 def run_reference(args) -> None:
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    """The reference's CPU implementation of the path (its eager arithmetic, restated in the
+    oracle) on the host cores; rank 0 only under torchrun."""
+    if int(os.environ.get("RANK", "0")) != 0:
         return
-    oracle = importlib.import_module("oracle.speccache_oracle")
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    dp = draw_shift(SEED)
-    g = torch.Generator().manual_seed(SEED)
-    t, h, d = T_TOKENS, H_HEADS, D_HEAD
-    kq = torch.randint(-127, 128, (t, h, d), generator=g, dtype=torch.int8)
-    vq = torch.randint(-127, 128, (t, h, d), generator=g, dtype=torch.int8)
-    ks = (torch.rand((t, h, 1), generator=g) * 0.03 + 1e-3).to(torch.float16)
-    vs = (torch.rand((t, h, 1), generator=g) * 0.03 + 1e-3).to(torch.float16)
-
-    def step():
-        cos, sin = oracle.compute_rope_cos_sin_delta(dp, d, THETA)
-        oracle.dequant_rope_shift(kq, ks, cos, sin, out_dtype=torch.bfloat16)
-        oracle.dequant_value(vq, vs, out_dtype=torch.bfloat16)
-
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    cfg = WORKLOADS[args.workload]
+    torch.set_num_threads(os.cpu_count() or 1)
+    fn, nbytes, what = cpu_step_fn(args.workload, cfg)
     for _ in range(args.warmup):
-        step()
+        fn()
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        step()
+        fn()
         times.append(time.perf_counter() - t0)
-    per_step = algorithmic_bytes(1, t, h, d)
     mean = sum(times) / len(times)
-    value = per_step / mean / 1e9
+    value = nbytes / mean / 1e9
     line = {
-        "impl": "reference", "metric": "dequant+RoPE-shift GB/s (algorithmic bytes)",
-        "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": mean * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32 math, bf16 out",
-        "data": "synthetic (seeded int8 codes, fp16 scales)",
-        "config": {"workload": "llama3-8b KV restore sample: 1 layer of 32, T=8192, H=8, D=128, "
-                               "theta=5e5, bf16 out", "layers_in_sample": 1, "seq_len": t,
-                   "kv_heads": h, "head_dim": d, "delta_p": dp, "l2": "inputs > L2 n/a (CPU)"},
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8/fp16 in, fp32 math, 16-bit out", "data": "synthetic (seeded)",
+        "config": workload_config(args.workload, cfg, world),
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": torch.get_num_threads(),
                          "kind": "port",
-                         "sample": "one layer of the 32-layer workload per step (reference eager "
-                                   "arithmetic restated in torch-CPU, the oracle)"},
+                         "sample": f"{what} per step (the reference's eager arithmetic "
+                                   "restated on torch-CPU, the oracle)"},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args) -> None:
-    world, rank, local = dist_setup(args.gpus)
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    scb = importlib.import_module("intelligent-bell_b200")
+METRIC = ("dequant+RoPE-shift GB/s (algorithmic bytes) & % of B200 HBM peak; "
+          "T=8192 KV restore ms")
+
+
+def workload_config(workload: str, cfg: dict, world: int) -> dict:
+    if workload == "llama8b":
+        return {"workload": "llama3-8b KV restore: 32 layers x (K,V), T=8192, 8 KV heads x 128 "
+                            "per GPU, theta=5e5, one delta_p in [1,4096], bf16 per-layer caches",
+                "layers": cfg["layers"], "seq_len": cfg["tokens"], "kv_heads_per_gpu": cfg["heads"],
+                "head_dim": cfg["head_dim"], "delta_p": draw_shift(SEED), "theta": cfg["theta"],
+                "parallelism": f"kv-head shards x{world} (weak)",
+                "l2": "inputs+outputs 1.62 GB per step > 126 MB L2 (no flush needed)"}
+    if workload == "paged":
+        return {"workload": "ragged paged batch: 64 requests, lengths U[256,8192], delta_p "
+                            "U[0,4096], 64-token pages, shuffled page table, H=8, D=128, "
+                            "bf16 packed caches", "requests": cfg["requests"], "page": cfg["page"],
+                "kv_heads": cfg["heads"], "head_dim": cfg["head_dim"], "theta": cfg["theta"],
+                "parallelism": f"independent batches x{world} (weak)",
+                "l2": "about 1.7 GB per step > L2 (no flush needed)"}
+    if workload == "roundtrip":
+        return {"workload": "qwen2.5-7b-like round trip: 28 layers, T=16384, 4 KV heads x 128, "
+                            "theta=1e6, 2% outlier channels; quantize then restore (delta_p 2048) "
+                            "to fp16", "layers": cfg["layers"], "seq_len": cfg["tokens"],
+                "kv_heads": cfg["heads"], "head_dim": cfg["head_dim"], "theta": cfg["theta"],
+                "delta_p": cfg["delta_p"], "parallelism": f"replicas x{world} (weak)",
+                "l2": "3.4 GB per step > L2 (no flush needed)"}
+    return {"workload": "llama3-70b KV restore from pinned host: 80 layers, T=32768, 8 KV heads "
+                        "x 128 sharded over the GPUs, delta_p 8192, theta=5e5, bf16",
+            "layers": cfg["layers"], "seq_len": cfg["tokens"], "kv_heads_total": cfg["heads"],
+            "kv_heads_per_gpu": cfg["heads"] // world, "head_dim": cfg["head_dim"],
+            "parallelism": f"kv-head shards x{world} (strong)", "l2": "pinned host source"}
+
+
+# ---------------------------------------------------------------------------------------
+# GPU arms
+# ---------------------------------------------------------------------------------------
+def roofline(nbytes: float, per_step_ms: list[float], workload: str) -> dict:
+    peak, kind = read_peaks()
+    avg = sum(per_step_ms) / len(per_step_ms)
+    achieved = nbytes / (avg / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "traffic": read_profiled_traffic(workload),
+            "peak_source": f"{kind} (MEASURED_PEAKS.json hbm_gbs, copy bandwidth)",
+            "launch_ms": avg}
+
+
+def e2e_line(nbytes, e2e_ms, steps, world, h2d, d2h, launches, path, extra=None) -> dict:
+    out = {"value": nbytes * world * steps / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+           "restore_ms": e2e_ms / steps, "h2d_bytes_per_step": int(h2d),
+           "d2h_bytes_per_step": int(d2h),
+           "h2d_gbs": h2d * world * steps / (e2e_ms / 1e3) / 1e9, "path": path,
+           "gpu_launches": launches}
+    out.update(extra or {})
+    return out
+
+
+def bench_llama8b(args, scb, dist: Dist, cfg: dict):
     from speccache_b200.cache import KVRestorePipeline
 
-    layers, t, h, d = args.layers, T_TOKENS, H_HEADS, D_HEAD
-    dp = draw_shift(SEED)
-    kq, ks, vq, vs = make_inputs(scb, device, layers, t, h, d, SEED + 1000 * rank)
-    k_out = torch.empty((layers, t, h, d), dtype=torch.bfloat16, device=device)
+    layers, t, h, d = args.layers, cfg["tokens"], cfg["heads"], cfg["head_dim"]
+    dev, dp, theta = dist.device, draw_shift(SEED), cfg["theta"]
+    kq, ks, vq, vs = make_dense_inputs(scb, dev, layers, t, h, d, SEED + 1000 * dist.rank)
+    k_out = torch.empty((layers, t, h, d), dtype=cfg["out"], device=dev)
     v_out = torch.empty_like(k_out)
-    per_step = algorithmic_bytes(layers, t, h, d)
-    stream = torch.cuda.current_stream(device)
+    nbytes = restore_bytes(layers * t * h, d)
 
     def step():
-        scb.restore_layers(kq, ks, vq, vs, delta_p=dp, theta=THETA, k_out=k_out, v_out=v_out)
+        scb.restore_layers(kq, ks, vq, vs, delta_p=dp, theta=theta, k_out=k_out, v_out=v_out)
 
-    # ---- e2e set-up: pinned host slabs with the same codes ---------------------------
+    total_ms, per = time_steps(step, args.steps, args.warmup, dist)
+    line = {"value": nbytes * dist.world * args.steps / (total_ms / 1e3) / 1e9,
+            "ms_per_step": total_ms / args.steps, "roofline": roofline(nbytes, per, "llama8b"),
+            "gpu_launches": args.steps}
+    if args.skip_e2e:
+        return line
     n_blocks = t // CHUNK
-    pipe = None if args.skip_e2e else KVRestorePipeline(layers, n_blocks, CHUNK, h, d, device=device,
-                             max_restore_blocks=n_blocks, n_slots=3)
-    if pipe is not None:
+    with KVRestorePipeline(layers, n_blocks, CHUNK, h, d, device=dev, n_slots=3) as pipe:
         pipe.k_quant.view(layers, t, h, d).copy_(kq.cpu())
         pipe.v_quant.view(layers, t, h, d).copy_(vq.cpu())
         pipe.k_scale.view(layers, t, h, 1).copy_(ks.cpu())
         pipe.v_scale.view(layers, t, h, 1).copy_(vs.cpu())
-    e2e_k = [k_out[layer] for layer in range(layers)]
-    e2e_v = [v_out[layer] for layer in range(layers)]
-    block_ids = list(range(n_blocks))
-    shifts = [dp] * n_blocks
-    tail_host = torch.empty((2, h, d), dtype=torch.bfloat16).pin_memory()
+        ko = [k_out[i] for i in range(layers)]
+        vo = [v_out[i] for i in range(layers)]
+        ids, shifts = list(range(n_blocks)), [dp] * n_blocks
+        tail = torch.empty((2, h, d), dtype=cfg["out"]).pin_memory()
+
+        def e2e_step():
+            pipe.restore(ids, shifts, ko, vo, theta=theta)
+            tail[0].copy_(k_out[layers - 1, t - 1], non_blocking=True)
+            tail[1].copy_(v_out[layers - 1, t - 1], non_blocking=True)
+
+        e2e_ms, _ = time_steps(e2e_step, args.steps, args.warmup, dist, per_step_events=False)
+        # one restore on its own (latency, nothing overlapping it)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        e2e_step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        single_ms = e0.elapsed_time(e1)
+        status = pipe.status()
+    line["e2e"] = e2e_line(nbytes, e2e_ms, args.steps, dist.world, h2d_bytes(layers * t * h, d),
+                           tail.numel() * tail.element_size(), layers * args.steps,
+                           "sc_pipeline_restore from pinned host slabs, one kernel per layer",
+                           {"restore_ms_single": single_ms, "device_status": status})
+    return line
+
+
+def bench_paged(args, scb, dist: Dist, cfg: dict):
+    dev = dist.device
+    h, d, page = cfg["heads"], cfg["head_dim"], cfg["page"]
+    lens, shifts, table, n_pool = make_paged_case(cfg, SEED + dist.rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED + dist.rank)
+    pkq = torch.randint(-127, 128, (n_pool, page, h, d), generator=gen, device=dev, dtype=torch.int8)
+    pvq = torch.randint(-127, 128, (n_pool, page, h, d), generator=gen, device=dev, dtype=torch.int8)
+    pks = (torch.rand((n_pool, page, h, 1), generator=gen, device=dev) * 0.03 + 1e-3).half()
+    pvs = (torch.rand((n_pool, page, h, 1), generator=gen, device=dev) * 0.03 + 1e-3).half()
+    total = int(lens.sum())
+    k_out = torch.empty((total, h, d), dtype=cfg["out"], device=dev)
+    v_out = torch.empty_like(k_out)
+    cu = np.concatenate([[0], np.cumsum(lens)])
+    offs = torch.from_numpy(cu[:-1] * h * d).to(dev)
+    tab, lens_d = torch.from_numpy(table).to(dev), torch.from_numpy(lens.astype(np.int32)).to(dev)
+    dps = torch.from_numpy(shifts).to(dev)
+    nbytes = restore_bytes(total * h, d)
+
+    def step():
+        scb.restore_paged(pkq, pks, pvq, pvs, tab, lens_d, dps, theta=cfg["theta"],
+                          k_out=k_out, v_out=v_out, out_offsets=offs)
+
+    total_ms, per = time_steps(step, args.steps, args.warmup, dist)
+    status = scb.paged_status(dev)
+    line = {"value": nbytes * dist.world * args.steps / (total_ms / 1e3) / 1e9,
+            "ms_per_step": total_ms / args.steps, "roofline": roofline(nbytes, per, "paged"),
+            "gpu_launches": args.steps, "device_status": status,
+            "tokens": total, "pool_pages": n_pool}
+    if args.skip_e2e:
+        return line
+    # e2e: the pool's pages arrive from pinned host memory, then one restore launch
+    hosts = [x.cpu().pin_memory() for x in (pkq, pks, pvq, pvs)]
+    tail = torch.empty((2, h, d), dtype=cfg["out"]).pin_memory()
 
     def e2e_step():
-        pipe.restore(block_ids, shifts, e2e_k, e2e_v, theta=THETA)
-        tail_host[0].copy_(k_out[layers - 1, t - 1], non_blocking=True)
-        tail_host[1].copy_(v_out[layers - 1, t - 1], non_blocking=True)
+        for dst, src in zip((pkq, pks, pvq, pvs), hosts):
+            dst.copy_(src, non_blocking=True)
+        step()
+        tail[0].copy_(k_out[total - 1], non_blocking=True)
+        tail[1].copy_(v_out[total - 1], non_blocking=True)
 
-    with ClockSampler(device.index if device.index is not None else 0) as clocks:
-        # ---- value: kernel with inputs resident ------------------------------------------
-        for _ in range(args.warmup):
-            step()
-        barrier(world)
-        torch.cuda.synchronize(device)
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
-        ev[0].record(stream)
-        for i in range(args.steps):
-            step()
-            ev[i + 1].record(stream)
-        torch.cuda.synchronize(device)
-        barrier(world)
-        launch_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
-        total_ms = ev[0].elapsed_time(ev[-1])
-        total_ms_max = max_over_ranks(total_ms, world, device)
+    e2e_ms, _ = time_steps(e2e_step, args.steps, args.warmup, dist, per_step_events=False)
+    h2d = sum(x.numel() * x.element_size() for x in hosts)
+    line["e2e"] = e2e_line(nbytes, e2e_ms, args.steps, dist.world, h2d,
+                           tail.numel() * tail.element_size(), args.steps,
+                           "pool pages H2D from pinned host, then sc_restore_paged")
+    return line
 
-        # ---- e2e: pinned host -> restore -> read back --------------------------------------
-        e2e_ms = None
-        if pipe is not None:
-            for _ in range(args.warmup):
-                e2e_step()
-            torch.cuda.synchronize(device)
-            barrier(world)
-            torch.cuda.synchronize(device)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for _ in range(args.steps):
-                e2e_step()
-            e1.record(stream)
-            torch.cuda.synchronize(device)
-            barrier(world)
-            e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, device)
-    pipe_status = None
-    if pipe is not None:
-        pipe_status = pipe.status()
-        pipe.close()
 
-    if rank != 0:
-        if world > 1:
-            import torch.distributed as dist
+def bench_roundtrip(args, scb, dist: Dist, cfg: dict):
+    dev = dist.device
+    layers, t, h, d = cfg["layers"], cfg["tokens"], cfg["heads"], cfg["head_dim"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED + dist.rank)
+    xs = []
+    for _ in range(2):
+        x = torch.randn((layers, t, h, d), generator=gen, device=dev)
+        ch = torch.randperm(d, generator=gen, device=dev)[: max(1, round(0.02 * d))]
+        x[..., ch] *= 10.0
+        xs.append(x.to(torch.float16).view(layers * t, h, d))
+    xk, xv = xs
+    kq = torch.empty((layers * t, h, d), dtype=torch.int8, device=dev)
+    vq = torch.empty_like(kq)
+    ks = torch.empty((layers * t, h, 1), dtype=torch.float16, device=dev)
+    vs = torch.empty_like(ks)
+    k_out = torch.empty((layers, t, h, d), dtype=cfg["out"], device=dev)
+    v_out = torch.empty_like(k_out)
+    rows = layers * t * h
+    nbytes = quantize_bytes(rows, d) + restore_bytes(rows, d)
 
-            dist.destroy_process_group()
-        return
+    def step():
+        scb.quantize_kv_int8(xk, q_out=kq, scale_out=ks)
+        scb.quantize_kv_int8(xv, q_out=vq, scale_out=vs)
+        scb.restore_layers(kq.view(layers, t, h, d), ks.view(layers, t, h, 1),
+                           vq.view(layers, t, h, d), vs.view(layers, t, h, 1),
+                           delta_p=cfg["delta_p"], theta=cfg["theta"], k_out=k_out, v_out=v_out)
 
-    value = per_step * world * args.steps / (total_ms_max / 1e3) / 1e9
-    avg_launch_ms = sum(launch_ms) / len(launch_ms)
-    achieved = per_step / (avg_launch_ms / 1e3) / 1e9
-    peak, peak_kind = read_peaks()
-    traffic = read_profiled_traffic()
-    e2e = None
-    if e2e_ms is not None:
-        e2e = {"value": per_step * world * args.steps / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
-               "restore_ms": e2e_ms / args.steps,
-               "h2d_bytes_per_step": h2d_bytes(layers, t, h, d),
-               "d2h_bytes_per_step": int(tail_host.numel() * tail_host.element_size()),
-               "h2d_gbs": h2d_bytes(layers, t, h, d) * world * args.steps / (e2e_ms / 1e3) / 1e9,
-               "path": "sc_pipeline_restore from pinned host slabs, one kernel per layer",
-               "gpu_launches": layers * args.steps, "device_status": pipe_status}
-    line = {
-        "metric": "dequant+RoPE-shift GB/s (algorithmic bytes) & % of B200 HBM peak; "
-                  "T=8192 KV restore ms",
-        "value": value,
-        "unit": "GB/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": total_ms_max / args.steps,
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "int8 in, fp32 math, bf16 out",
-        "data": "synthetic: seeded fp16 N(0,1) K/V quantised to int8 + fp16 scales",
-        "config": {
-            "workload": "llama3-8b KV restore: 32 layers x (K,V), T=8192, 8 KV heads x 128, "
-                        "theta=5e5, one delta_p in [1,4096], bf16 contiguous per-layer caches",
-            "layers": layers, "seq_len": t, "kv_heads_per_gpu": h, "head_dim": d,
-            "delta_p": dp, "theta": THETA, "parallelism": f"kv-head shards x{world}",
-            "l2": "inputs+outputs 1.62 GB per step > 126 MB L2 (no flush needed)",
-        },
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": traffic,
-                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
-        "e2e": e2e,
-        "gpu_launches": args.steps,
-        "clocks": clocks.summary(),
-    }
-    if world == 1 and not args.skip_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_sample(layers, t, h, d, dp)
-    print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
+    total_ms, per = time_steps(step, args.steps, args.warmup, dist)
+    line = {"value": nbytes * dist.world * args.steps / (total_ms / 1e3) / 1e9,
+            "ms_per_step": total_ms / args.steps, "roofline": roofline(nbytes, per, "roundtrip"),
+            "gpu_launches": 3 * args.steps}
+    if args.skip_e2e:
+        return line
+    hk, hv = xk.cpu().pin_memory(), xv.cpu().pin_memory()
+    tail = torch.empty((2, h, d), dtype=cfg["out"]).pin_memory()
 
-        dist.destroy_process_group()
+    def e2e_step():
+        xk.copy_(hk, non_blocking=True)
+        xv.copy_(hv, non_blocking=True)
+        step()
+        tail[0].copy_(k_out[layers - 1, t - 1], non_blocking=True)
+        tail[1].copy_(v_out[layers - 1, t - 1], non_blocking=True)
+
+    e2e_ms, _ = time_steps(e2e_step, args.steps, args.warmup, dist, per_step_events=False)
+    line["e2e"] = e2e_line(nbytes, e2e_ms, args.steps, dist.world,
+                           2 * hk.numel() * hk.element_size(), tail.numel() * tail.element_size(),
+                           3 * args.steps, "fp16 K/V H2D from pinned host, quantize, restore")
+    return line
+
+
+def bench_llama70b(args, scb, dist: Dist, cfg: dict):
+    from speccache_b200.cache import KVRestorePipeline
+
+    dev = dist.device
+    layers, t, d = cfg["layers"], cfg["tokens"], cfg["head_dim"]
+    if cfg["heads"] % dist.world:
+        raise SystemExit(f"{cfg['heads']} KV heads do not split over {dist.world} GPUs")
+    h = cfg["heads"] // dist.world
+    n_blocks = t // CHUNK
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED + dist.rank)
+    k_out = torch.empty((layers, t, h, d), dtype=cfg["out"], device=dev)
+    v_out = torch.empty_like(k_out)
+    rows = layers * t * h
+    nbytes = restore_bytes(rows, d)
+    with KVRestorePipeline(layers, n_blocks, CHUNK, h, d, device=dev, n_slots=3) as pipe:
+        for layer in range(layers):  # this rank's head shard of every layer
+            for q, s in ((pipe.k_quant, pipe.k_scale), (pipe.v_quant, pipe.v_scale)):
+                x = torch.randn((t, h, d), generator=gen, device=dev).to(torch.float16)
+                qd, sd = scb.quantize_kv_int8(x)
+                q[layer].view(t, h, d).copy_(qd.cpu())
+                s[layer].view(t, h, 1).copy_(sd.cpu())
+        ko = [k_out[i] for i in range(layers)]
+        vo = [v_out[i] for i in range(layers)]
+        ids, shifts = list(range(n_blocks)), [cfg["delta_p"]] * n_blocks
+        tail = torch.empty((2, h, d), dtype=cfg["out"]).pin_memory()
+
+        def step():
+            pipe.restore(ids, shifts, ko, vo, theta=cfg["theta"])
+            tail[0].copy_(k_out[layers - 1, t - 1], non_blocking=True)
+            tail[1].copy_(v_out[layers - 1, t - 1], non_blocking=True)
+
+        total_ms, _ = time_steps(step, args.steps, args.warmup, dist, per_step_events=False)
+        status = pipe.status()
+    h2d = h2d_bytes(rows, d)
+    e2e = e2e_line(nbytes, total_ms, args.steps, 1, h2d * dist.world,
+                   tail.numel() * tail.element_size(), layers * args.steps,
+                   "sc_pipeline_restore from pinned host slabs (all ranks' bytes)",
+                   {"device_status": status})
+    return {"value": e2e["value"], "ms_per_step": total_ms / args.steps, "scaling": "strong",
+            "gpu_launches": layers * args.steps, "e2e": e2e,
+            "roofline": {"bound": "pcie-h2d", "achieved": e2e["h2d_gbs"] / dist.world,
+                         "unit": "GB/s per GPU", "peak": None, "frac": None, "traffic": None}}
+
+
+def run_ours(args) -> None:
+    dist = Dist()
+    scb = importlib.import_module("intelligent-bell_b200")
+    cfg = WORKLOADS[args.workload]
+    fn = {"llama8b": bench_llama8b, "paged": bench_paged, "roundtrip": bench_roundtrip,
+          "llama70b": bench_llama70b}[args.workload]
+    with ClockSampler(dist.device.index or 0) as clocks:
+        part = fn(args, scb, dist, cfg)
+    if dist.rank == 0:
+        line = {"metric": METRIC, "value": part.pop("value"), "unit": "GB/s",
+                "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": part.pop("ms_per_step"), "higher_is_better": True,
+                "scaling": part.pop("scaling", "weak"), "vs_baseline": None,
+                "dtype": "int8 in, fp32 math, " + str(cfg["out"]).replace("torch.", "") + " out",
+                "data": "synthetic: seeded, see config",
+                "config": workload_config(args.workload, cfg, dist.world)}
+        line.update(part)
+        line["clocks"] = clocks.summary()
+        if dist.world == 1 and not args.skip_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.workload, cfg)
+        print(json.dumps(line), flush=True)
+    dist.close()
 
 
 def main() -> None:
@@ -407,13 +658,14 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--layers", type=int, default=L_LAYERS,
-                    help="layers per step (32 = the workload; fewer only for profiling captures)")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama8b")
+    ap.add_argument("--layers", type=int, default=WORKLOADS["llama8b"]["layers"],
+                    help="llama8b layers per step (32 = the workload; fewer only for "
+                         "profiling captures)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling aid: kernel leg only")
     ap.add_argument("--skip-cpu-baseline", action="store_true", help="profiling aid")
     args = ap.parse_args()
-    if args.warmup < 3:
-        args.warmup = 3
+    args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         run_reference(args)
     else:

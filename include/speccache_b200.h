@@ -125,6 +125,30 @@ SC_API int32_t sc_dequant_rope_kv(int32_t n_layers, int64_t n_tokens, int32_t n_
                            int32_t out_dtype, uint32_t flags, void* stream);
 
 /*
+ * Per-token-shift restore that allocates no device memory.  No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc (an engine that has
+ * reserved the device's memory for its own pools, or a request path that must not risk
+ * the device synchronisation cudaMalloc/cudaFree can cause).
+ *
+ * Same work as building cos/sin tables for delta_p_tokens (device float32 [n_tokens],
+ * one shift per token) with sc_rope_cos_sin_delta and passing them to sc_dequant_rope_kv,
+ * but the two tables live in a fixed array inside the library (4 MiB per GPU that loads
+ * it, held until exit) instead of caller-allocated buffers.  Limit: n_tokens * head_dim/2
+ * <= 1,048,576 (e.g. 16384 tokens at head_dim 128); larger calls are rejected with
+ * SC_ERR_INVALID_ARGUMENT.  Keys are required, values optional; other arguments as for
+ * sc_dequant_rope_kv.  The first call on a device looks up the array's device address
+ * (make it before any stream capture).  Calls share the array: calls that overlap on the
+ * GPU race.
+ */
+SC_API int32_t sc_dequant_rope_kv_token_shifts_noalloc(
+    int32_t n_layers, int64_t n_tokens, int32_t n_heads, int32_t head_dim, const int8_t* k_quant,
+    const int64_t* kq_strides, const void* k_scale, const int64_t* ks_strides,
+    const int8_t* v_quant, const int64_t* vq_strides, const void* v_scale,
+    const int64_t* vs_strides, int32_t scale_dtype, const float* delta_p_tokens,
+    double theta_base, const float* inv_freq, void* k_out, const int64_t* ko_strides,
+    void* v_out, const int64_t* vo_strides, int32_t out_dtype, uint32_t flags, void* stream);
+
+/*
  * Per-(token, head) absmax INT8 quantisation (the offload twin).
  * Replaces quantize_kv_int8 / quantize_symmetric_int8 (speccache/kernels/reference.py:179-209).
  *

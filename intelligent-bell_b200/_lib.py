@@ -57,6 +57,12 @@ _SIGNATURES = {
                                   _f64, _vp, _f64, _vp,  # delta_p, delta_p_dev, theta, inv_freq
                                   _vp, _vp, _vp, _vp,   # k_out, ko_strides, v_out, vo_strides
                                   _i32, _u32, _vp]),
+    "sc_dequant_rope_kv_token_shifts_noalloc": (_i32, [_i32, _i64, _i32, _i32,
+                                                       _vp, _vp, _vp, _vp,  # K codes/scales
+                                                       _vp, _vp, _vp, _vp,  # V codes/scales
+                                                       _i32, _vp, _f64, _vp,  # dtype, shifts
+                                                       _vp, _vp, _vp, _vp,  # outputs
+                                                       _i32, _u32, _vp]),
     "sc_quantize_int8": (_i32, [_i64, _i32, _i32, _vp, _i32, _vp, _f32, _vp, _vp, _vp, _i32,
                                 _vp, _u32, _vp]),
     "sc_restore_paged": (_i32, [_i32, _i32, _i32, _i32, _i32, _i64,

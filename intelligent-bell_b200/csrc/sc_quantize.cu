@@ -4,11 +4,12 @@
 //   scale = fp16(max(amax / 127, eps))      IEEE fp32 division by 127
 //   q     = clamp(round_half_even(x / float(scale)), -127, 127)   IEEE fp32 division
 //
-// Vector path: a row is G lanes x 16 bytes (G = head_dim * sizeof(x) / 16, a power of two
-// <= 32); the absmax is reduced with G-lane xor shuffles; each lane writes 16/sizeof(x)
-// codes with one store.  Rounding to an integer is done by adding 1.5 * 2^23 (the fp32
-// add rounds half to even and leaves the integer in the low mantissa byte), so no
-// float->int conversion instruction is needed.
+// Vector path: a row is G lanes x 32 bytes (G = head_dim * sizeof(x) / 32, a power of two
+// <= 32, one 256-bit load per lane); the absmax is reduced with G-lane xor shuffles; each
+// lane writes 32/sizeof(x) codes with one store.  Codes come from x * (1/scale) in packed
+// fp32x2 arithmetic, exact unless the quotient lies within 2^-14 of a half-integer, where
+// the lane redoes the IEEE division; rounding to an integer is done by adding 1.5 * 2^23
+// (the fp32 add rounds half to even and leaves the integer in the low mantissa byte).
 // Generic path: one warp per row, any strides, two passes over the row.
 #include <type_traits>
 
@@ -77,16 +78,62 @@ __device__ __forceinline__ float quant_scale(float amax, float eps, bool f16_sca
     return f16_scale ? __half2float(__float2half_rn(s)) : s;
 }
 
-// Round-half-even of a value clamped to [-127, 127], returned as the int8 bit pattern.
-__device__ __forceinline__ uint32_t code_byte(float x, float scale) {
-    float y = __fdiv_rn(x, scale);
+// int8 bit pattern of round_half_even(clamp(y, -127, 127)): adding 1.5 * 2^23 rounds to an
+// integer (half to even) and leaves it in the low mantissa byte.
+__device__ __forceinline__ uint32_t byte_of(float y) {
     y = fminf(fmaxf(y, -127.0f), 127.0f);
     return __float_as_uint(__fadd_rn(y, 12582912.0f)) & 0xffu;
 }
 
+// Exact code: IEEE division, as the reference (clamping before or after rounding gives the
+// same integer in [-127, 127]).
+__device__ __forceinline__ uint32_t code_byte(float x, float scale) {
+    return byte_of(__fdiv_rn(x, scale));
+}
+
+// Fast codes.  y = RN(x * RN(1/scale)) is within 2^-16 of the true quotient x / scale
+// whenever |x / scale| < 128 (two roundings of 2^-24 relative each), and RN(x / scale)
+// is within half an ulp (<= 2^-18) of the true quotient, so when y is farther than
+// kTieBand from every half-integer both round to the same integer.  For a finite row the
+// quotient is also below 127.5 in magnitude (the fp16 scale is amax/127 up to a relative
+// 2^-11, or 0.3 % in the fp16 subnormal range, or the larger eps), so the rounded value
+// needs no clamp.  n = (y + 1.5*2^23) - 1.5*2^23 is y rounded half to even, the sum's
+// low byte is n as int8, and |y - n| > 0.5 - kTieBand flags a quotient near a half-integer,
+// for which the caller redoes the IEEE division.
+constexpr float kTieBand = 6.103515625e-05f;  // 2^-14
+constexpr float kRound = 12582912.0f;          // 1.5 * 2^23
+
+__device__ __forceinline__ void fast_codes2(float2 x, float2 rcp2, uint32_t& t0, uint32_t& t1,
+                                            bool& tie) {
+    const float2 m2 = make_float2(kRound, kRound);
+    const float2 y = __fmul2_rn(x, rcp2);
+    const float2 t = __fadd2_rn(y, m2);
+    const float2 n = __fadd2_rn(t, make_float2(-kRound, -kRound));
+    const float2 r = __fadd2_rn(y, make_float2(-n.x, -n.y));
+    tie |= fabsf(r.x) > 0.5f - kTieBand;
+    tie |= fabsf(r.y) > 0.5f - kTieBand;
+    t0 = __float_as_uint(t.x);
+    t1 = __float_as_uint(t.y);
+}
+
+// Low bytes of four words -> one word.
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+// 32-byte non-coherent load (one 256-bit access; the address must be 32-byte aligned).
+__device__ __forceinline__ void ld_stream_v8(const void* p, uint32_t (&w)[8]) {
+    asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]),
+                   "=r"(w[6]), "=r"(w[7])
+                 : "l"(p));
+}
+
+// Vector path: each lane owns 32 bytes of a row (E = 32 / sizeof(x) elements); G lanes
+// (a power of two <= 32) cover the row.
 template <typename InT, typename ScaleT>
 __global__ void __launch_bounds__(kQThreads) quant_vec(const __grid_constant__ QuantParams p) {
-    constexpr int E = 16 / sizeof(InT);
+    constexpr int E = 32 / sizeof(InT);
     const int G = p.G;
     const int lane = threadIdx.x % G;
     const int RB = blockDim.x / G;
@@ -103,24 +150,36 @@ __global__ void __launch_bounds__(kQThreads) quant_vec(const __grid_constant__ Q
             t = ti;
             h = static_cast<int64_t>(static_cast<uint32_t>(row) - ti * static_cast<uint32_t>(p.H));
             const InT* xp = reinterpret_cast<const InT*>(p.x) + t * p.x_t + h * p.x_h + lane * E;
-            unpack16<InT>(ld_stream_v4(xp), f);
+            uint32_t w[8];
+            ld_stream_v8(xp, w);
+            unpack16<InT>(make_uint4(w[0], w[1], w[2], w[3]), f);
+            unpack16<InT>(make_uint4(w[4], w[5], w[6], w[7]), f + E / 2);
 #pragma unroll
             for (int k = 0; k < E; ++k) m = fmaxf(m, fabsf(f[k]));
         }
         for (int o = G >> 1; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if (!active) continue;
         const float sc = quant_scale(m, p.eps, kF16Scale);
-        uint32_t b[E];
+        const float rcp = __frcp_rn(sc);
+        const float2 rcp2 = make_float2(rcp, rcp);
+        bool tie = !(sc > 0.0f && sc < 3.0e38f);  // non-finite or zero scale: exact path
+        uint32_t tw[E];
 #pragma unroll
-        for (int k = 0; k < E; ++k) b[k] = code_byte(f[k], sc);
-        int8_t* qp = p.q + t * p.q_t + h * p.q_h + lane * E;
-        if constexpr (E == 8) {
-            const uint32_t lo = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
-            const uint32_t hi = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
-            st_v2(qp, make_uint2(lo, hi));
-        } else {
-            *reinterpret_cast<uint32_t*>(qp) = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
+        for (int k = 0; k < E; k += 2)
+            fast_codes2(make_float2(f[k], f[k + 1]), rcp2, tw[k], tw[k + 1], tie);
+        if (tie) {
+#pragma unroll
+            for (int k = 0; k < E; ++k) tw[k] = code_byte(f[k], sc);
         }
+        uint32_t packed[E / 4];
+#pragma unroll
+        for (int k = 0; k < E / 4; ++k)
+            packed[k] = pack_low_bytes(tw[4 * k], tw[4 * k + 1], tw[4 * k + 2], tw[4 * k + 3]);
+        int8_t* qp = p.q + t * p.q_t + h * p.q_h + lane * E;
+        if constexpr (E == 16)
+            st_v4(qp, make_uint4(packed[0], packed[1], packed[2], packed[3]));
+        else
+            st_v2(qp, make_uint2(packed[0], packed[1]));
         if (lane == 0) {
             ScaleT* sp = reinterpret_cast<ScaleT*>(p.s) + t * p.s_t + h * p.s_h;
             if constexpr (kF16Scale)
@@ -157,19 +216,28 @@ __global__ void __launch_bounds__(kQThreads) quant_generic(const __grid_constant
     }
 }
 
+template <typename K>
+int resident_blocks(K kernel) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kQThreads, 0) != cudaSuccess || n <= 0)
+        n = 1;
+    return n;
+}
+
+// Grids are sized to exactly the resident blocks (no partial wave) or to the work.
 template <typename InT, typename ScaleT>
 cudaError_t launch_quant(const QuantParams& p, bool vec, cudaStream_t stream) {
-    const int cap = sm_count() * (2048 / kQThreads);
     if (vec) {
-        const int threads = kQThreads;
-        const int rb = threads / p.G;
+        auto kern = quant_vec<InT, ScaleT>;
+        const int rb = kQThreads / p.G;
         const int64_t need = (static_cast<int64_t>(p.rows) + rb - 1) / rb;
-        const int grid = static_cast<int>(need < cap ? need : cap);
-        quant_vec<InT, ScaleT><<<grid, threads, 0, stream>>>(p);
+        const int64_t cap = static_cast<int64_t>(sm_count()) * resident_blocks(kern);
+        kern<<<static_cast<int>(need < cap ? need : cap), kQThreads, 0, stream>>>(p);
     } else {
+        auto kern = quant_generic<InT, ScaleT>;
         const int64_t need = (static_cast<int64_t>(p.rows) + 7) / 8;
-        const int grid = static_cast<int>(need < cap ? need : cap);
-        quant_generic<InT, ScaleT><<<grid, kQThreads, 0, stream>>>(p);
+        const int64_t cap = static_cast<int64_t>(sm_count()) * resident_blocks(kern);
+        kern<<<static_cast<int>(need < cap ? need : cap), kQThreads, 0, stream>>>(p);
     }
     return cudaGetLastError();
 }
@@ -222,17 +290,19 @@ extern "C" int32_t sc_quantize_int8(int64_t n_tokens, int32_t n_heads, int32_t h
     p.s_t = s_strides[0], p.s_h = s_strides[1];
     p.eps = eps;
 
+    // Vector path: 32 bytes of input per lane (one 256-bit load), G = row_bytes / 32 lanes
+    // per row (a power of two <= 32), 32-byte aligned input rows, E-byte aligned code rows.
     const int es = x_dtype == SC_DTYPE_F32 ? 4 : 2;
-    const int E = 16 / es;
+    const int E = 32 / es;
     const int64_t row_bytes = static_cast<int64_t>(head_dim) * es;
-    int G = static_cast<int>(row_bytes / 16);
-    bool vec = !(flags & SC_FLAG_FORCE_GENERIC) && row_bytes % 16 == 0 && G >= 1 && G <= 32 &&
+    int G = static_cast<int>(row_bytes / 32);
+    bool vec = !(flags & SC_FLAG_FORCE_GENERIC) && row_bytes % 32 == 0 && G >= 1 && G <= 32 &&
                (G & (G - 1)) == 0;
     auto al = [](const void* ptr, int a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; };
     auto st_ok = [](int64_t st, int64_t size, int64_t a) { return size <= 1 || st % a == 0; };
     if (vec) {
-        vec = p.x_d == 1 && al(x, 16) && st_ok(p.x_t * es, n_tokens, 16) &&
-              st_ok(p.x_h * es, n_heads, 16) && p.q_d == 1 && al(q_out, E) &&
+        vec = p.x_d == 1 && al(x, 32) && st_ok(p.x_t * es, n_tokens, 32) &&
+              st_ok(p.x_h * es, n_heads, 32) && p.q_d == 1 && al(q_out, E) &&
               st_ok(p.q_t, n_tokens, E) && st_ok(p.q_h, n_heads, E);
     }
     p.G = vec ? G : 32;

@@ -391,3 +391,25 @@ def test_validation_on_device(scb):
                                               out=torch.empty((4, 2, 64), device=DEV))
     with pytest.raises(ValueError, match="must have shape"):
         scb.dequant_value(k, s, out=torch.empty((4, 2, 63), dtype=torch.float16, device=DEV))
+
+
+@pytest.mark.parametrize("rows", [4096, 65536])
+def test_quantize_ties_and_near_ties_bit_exact(scb, oracle, rows):
+    # Rows whose scale is an exact fp16 value s (one element is 127*s) and whose other
+    # elements are (k + 0.5) * s exactly, or one float32 ulp either side: the quotients land
+    # on or next to half-integers, where the kernel must fall back to the IEEE division.
+    g = torch.Generator().manual_seed(rows)
+    d = 128
+    s16 = (torch.rand((rows, 1), generator=g) * 0.999 + 0.001).to(torch.float16).to(torch.float32)
+    k = torch.randint(-127, 127, (rows, d), generator=g).to(torch.float32)
+    x = (k + 0.5) * s16
+    which = torch.randint(0, 3, (rows, d), generator=g)
+    x = torch.where(which == 1, torch.nextafter(x, torch.full_like(x, float("inf"))), x)
+    x = torch.where(which == 2, torch.nextafter(x, torch.full_like(x, float("-inf"))), x)
+    x[:, 0] = 127.0 * s16[:, 0]
+    x = x.view(rows // 4, 4, d)
+    q, s = scb.quantize_kv_int8(x.to(DEV))
+    q_ref, s_ref = oracle.quantize_kv_int8(x)
+    torch.cuda.synchronize()
+    assert bits_equal(s.cpu(), s_ref)
+    assert torch.equal(q.cpu(), q_ref)

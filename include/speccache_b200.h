@@ -236,7 +236,26 @@ SC_API int32_t sc_pipeline_restore(sc_pipeline* p, const int32_t* block_ids, con
                             void* const* k_out, void* const* v_out, const int64_t* out_strides,
                             int64_t out_numel, int32_t out_dtype, void* compute_stream);
 
-/* Wait (bounded by timeout_s, polling) for the last restore; SC_ERR_TIMEOUT if it ran out. */
+/*
+ * Enqueue the offload of n_blocks freshly computed K/V blocks of one layer into the slabs:
+ * quantize on the GPU (sc_quantize_int8 arithmetic, bit-exact with the reference) into a
+ * device staging buffer on compute_stream, then copy codes and scales to the pinned slabs on
+ * the pipeline's transfer stream.  Replaces the cold-miss offload of the reference runner:
+ * quantize_kv_int8 + .cpu() + PinnedKVPool.write_block (speccache/serving/pipeline.py:506-524,
+ * speccache/cache/pinned_pool.py:275-367).
+ *  k, v       device [n_blocks * chunk_size, n_heads, head_dim], dtype x_dtype (F16|BF16|F32),
+ *             strides [token, head, dim]; block i's tokens go to slab block block_ids[i]
+ *  block_ids  host int32 [n_blocks]
+ * Offloads and restores share the transfer stream, so a restore enqueued after an offload
+ * reads the offloaded blocks.  The host may read the slabs after sc_pipeline_synchronize.
+ */
+SC_API int32_t sc_pipeline_offload(sc_pipeline* p, int32_t layer, const int32_t* block_ids,
+                                   int32_t n_blocks, const void* k, const int64_t* k_strides,
+                                   const void* v, const int64_t* v_strides, int32_t x_dtype,
+                                   void* compute_stream);
+
+/* Wait (bounded by timeout_s, polling) for the last restore and offload; SC_ERR_TIMEOUT if
+ * it ran out. */
 SC_API int32_t sc_pipeline_synchronize(sc_pipeline* p, double timeout_s);
 
 /* Read and clear the device status word of the pipeline's kernels (synchronises). */

@@ -75,6 +75,7 @@ _SIGNATURES = {
     "sc_pipeline_host_slabs": (_i32, [_vp, _vp, _vp, _vp, _vp]),
     "sc_pipeline_restore": (_i32, [_vp, _vp, _vp, _i32, _f64, _vp, _vp, _vp, _vp, _i64, _i32,
                                    _vp]),
+    "sc_pipeline_offload": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _i32, _vp]),
     "sc_pipeline_synchronize": (_i32, [_vp, _f64]),
     "sc_pipeline_status": (_i32, [_vp, _vp]),
     "sc_pipeline_destroy": (_i32, [_vp]),

@@ -1,5 +1,7 @@
-"""Host-side restore machinery: pinned slabs and the multi-layer H2D pipeline."""
+"""Host-side restore machinery: pinned slabs, the pool interface and the H2D pipeline."""
 
+from .pinned_pool import BlockMetadata, OriginalPositionMetadata, PinnedHostPool, PinnedKVPool
 from .pipeline import KVRestorePipeline
 
-__all__ = ["KVRestorePipeline"]
+__all__ = ["BlockMetadata", "KVRestorePipeline", "OriginalPositionMetadata", "PinnedHostPool",
+           "PinnedKVPool"]

@@ -120,8 +120,33 @@ class KVRestorePipeline:
             _lib.DTYPE_CODE[ref.dtype], _lib.stream_handle(self.device))
         _lib.check(rc, "sc_pipeline_restore")
 
+    def offload(self, layer: int, block_ids, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Enqueue quantize-on-GPU + D2H of freshly computed K/V into the slabs.
+
+        ``k`` / ``v``: ``[n * chunk, H, D]`` fp16/bf16/fp32 CUDA tensors; block i's tokens go
+        to slab block ``block_ids[i]`` of ``layer``.  The quantisation is bit-exact with the
+        reference's ``quantize_kv_int8``.  Ordered before later restores (same transfer
+        stream); the host may read the slabs after :meth:`synchronize`.
+        """
+        ids = np.ascontiguousarray(np.asarray(block_ids, dtype=np.int32).reshape(-1))
+        n_tok = ids.size * self.chunk_size
+        for x in (k, v):
+            if x.shape != (n_tok, self.num_kv_heads, self.head_dim) or x.device != self.device:
+                raise ValueError(f"K/V must be [{n_tok}, {self.num_kv_heads}, {self.head_dim}] "
+                                 f"on {self.device}, got {tuple(x.shape)} on {x.device}")
+            if x.dtype not in _lib.DTYPE_CODE:
+                raise TypeError(f"K/V must be float16, bfloat16 or float32, got {x.dtype}")
+        if k.dtype != v.dtype:
+            raise TypeError("K and V must share a dtype")
+        rc = self._lib.sc_pipeline_offload(
+            self._h, int(layer), ids.ctypes.data, int(ids.size), k.data_ptr(),
+            _lib.strides(*k.stride()), v.data_ptr(), _lib.strides(*v.stride()),
+            _lib.DTYPE_CODE[k.dtype], _lib.stream_handle(self.device))
+        _lib.check(rc, "sc_pipeline_offload")
+
     def synchronize(self, timeout: float = 60.0) -> None:
-        """Wait for the last restore, polling; raises TimeoutError after ``timeout`` s."""
+        """Wait for the last restore and offload, polling; raises TimeoutError after
+        ``timeout`` seconds."""
         _lib.check(self._lib.sc_pipeline_synchronize(self._h, float(timeout)), "sc_pipeline_synchronize")
 
     def status(self) -> int:
@@ -133,8 +158,10 @@ class KVRestorePipeline:
         return int(bits.value)
 
     def close(self) -> None:
+        """Release the slabs and device buffers; the slab views become unusable."""
         h = getattr(self, "_h", None)
         if h is not None and h.value:
+            self.k_quant = self.k_scale = self.v_quant = self.v_scale = None
             self._lib.sc_pipeline_destroy(h)
             self._h = ctypes.c_void_p()
 

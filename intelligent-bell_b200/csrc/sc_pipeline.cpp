@@ -9,8 +9,10 @@
 //   * an event per slot joins the transfer stream to the caller's compute stream, where
 //     the paged restore kernel (identity page table, one shift per block) writes the
 //     layer's K and V; a second event per slot releases the slot for layer l + n_slots.
-// Nothing on the host waits during a restore; sc_pipeline_synchronize polls an event
-// with a deadline.
+// The offload runs the other way: the quantize kernel writes a device staging buffer on
+// the compute stream, an event hands it to the transfer stream, D2H copies fill the slabs.
+// Nothing on the host waits during a restore or an offload; sc_pipeline_synchronize polls
+// events with a deadline.
 #include <errno.h>
 #include <sched.h>
 #include <stdio.h>
@@ -115,6 +117,11 @@ struct sc_pipeline {
     std::vector<bool> slot_used;
     cudaEvent_t meta_uploaded = nullptr, done = nullptr;
     bool any_restore = false;
+    // offload: quantize into a device staging buffer, then D2H into the slabs
+    int8_t *o_kq = nullptr, *o_vq = nullptr;
+    uint16_t *o_ks = nullptr, *o_vs = nullptr;
+    cudaEvent_t o_ready = nullptr, o_done = nullptr;
+    bool any_offload = false;
 };
 
 namespace {
@@ -126,8 +133,15 @@ void release(sc_pipeline* p) {
     if (p->done && p->any_restore) cudaEventSynchronize(p->done);
     for (auto e : p->ready) cudaEventDestroy(e);
     for (auto e : p->slot_free) cudaEventDestroy(e);
+    if (p->o_done && p->any_offload) cudaEventSynchronize(p->o_done);
     if (p->meta_uploaded) cudaEventDestroy(p->meta_uploaded);
     if (p->done) cudaEventDestroy(p->done);
+    if (p->o_ready) cudaEventDestroy(p->o_ready);
+    if (p->o_done) cudaEventDestroy(p->o_done);
+    cudaFree(p->o_kq);
+    cudaFree(p->o_vq);
+    cudaFree(p->o_ks);
+    cudaFree(p->o_vs);
     if (p->transfer) cudaStreamDestroy(p->transfer);
     for (auto x : p->d_kq) cudaFree(x);
     for (auto x : p->d_vq) cudaFree(x);
@@ -237,6 +251,12 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
     }
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->meta_uploaded, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->o_ready, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->o_done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaMalloc(&p->o_kq, stage_codes);
+    if (e == cudaSuccess) e = cudaMalloc(&p->o_vq, stage_codes);
+    if (e == cudaSuccess) e = cudaMalloc(&p->o_ks, stage_scales * 2);
+    if (e == cudaSuccess) e = cudaMalloc(&p->o_vs, stage_scales * 2);
     if (e != cudaSuccess) {
         const int32_t rc = cuda_error(e, "pipeline device set-up");
         release(p);
@@ -364,23 +384,101 @@ extern "C" int32_t sc_pipeline_restore(sc_pipeline* p, const int32_t* block_ids,
     return sc::ok();
 }
 
-extern "C" int32_t sc_pipeline_synchronize(sc_pipeline* p, double timeout_s) {
+extern "C" int32_t sc_pipeline_offload(sc_pipeline* p, int32_t layer, const int32_t* block_ids,
+                                       int32_t n_blocks, const void* k, const int64_t* k_strides,
+                                       const void* v, const int64_t* v_strides, int32_t x_dtype,
+                                       void* compute_stream) {
     if (!p) return set_error(SC_ERR_INVALID_ARGUMENT, "null pipeline");
-    if (!p->any_restore) return sc::ok();
+    if (n_blocks == 0) return sc::ok();
+    if (layer < 0 || layer >= p->L)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "layer %d outside [0, %d)", layer, p->L);
+    if (n_blocks < 0 || n_blocks > p->max_blocks)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "n_blocks %d outside [0, %lld]", n_blocks,
+                         (long long)p->max_blocks);
+    if (!block_ids || !k || !v || !k_strides || !v_strides)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "null argument");
+    for (int32_t i = 0; i < n_blocks; ++i)
+        if (block_ids[i] < 0 || block_ids[i] >= p->B)
+            return set_error(SC_ERR_INVALID_ARGUMENT, "block id %d outside [0, %lld)",
+                             block_ids[i], (long long)p->B);
     DeviceGuard g(p->device);
-    const double deadline = now_s() + (timeout_s > 0 ? timeout_s : 0);
+    if (!g.ok) return set_error(SC_ERR_CUDA, "cudaSetDevice(%d) failed", p->device);
+    cudaStream_t cs = static_cast<cudaStream_t>(compute_stream);
+    const int64_t n_tok = static_cast<int64_t>(n_blocks) * p->chunk;
+    cudaError_t e = cudaSuccess;
+    // the staging buffer may still feed the previous offload's copies
+    if (p->any_offload) e = cudaStreamWaitEvent(cs, p->o_done, 0);
+    if (e != cudaSuccess) return cuda_error(e, "ordering the offload staging buffer");
+    const int64_t q_st[3] = {static_cast<int64_t>(p->H) * p->D, p->D, 1};
+    const int64_t s_st[2] = {p->H, 1};
+    int32_t rc = sc_quantize_int8(n_tok, p->H, p->D, k, x_dtype, k_strides, 1e-5f, p->o_kq, q_st,
+                                  p->o_ks, SC_DTYPE_F16, s_st, 0, cs);
+    if (rc != SC_OK) return rc;
+    rc = sc_quantize_int8(n_tok, p->H, p->D, v, x_dtype, v_strides, 1e-5f, p->o_vq, q_st, p->o_vs,
+                          SC_DTYPE_F16, s_st, 0, cs);
+    if (rc != SC_OK) return rc;
+    e = cudaEventRecord(p->o_ready, cs);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(p->transfer, p->o_ready, 0);
+    const size_t row = static_cast<size_t>(p->chunk) * p->H;
+    const size_t blk_codes = row * p->D, blk_scales = row;
+    const size_t lay_codes = static_cast<size_t>(layer) * p->B * blk_codes;
+    const size_t lay_scales = static_cast<size_t>(layer) * p->B * blk_scales;
+    for (int32_t i = 0; i < n_blocks && e == cudaSuccess;) {
+        int32_t n = 1;
+        while (i + n < n_blocks && block_ids[i + n] == block_ids[i] + n) ++n;
+        const size_t b0 = static_cast<size_t>(block_ids[i]);
+        const size_t src = static_cast<size_t>(i);
+        e = cudaMemcpyAsync(p->h_kq + lay_codes + b0 * blk_codes, p->o_kq + src * blk_codes,
+                            n * blk_codes, cudaMemcpyDeviceToHost, p->transfer);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(p->h_vq + lay_codes + b0 * blk_codes, p->o_vq + src * blk_codes,
+                                n * blk_codes, cudaMemcpyDeviceToHost, p->transfer);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(p->h_ks + lay_scales + b0 * blk_scales, p->o_ks + src * blk_scales,
+                                n * blk_scales * 2, cudaMemcpyDeviceToHost, p->transfer);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(p->h_vs + lay_scales + b0 * blk_scales, p->o_vs + src * blk_scales,
+                                n * blk_scales * 2, cudaMemcpyDeviceToHost, p->transfer);
+        i += n;
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(p->o_done, p->transfer);
+    if (e != cudaSuccess) return cuda_error(e, "offload enqueue");
+    p->any_offload = true;
+    return sc::ok();
+}
+
+namespace {
+int32_t wait_event(cudaEvent_t ev, double deadline, double timeout_s, const char* what) {
     for (;;) {
-        const cudaError_t e = cudaEventQuery(p->done);
-        if (e == cudaSuccess) return sc::ok();
-        if (e != cudaErrorNotReady) return cuda_error(e, "restore completion");
+        const cudaError_t e = cudaEventQuery(ev);
+        if (e == cudaSuccess) return SC_OK;
+        if (e != cudaErrorNotReady) return cuda_error(e, what);
         if (now_s() >= deadline)
-            return set_error(SC_ERR_TIMEOUT, "restore not complete after %.3f s", timeout_s);
+            return set_error(SC_ERR_TIMEOUT, "%s not complete after %.3f s", what, timeout_s);
         usleep(50);
     }
+}
+}  // namespace
+
+extern "C" int32_t sc_pipeline_synchronize(sc_pipeline* p, double timeout_s) {
+    if (!p) return set_error(SC_ERR_INVALID_ARGUMENT, "null pipeline");
+    DeviceGuard g(p->device);
+    const double deadline = now_s() + (timeout_s > 0 ? timeout_s : 0);
+    if (p->any_restore) {
+        const int32_t rc = wait_event(p->done, deadline, timeout_s, "restore");
+        if (rc != SC_OK) return rc;
+    }
+    if (p->any_offload) {
+        const int32_t rc = wait_event(p->o_done, deadline, timeout_s, "offload");
+        if (rc != SC_OK) return rc;
+    }
+    return sc::ok();
 }
 
 extern "C" int32_t sc_pipeline_status(sc_pipeline* p, int32_t* status_bits) {
     if (!p || !status_bits) return set_error(SC_ERR_INVALID_ARGUMENT, "null argument");
+    const int32_t rc = sc_pipeline_synchronize(p, 60.0);
+    if (rc != SC_OK) return rc;
     DeviceGuard g(p->device);
     int32_t v = 0;
     cudaError_t e = cudaMemcpy(&v, p->d_status, sizeof(int32_t), cudaMemcpyDeviceToHost);

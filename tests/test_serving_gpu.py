@@ -1,0 +1,182 @@
+"""GPU tests of the pool, injector, cache sink and offload against the oracle and the
+reference's own injector outputs (golden vectors).
+
+Mirrors tests/test_phase3_serving.py:137-235 (multi-layer shifted injection) and
+tests/test_phase2_engine.py:297-359 (multi-chunk pipeline parity) of the reference.
+K is compared with the reference tolerance (the kernels build cos/sin from delta_p, one
+fp16 ulp apart from torch's tables in rare entries), V bit for bit.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import as_tensor, bits_equal
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0) if torch.cuda.is_available() else None
+
+
+def test_multi_layer_shifted_kv_injection(scb, oracle):
+    from speccache_b200.serving import MultiLayerKVInjector, SpecDynamicCache
+
+    layers, h, d, chunk = 4, 4, 64, 32
+    inj = MultiLayerKVInjector(layers, h, d, device=DEV, max_blocks=16, chunk_size=chunk)
+    p_cached, delta_p = 256, -256
+    g = torch.Generator().manual_seed(123)
+    c256, s256 = oracle.compute_rope_cos_sin_delta(p_cached, d)
+    cf = torch.cat([c256, c256], -1)[:, None, :].float()
+    sf = torch.cat([s256, s256], -1)[:, None, :].float()
+    raw_k, raw_v = [], []
+    for layer in range(layers):
+        k = torch.randn((chunk, h, d), generator=g)
+        v = torch.randn((chunk, h, d), generator=g)
+        raw_k.append(k)
+        raw_v.append(v)
+        kq, ks = scb.quantize_kv_int8((k * cf + oracle.rotate_half(k) * sf).to(torch.float16).to(DEV))
+        vq, vs = scb.quantize_kv_int8(v.to(DEV))
+        pool = inj.layer_pools[layer]
+        pool.allocate(block_id=0, start_pos=p_cached)
+        pool.write_block(block_id=0, k_quant=kq.cpu(), k_scale=ks.cpu(), v_quant=vq.cpu(),
+                         v_scale=vs.cpu(), start_pos=p_cached)
+    cache = SpecDynamicCache()
+    legacy = inj.reconstruct_and_inject_multi_layer(cache, block_ids=[0], delta_ps=[delta_p])
+    inj.pipeline.synchronize()
+    assert len(cache) == layers and len(legacy) == layers
+    for layer in range(layers):
+        k_c, v_c = cache[layer]
+        assert k_c.shape == (1, h, chunk, d) and v_c.shape == (1, h, chunk, d)
+        k_exp = raw_k[layer].to(torch.float16).permute(1, 0, 2).unsqueeze(0)
+        v_exp = raw_v[layer].to(torch.float16).permute(1, 0, 2).unsqueeze(0)
+        torch.testing.assert_close(v_c.float().cpu(), v_exp.float(), rtol=2e-2, atol=2e-2)
+        torch.testing.assert_close(k_c.float().cpu(), k_exp.float(), rtol=3e-2, atol=3e-2)
+    inj.close()
+
+
+def test_injector_matches_reference_golden(scb, golden):
+    from speccache_b200.serving import MultiLayerKVInjector, SpecDynamicCache
+
+    kq_all, ks_all = as_tensor(golden["inj_kq"]), as_tensor(golden["inj_ks"])
+    vq_all, vs_all = as_tensor(golden["inj_vq"]), as_tensor(golden["inj_vs"])
+    layers, blocks, chunk, h, d = kq_all.shape
+    block_ids = golden["inj_blocks"].tolist()
+    inj = MultiLayerKVInjector(layers, h, d, device=DEV, max_blocks=blocks, chunk_size=chunk)
+    inj.unified_k_quant.copy_(kq_all)
+    inj.unified_k_scale.copy_(ks_all)
+    inj.unified_v_quant.copy_(vq_all)
+    inj.unified_v_scale.copy_(vs_all)
+    for tag in ("const", "mixed"):
+        cache = SpecDynamicCache()
+        legacy = inj.reconstruct_and_inject_multi_layer(
+            cache, block_ids, golden[f"inj_{tag}_dps"].tolist())
+        inj.pipeline.synchronize()
+        assert inj.pipeline.status() == 0
+        for layer, (k, v) in enumerate(legacy):
+            k_ref = as_tensor(golden[f"inj_{tag}_k{layer}"])
+            v_ref = as_tensor(golden[f"inj_{tag}_v{layer}"])
+            torch.testing.assert_close(k.cpu(), k_ref, rtol=1e-2, atol=1e-2)
+            assert bits_equal(v.contiguous().cpu(), v_ref)
+    inj.close()
+
+
+def test_injector_appends_after_existing_tokens(scb, oracle):
+    from speccache_b200.serving import MultiLayerKVInjector, SpecDynamicCache
+
+    layers, h, d, chunk = 2, 8, 128, 16
+    inj = MultiLayerKVInjector(layers, h, d, device=DEV, max_blocks=8, chunk_size=chunk,
+                               out_dtype=torch.bfloat16, theta=500000.0)
+    g = torch.Generator().manual_seed(4)
+    inj.unified_k_quant.copy_(torch.randint(-127, 128, inj.unified_k_quant.shape, generator=g, dtype=torch.int8))
+    inj.unified_v_quant.copy_(torch.randint(-127, 128, inj.unified_v_quant.shape, generator=g, dtype=torch.int8))
+    inj.unified_k_scale.fill_(0.02)
+    inj.unified_v_scale.fill_(0.03)
+    cache = SpecDynamicCache()
+    prefix = torch.randn((1, h, 5, d), generator=g).to(torch.bfloat16).to(DEV)
+    for layer in range(layers):
+        cache.update(prefix, prefix, layer)
+    inj.reconstruct_and_inject_multi_layer(cache, [6, 1], [10, -10])
+    inj.reconstruct_and_inject_multi_layer(cache, [3], [77])
+    inj.pipeline.synchronize()
+    for layer in range(layers):
+        k, v = cache[layer]
+        assert k.shape == (1, h, 5 + 3 * chunk, d)
+        assert torch.equal(k[:, :, :5], prefix)
+        kr, vr = oracle.restore_blocks(inj.unified_k_quant[layer], inj.unified_k_scale[layer],
+                                       inj.unified_v_quant[layer], inj.unified_v_scale[layer],
+                                       [6, 1, 3], [10, -10, 77], 500000.0, torch.bfloat16)
+        torch.testing.assert_close(k[0, :, 5:].permute(1, 0, 2).float().cpu(), kr.float(),
+                                   rtol=1e-2, atol=1e-2)
+        assert bits_equal(v[0, :, 5:].permute(1, 0, 2).contiguous().cpu(), vr)
+    inj.close()
+
+
+def test_offload_then_restore_round_trip(scb, oracle):
+    from speccache_b200.serving import MultiLayerKVInjector, SpecDynamicCache
+
+    layers, h, d, chunk = 3, 4, 128, 32
+    inj = MultiLayerKVInjector(layers, h, d, device=DEV, max_blocks=10, chunk_size=chunk)
+    g = torch.Generator().manual_seed(9)
+    blocks = [7, 2, 3]
+    ks_, vs_ = [], []
+    for _ in range(layers):
+        ks_.append(torch.randn((len(blocks) * chunk, h, d), generator=g).to(torch.float16))
+        vs_.append(torch.randn((len(blocks) * chunk, h, d), generator=g).to(torch.float16))
+    inj.offload_multi_layer(blocks, [k.to(DEV) for k in ks_], [v.to(DEV) for v in vs_])
+    cache = SpecDynamicCache()
+    inj.reconstruct_and_inject_multi_layer(cache, blocks, [0, 0, 0])  # ordered after the offload
+    inj.pipeline.synchronize()
+    for layer in range(layers):
+        kq, ks = oracle.quantize_kv_int8(ks_[layer])
+        vq, vs = oracle.quantize_kv_int8(vs_[layer])
+        got_kq = torch.cat([inj.unified_k_quant[layer, b] for b in blocks])
+        got_ks = torch.cat([inj.unified_k_scale[layer, b] for b in blocks])
+        got_vq = torch.cat([inj.unified_v_quant[layer, b] for b in blocks])
+        assert torch.equal(got_kq, kq) and torch.equal(got_vq, vq)
+        assert bits_equal(got_ks, ks)
+        k, v = cache[layer]
+        assert bits_equal(v[0].permute(1, 0, 2).contiguous().cpu(), oracle.dequant_value(vq, vs))
+        c, s = oracle.compute_rope_cos_sin_delta(0, d)
+        torch.testing.assert_close(k[0].permute(1, 0, 2).cpu(), oracle.dequant_rope_shift(kq, ks, c, s),
+                                   rtol=0, atol=0)
+    inj.close()
+
+
+def test_pool_async_dma_multi_chunk_parity(scb, oracle):
+    # reference tests/test_phase2_engine.py:297-359: 4 chunks with distinct shifts
+    from speccache_b200.cache import PinnedKVPool
+
+    chunk, h, d = 128, 8, 128
+    pool = PinnedKVPool(8, chunk, h, d, device=DEV)
+    g = torch.Generator().manual_seed(77)
+    ids = []
+    for i in range(4):
+        kq, ks = oracle.quantize_kv_int8(torch.randn((chunk, h, d), generator=g))
+        vq, vs = oracle.quantize_kv_int8(torch.randn((chunk, h, d), generator=g))
+        b = pool.allocate(start_pos=512 * (i + 1))
+        pool.write_block(b, kq, ks, vq, vs, start_pos=512 * (i + 1))
+        ids.append(b)
+    shifts = [100 * i - pool.get_start_pos(b) for i, b in enumerate(ids)]
+    k, v = pool.execute_async_dma_and_rope(ids, shifts)
+    kr, vr = oracle.restore_blocks(pool.k_quant, pool.k_scale, pool.v_quant, pool.v_scale, ids, shifts)
+    torch.testing.assert_close(k.cpu(), kr, rtol=1e-2, atol=1e-2)
+    assert bits_equal(v.cpu(), vr)
+    pool.close()
+
+
+def test_reconstruct_layer_chunk(scb, oracle):
+    from speccache_b200.serving import MultiLayerKVInjector
+
+    inj = MultiLayerKVInjector(2, 4, 64, device=DEV, max_blocks=4, chunk_size=16)
+    g = torch.Generator().manual_seed(5)
+    kq, ks = oracle.quantize_kv_int8(torch.randn((16, 4, 64), generator=g))
+    vq, vs = oracle.quantize_kv_int8(torch.randn((16, 4, 64), generator=g))
+    inj.layer_pools[1].allocate(block_id=2, start_pos=64)
+    inj.layer_pools[1].write_block(2, kq, ks, vq, vs, start_pos=64)
+    k, v = inj.reconstruct_layer_chunk(1, 2, -64)
+    c, s = oracle.compute_rope_cos_sin_delta(-64, 64)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(k.cpu(), oracle.dequant_rope_shift(kq, ks, c, s), rtol=1e-2, atol=1e-2)
+    assert bits_equal(v.cpu(), oracle.dequant_value(vq, vs))
+    inj.close()

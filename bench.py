@@ -169,21 +169,25 @@ class ClockSampler:
 
 
 class Dist:
-    """One process per GPU (torchrun env); barrier and max-over-ranks on NCCL."""
+    """One process per GPU (torchrun env); barrier and max-over-ranks over the process
+    group (NCCL on GPUs; gloo on CPU for the host-side tests)."""
 
-    def __init__(self) -> None:
+    def __init__(self, backend: str = "nccl") -> None:
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
-        self.device = torch.device("cuda", self.local)
-        torch.cuda.set_device(self.device)
+        if backend == "nccl":
+            self.device = torch.device("cuda", self.local)
+            torch.cuda.set_device(self.device)
+        else:
+            self.device = torch.device("cpu")
         if self.world > 1:
             import datetime
 
             import torch.distributed as dist
 
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                    device_id=self.device)
+            kw = {"device_id": self.device} if backend == "nccl" else {}
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
 
     def barrier(self) -> None:
         if self.world > 1:

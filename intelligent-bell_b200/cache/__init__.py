@@ -2,6 +2,7 @@
 
 from .pinned_pool import BlockMetadata, OriginalPositionMetadata, PinnedHostPool, PinnedKVPool
 from .pipeline import KVRestorePipeline
+from .sharding import head_shard, shard_view
 
 __all__ = ["BlockMetadata", "KVRestorePipeline", "OriginalPositionMetadata", "PinnedHostPool",
-           "PinnedKVPool"]
+           "PinnedKVPool", "head_shard", "shard_view"]

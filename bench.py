@@ -622,9 +622,9 @@ def bench_llama70b(args, scb, dist: Dist, cfg: dict):
         total_ms, _ = time_steps(step, args.steps, args.warmup, dist, per_step_events=False)
         status = pipe.status()
     h2d = h2d_bytes(rows, d)
-    e2e = e2e_line(nbytes, total_ms, args.steps, 1, h2d * dist.world,
+    e2e = e2e_line(nbytes, total_ms, args.steps, dist.world, h2d,
                    tail.numel() * tail.element_size(), layers * args.steps,
-                   "sc_pipeline_restore from pinned host slabs (all ranks' bytes)",
+                   "sc_pipeline_restore from pinned host slabs (bytes of all ranks)",
                    {"device_status": status})
     return {"value": e2e["value"], "ms_per_step": total_ms / args.steps, "scaling": "strong",
             "gpu_launches": layers * args.steps, "e2e": e2e,

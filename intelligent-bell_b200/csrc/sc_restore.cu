@@ -8,11 +8,17 @@
 //   their rotate-half partners [D/2+16j, D/2+16j+16) with two 16-byte loads, so the
 //   rotation needs no data from other lanes.  The same thread does the V row slice.
 //   Each 16-output run is written with one 32-byte store, i.e. one full L2 sector.
-//   The cos/sin table of a single shift is built once per block in shared memory and read
-//   as float4 (per-token tables are read from global memory per row).  Each thread keeps
-//   the next row's four 16-byte loads in flight while it converts and stores the current
-//   row, so the load queue never drains during the arithmetic.
+//   Blocks are one-shot tiles of consecutive rows (no grid-stride loop): each thread
+//   issues the loads of its SC_ROWS_PER_THREAD row-slices, then converts and stores them.
+//   On B200 this streams 9-10 % faster than a persistent grid walking the same rows.
+//   The cos/sin table of a single shift is computed once on the host (double cos/sin of
+//   the fp32 angle, rounded to fp32 then fp16, like the reference's tables), travels in the
+//   kernel parameters, and is unpacked into shared memory by every block; a shift read from
+//   device memory is expanded per block; per-token tables are read per row.
 // Generic path: any strides, any even head_dim <= 1024, one thread per (row, frequency).
+#include <math.h>
+#include <string.h>
+
 #include <type_traits>
 
 #include "sc_common.cuh"
@@ -21,13 +27,13 @@ namespace sc {
 namespace {
 
 constexpr int kThreads = 256;
-// Resident blocks per SM the register allocation aims for (vector kernels).
+// Resident blocks per SM the register allocation aims for (vector kernel).
 #ifndef SC_DENSE_MIN_BLOCKS
-#define SC_DENSE_MIN_BLOCKS 2
+#define SC_DENSE_MIN_BLOCKS 4
 #endif
-// Row-slices whose loads a thread keeps in flight ahead of the one it stores.
-#ifndef SC_PREFETCH_ROWS
-#define SC_PREFETCH_ROWS 2
+// Row-slices per thread (all their loads are issued before the first store).
+#ifndef SC_ROWS_PER_THREAD
+#define SC_ROWS_PER_THREAD 1
 #endif
 
 struct DenseParams {
@@ -35,7 +41,8 @@ struct DenseParams {
     int32_t D;
     int32_t P;  // 16-frequency slices per half row: D / 32 (vector path)
     int32_t has_k, has_v;
-    int32_t cs_kind;  // 0: from delta_p, 1: one table row, 2: one table row per token
+    int32_t cs_kind;  // 0: shift in device memory, 1: one table row, 2: one table row per
+                      // token, 3: table computed on the host (in `tab`)
     FastDiv divH, divT;
     int32_t H, T;
     const int8_t* kq;
@@ -48,9 +55,9 @@ struct DenseParams {
     const __half* cos;
     const __half* sin;
     int64_t cs_t, cs_d;
-    float dp;
     const float* dp_dev;
-    float inv_freq[kMaxHeadDim / 2];
+    // cs_kind 0: float inverse frequencies; cs_kind 3: half2(cos, sin) per frequency.
+    uint32_t tab[kMaxHeadDim / 2];
 };
 
 __device__ __forceinline__ void row_coords(const DenseParams& p, uint32_t row, int64_t& l,
@@ -62,20 +69,26 @@ __device__ __forceinline__ void row_coords(const DenseParams& p, uint32_t row, i
     l = static_cast<int64_t>(li);
 }
 
-// Fill the block's shared cos/sin table for a single shift (cs_kind 0 or 1).
+// Fill the block's shared cos/sin table for a single shift (cs_kind 0, 1 or 3).
 __device__ __forceinline__ void fill_shared_table(const DenseParams& p, float* s_cos,
                                                   float* s_sin) {
     const int half = p.D >> 1;
-    if (p.cs_kind == 1) {
+    if (p.cs_kind == 3) {
+        for (int f = threadIdx.x; f < half; f += blockDim.x) {
+            const float2 cs = __half22float2(bit_cast_u32<__half2>(p.tab[f]));
+            s_cos[f] = cs.x;
+            s_sin[f] = cs.y;
+        }
+    } else if (p.cs_kind == 1) {
         for (int f = threadIdx.x; f < half; f += blockDim.x) {
             s_cos[f] = __half2float(p.cos[f * p.cs_d]);
             s_sin[f] = __half2float(p.sin[f * p.cs_d]);
         }
     } else {
-        const float dp = p.dp_dev != nullptr ? *p.dp_dev : p.dp;
+        const float dp = *p.dp_dev;
         for (int f = threadIdx.x; f < half; f += blockDim.x) {
             float c, s;
-            rope_cs(dp, p.inv_freq[f], c, s);
+            rope_cs(dp, __uint_as_float(p.tab[f]), c, s);
             s_cos[f] = c;
             s_sin[f] = s;
         }
@@ -160,31 +173,37 @@ __device__ __forceinline__ void store_row(const DenseParams& p, const RowLoad<Sc
     }
 }
 
-// Grid-stride over rows; each thread keeps the next row's loads in flight while it
-// converts and stores the current one.
-template <typename OutT, typename ScaleT, bool X16, bool PER_TOKEN>
-__global__ void __launch_bounds__(kThreads, SC_DENSE_MIN_BLOCKS) dense_restore_vec(const __grid_constant__ DenseParams p) {
+// Where a block's cos/sin come from (a template parameter, so each order compiles alone):
+enum CsMode : int {
+    kCsCopied = 0,  // host-computed or caller's single row: filled into shared memory first
+    kCsDevice = 1,  // shift read from device memory: expanded (double sincos) while the
+                    // block's loads are in flight
+    kCsToken = 2,   // one table row per token, read per row from global memory
+};
+
+// One-shot tile: block b owns rows [b * RB * R, (b + 1) * RB * R); each thread loads its R
+// row-slices, then converts and stores them.
+template <typename OutT, typename ScaleT, bool X16, int CSM>
+__global__ void __launch_bounds__(kThreads, SC_DENSE_MIN_BLOCKS)
+    dense_restore_vec(const __grid_constant__ DenseParams p) {
     __shared__ __align__(16) float s_cos[kMaxHeadDim / 2];
     __shared__ __align__(16) float s_sin[kMaxHeadDim / 2];
+    constexpr int R = SC_ROWS_PER_THREAD;
+    constexpr bool kPerToken = CSM == kCsToken;
     const int P = p.P;
     const int j = threadIdx.x % P;
     const int rl = threadIdx.x / P;
     const int RB = blockDim.x / P;
-    if constexpr (!PER_TOKEN) fill_shared_table(p, s_cos, s_sin);
+    if constexpr (CSM == kCsCopied) fill_shared_table(p, s_cos, s_sin);
     const CsShared cs{reinterpret_cast<const float4*>(s_cos + j * 16),
                       reinterpret_cast<const float4*>(s_sin + j * 16)};
-    if (rl >= RB) return;
-    const int64_t step = static_cast<int64_t>(gridDim.x) * RB;
-    int64_t row = static_cast<int64_t>(blockIdx.x) * RB + rl;
-    RowLoad<ScaleT> buf[SC_PREFETCH_ROWS + 1];
+    const int64_t row0 = static_cast<int64_t>(blockIdx.x) * RB * R + rl;
+    RowLoad<ScaleT> buf[R];
 #pragma unroll
-    for (int k = 0; k < SC_PREFETCH_ROWS; ++k) load_row<ScaleT>(p, row + k * step, j, buf[k]);
-    for (; row < p.rows; row += step) {
-        load_row<ScaleT>(p, row + SC_PREFETCH_ROWS * step, j, buf[SC_PREFETCH_ROWS]);
-        store_row<OutT, ScaleT, X16, PER_TOKEN>(p, buf[0], j, cs);
+    for (int k = 0; k < R; ++k) load_row<ScaleT>(p, row0 + k * RB, j, buf[k]);
+    if constexpr (CSM == kCsDevice) fill_shared_table(p, s_cos, s_sin);
 #pragma unroll
-        for (int k = 0; k < SC_PREFETCH_ROWS; ++k) buf[k] = buf[k + 1];
-    }
+    for (int k = 0; k < R; ++k) store_row<OutT, ScaleT, X16, kPerToken>(p, buf[k], j, cs);
 }
 
 // Stride-generic path: one thread per (row, frequency f), both halves of the pair.
@@ -252,7 +271,7 @@ __global__ void __launch_bounds__(kThreads)
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int64_t r = i / half;
         const int f = static_cast<int>(i - r * half);
-        const float angle = __fmul_rn(dp[r], p.inv_freq[f]);
+        const float angle = __fmul_rn(dp[r], __uint_as_float(p.tab[f]));
         double sd, cd;
         sincos(static_cast<double>(angle), &sd, &cd);
         const float c = static_cast<float>(cd), s = static_cast<float>(sd);
@@ -263,6 +282,32 @@ __global__ void __launch_bounds__(kThreads)
             cos_out[i] = from_float<OutT>(c);
             sin_out[i] = from_float<OutT>(s);
         }
+    }
+}
+
+void fill_inv_freq(DenseParams& p, int head_dim, double theta, const float* inv_freq) {
+    float tmp[kMaxHeadDim / 2];
+    if (inv_freq == nullptr) {
+        default_inv_freq(head_dim, theta, tmp);
+        inv_freq = tmp;
+    }
+    for (int i = 0; i < head_dim / 2; ++i) memcpy(&p.tab[i], &inv_freq[i], sizeof(float));
+}
+
+// cos/sin of one shift as the reference tabulates them: angle = fp32(dp * inv_freq) (one
+// fp32 multiply), cos/sin in double, rounded to fp32 and then to fp16.
+void fill_host_table(DenseParams& p, int head_dim, float dp, double theta, const float* inv_freq) {
+    float tmp[kMaxHeadDim / 2];
+    if (inv_freq == nullptr) {
+        default_inv_freq(head_dim, theta, tmp);
+        inv_freq = tmp;
+    }
+    for (int i = 0; i < head_dim / 2; ++i) {
+        const volatile float angle = dp * inv_freq[i];  // one rounding, no contraction
+        const __half c = __float2half_rn(static_cast<float>(cos(static_cast<double>(angle))));
+        const __half s = __float2half_rn(static_cast<float>(sin(static_cast<double>(angle))));
+        const __half2 cs = __halves2half2(c, s);
+        memcpy(&p.tab[i], &cs, sizeof(uint32_t));
     }
 }
 
@@ -285,15 +330,13 @@ inline bool stride_ok(int64_t stride, int64_t size, int64_t align) {
     return size <= 1 || (stride % align) == 0;
 }
 
-template <typename OutT, typename ScaleT, bool X16, bool PER_TOKEN>
+template <typename OutT, typename ScaleT, bool X16, int CSM>
 cudaError_t launch_vec(const DenseParams& p, cudaStream_t stream) {
-    auto kern = dense_restore_vec<OutT, ScaleT, X16, PER_TOKEN>;
+    auto kern = dense_restore_vec<OutT, ScaleT, X16, CSM>;
     const int threads = (kThreads / p.P) * p.P;
-    const int rb = threads / p.P;
-    const int64_t need = (static_cast<int64_t>(p.rows) + rb - 1) / rb;
-    const int64_t cap = static_cast<int64_t>(sm_count()) * blocks_per_sm(kern, threads);
-    const int grid = static_cast<int>(need < cap ? (need > 0 ? need : 1) : cap);
-    kern<<<grid, threads, 0, stream>>>(p);
+    const int64_t per_block = static_cast<int64_t>(threads / p.P) * SC_ROWS_PER_THREAD;
+    const int64_t grid = (static_cast<int64_t>(p.rows) + per_block - 1) / per_block;
+    kern<<<static_cast<unsigned>(grid), threads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
@@ -312,11 +355,15 @@ template <typename OutT, typename ScaleT>
 cudaError_t dispatch(const DenseParams& p, const GenericStrides& g, bool vec, bool x16,
                      cudaStream_t stream) {
     if (vec) {
-        if (p.cs_kind == 2)
-            return x16 ? launch_vec<OutT, ScaleT, true, true>(p, stream)
-                       : launch_vec<OutT, ScaleT, false, true>(p, stream);
-        return x16 ? launch_vec<OutT, ScaleT, true, false>(p, stream)
-                   : launch_vec<OutT, ScaleT, false, false>(p, stream);
+        const int mode = p.cs_kind == 2 ? kCsToken : (p.cs_kind == 0 ? kCsDevice : kCsCopied);
+        if (mode == kCsToken)
+            return x16 ? launch_vec<OutT, ScaleT, true, kCsToken>(p, stream)
+                       : launch_vec<OutT, ScaleT, false, kCsToken>(p, stream);
+        if (mode == kCsDevice)
+            return x16 ? launch_vec<OutT, ScaleT, true, kCsDevice>(p, stream)
+                       : launch_vec<OutT, ScaleT, false, kCsDevice>(p, stream);
+        return x16 ? launch_vec<OutT, ScaleT, true, kCsCopied>(p, stream)
+                   : launch_vec<OutT, ScaleT, false, kCsCopied>(p, stream);
     }
     return x16 ? launch_generic<OutT, ScaleT, true>(p, g, stream)
                : launch_generic<OutT, ScaleT, false>(p, g, stream);
@@ -341,10 +388,7 @@ extern "C" int32_t sc_rope_cos_sin_delta(const float* delta_pos, int64_t n, int3
         return set_error(SC_ERR_INVALID_ARGUMENT, "null pointer argument");
     DenseParams p{};
     p.D = head_dim;
-    if (inv_freq)
-        for (int i = 0; i < head_dim / 2; ++i) p.inv_freq[i] = inv_freq[i];
-    else
-        default_inv_freq(head_dim, theta_base, p.inv_freq);
+    fill_inv_freq(p, head_dim, theta_base, inv_freq);
     const int half = head_dim / 2;
     const int64_t total = n * half;
     const int64_t need = (total + kThreads - 1) / kThreads;
@@ -448,13 +492,14 @@ extern "C" int32_t sc_dequant_rope_kv(
         p.cs_d = cs_strides[1];
         p.cs_kind = (p.cs_t == 0 || n_tokens == 1) ? 1 : 2;
     } else {
-        p.cs_kind = 0;
-        p.dp = static_cast<float>(delta_p);
-        p.dp_dev = delta_p_dev;
-        if (inv_freq)
-            for (int i = 0; i < head_dim / 2; ++i) p.inv_freq[i] = inv_freq[i];
-        else
-            default_inv_freq(head_dim, theta_base, p.inv_freq);
+        if (delta_p_dev != nullptr) {
+            p.cs_kind = 0;  // shift known on the device only: expand per block
+            p.dp_dev = delta_p_dev;
+            fill_inv_freq(p, head_dim, theta_base, inv_freq);
+        } else {
+            p.cs_kind = 3;
+            fill_host_table(p, head_dim, static_cast<float>(delta_p), theta_base, inv_freq);
+        }
     }
 
     // Vector path eligibility: 16-byte aligned row starts, unit dim stride, D % 32 == 0.

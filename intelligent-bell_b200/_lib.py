@@ -129,12 +129,76 @@ def strides(*values) -> ctypes.Array:
     return arr
 
 
+class StrideBuffer:
+    """A reusable per-thread host buffer for the stride arrays of one call.
+
+    The library copies the strides during the call, so one buffer per thread can serve
+    every call; ``put`` writes values and returns their address.
+    """
+
+    SIZE = 64
+
+    def __init__(self) -> None:
+        self.buf = (ctypes.c_int64 * self.SIZE)()
+        self.base = ctypes.addressof(self.buf)
+        self.used = 0
+
+    def reset(self) -> "StrideBuffer":
+        self.used = 0
+        return self
+
+    def put(self, values) -> int:
+        n = len(values)
+        start = self.used
+        self.buf[start:start + n] = values
+        self.used = start + n
+        return self.base + 8 * start
+
+
+_tls = threading.local()
+
+
+def stride_buffer() -> StrideBuffer:
+    b = getattr(_tls, "strides", None)
+    if b is None:
+        b = _tls.strides = StrideBuffer()
+    return b.reset()
+
+
 def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """cudaStream_t of torch's current stream on ``device``."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if _raw_stream is not None:
+        return _raw_stream(idx)
+    return torch.cuda.current_stream(idx).cuda_stream
+
+
+class on_device:
+    """Make ``device`` current for the call only if it is not already (cheap no-op path)."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, device: torch.device) -> None:
+        self.idx = device.index
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if self.idx is not None and self.idx != cur:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+        return self
+
+    def __exit__(self, *exc) -> None:
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
 
 
 _INV_FREQ: dict[tuple[int, float], np.ndarray] = {}

@@ -295,20 +295,61 @@ void fill_inv_freq(DenseParams& p, int head_dim, double theta, const float* inv_
 }
 
 // cos/sin of one shift as the reference tabulates them: angle = fp32(dp * inv_freq) (one
-// fp32 multiply), cos/sin in double, rounded to fp32 and then to fp16.
+// fp32 multiply), cos/sin in double, rounded to fp32 and then to fp16.  A few recent tables
+// are kept per host thread (keyed by the shift, head_dim and the inverse frequencies), so
+// restoring many layers with one shift computes the table once.
+struct HostTable {
+    uint32_t dp_bits = 0;
+    int head_dim = 0;
+    uint64_t freq_hash = 0;
+    bool valid = false;
+    uint32_t tab[kMaxHeadDim / 2];
+};
+
+uint64_t hash_freqs(const float* f, int n) {
+    uint64_t h = 1469598103934665603ull;  // FNV-1a over the float bit patterns
+    for (int i = 0; i < n; ++i) {
+        uint32_t b;
+        memcpy(&b, &f[i], sizeof(b));
+        h = (h ^ b) * 1099511628211ull;
+    }
+    return h;
+}
+
 void fill_host_table(DenseParams& p, int head_dim, float dp, double theta, const float* inv_freq) {
     float tmp[kMaxHeadDim / 2];
     if (inv_freq == nullptr) {
         default_inv_freq(head_dim, theta, tmp);
         inv_freq = tmp;
     }
-    for (int i = 0; i < head_dim / 2; ++i) {
-        const volatile float angle = dp * inv_freq[i];  // one rounding, no contraction
-        const __half c = __float2half_rn(static_cast<float>(cos(static_cast<double>(angle))));
-        const __half s = __float2half_rn(static_cast<float>(sin(static_cast<double>(angle))));
-        const __half2 cs = __halves2half2(c, s);
-        memcpy(&p.tab[i], &cs, sizeof(uint32_t));
+    const int half = head_dim / 2;
+    uint32_t dp_bits;
+    memcpy(&dp_bits, &dp, sizeof(dp_bits));
+    const uint64_t fh = hash_freqs(inv_freq, half);
+    constexpr int kEntries = 4;
+    thread_local HostTable cache[kEntries];
+    thread_local int next_slot = 0;
+    for (int e = 0; e < kEntries; ++e) {
+        const HostTable& c = cache[e];
+        if (c.valid && c.dp_bits == dp_bits && c.head_dim == head_dim && c.freq_hash == fh) {
+            memcpy(p.tab, c.tab, sizeof(uint32_t) * half);
+            return;
+        }
     }
+    HostTable& c = cache[next_slot];
+    next_slot = (next_slot + 1) % kEntries;
+    for (int i = 0; i < half; ++i) {
+        const volatile float angle = dp * inv_freq[i];  // one rounding, no contraction
+        const __half cv = __float2half_rn(static_cast<float>(cos(static_cast<double>(angle))));
+        const __half sv = __float2half_rn(static_cast<float>(sin(static_cast<double>(angle))));
+        const __half2 cs = __halves2half2(cv, sv);
+        memcpy(&c.tab[i], &cs, sizeof(uint32_t));
+    }
+    c.dp_bits = dp_bits;
+    c.head_dim = head_dim;
+    c.freq_hash = fh;
+    c.valid = true;
+    memcpy(p.tab, c.tab, sizeof(uint32_t) * half);
 }
 
 template <typename K>

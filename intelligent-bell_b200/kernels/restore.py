@@ -88,18 +88,18 @@ def _launch(n_layers, n_tokens, n_heads, head_dim, kq, ks, vq, vs, cos, sin, dp,
         raise TypeError(f"scale must be torch.float16 (or torch.float32), got {scale.dtype}")
     flags = (_lib.SC_FLAG_FP32_INTERMEDIATE if fp32_intermediate else 0) | (
         _lib.SC_FLAG_FORCE_GENERIC if force_generic else 0)
-    st = _lib.strides
-    kq_s = st(*_strides4(kq)) if kq is not None else None
-    ks_s = st(*_strides4(ks)[:3]) if ks is not None else None
-    vq_s = st(*_strides4(vq)) if vq is not None else None
-    vs_s = st(*_strides4(vs)[:3]) if vs is not None else None
-    ko_s = st(*_strides4(ko)) if ko is not None else None
-    vo_s = st(*_strides4(vo)) if vo is not None else None
+    sb = _lib.stride_buffer()
+    kq_s = sb.put(_strides4(kq)) if kq is not None else None
+    ks_s = sb.put(_strides4(ks)[:3]) if ks is not None else None
+    vq_s = sb.put(_strides4(vq)) if vq is not None else None
+    vs_s = sb.put(_strides4(vs)[:3]) if vs is not None else None
+    ko_s = sb.put(_strides4(ko)) if ko is not None else None
+    vo_s = sb.put(_strides4(vo)) if vo is not None else None
     cs_s = None
     if cos is not None:
-        cs_s = st(0 if cos.shape[0] == 1 else cos.stride(0), cos.stride(1))
+        cs_s = sb.put((0 if cos.shape[0] == 1 else cos.stride(0), cos.stride(1)))
     inv = _lib.inv_freq_ptr(head_dim, theta) if cos is None else None
-    with torch.cuda.device(ref.device):
+    with _lib.on_device(ref.device):
         rc = lib.sc_dequant_rope_kv(
             n_layers, n_tokens, n_heads, head_dim,
             _lib.ptr(kq), kq_s, _lib.ptr(ks), ks_s,

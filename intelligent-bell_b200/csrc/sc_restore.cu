@@ -480,6 +480,8 @@ extern "C" int32_t sc_dequant_rope_kv(
     if (scale_dtype != SC_DTYPE_F16 && scale_dtype != SC_DTYPE_F32)
         return set_error(SC_ERR_INVALID_DTYPE, "scale dtype code %d: float16 or float32 only",
                          scale_dtype);
+    const int64_t rows = static_cast<int64_t>(n_layers) * n_tokens * n_heads;
+    if (rows == 0) return ok();  // empty tensors may carry null pointers
     const bool has_k = k_quant != nullptr, has_v = v_quant != nullptr;
     if (!has_k && !has_v) return set_error(SC_ERR_INVALID_ARGUMENT, "neither K nor V given");
     if (has_k && (!k_scale || !k_out || !kq_strides || !ks_strides || !ko_strides))
@@ -490,11 +492,9 @@ extern "C" int32_t sc_dequant_rope_kv(
         return set_error(SC_ERR_INVALID_ARGUMENT, "cos_delta and sin_delta must both be given");
     if (cos_delta && !cs_strides)
         return set_error(SC_ERR_INVALID_ARGUMENT, "cos/sin tables given without strides");
-    const int64_t rows = static_cast<int64_t>(n_layers) * n_tokens * n_heads;
     if (rows >= (int64_t(1) << 31))
         return set_error(SC_ERR_INVALID_ARGUMENT,
                          "%lld rows in one call; split the call below 2^31 rows", (long long)rows);
-    if (rows == 0) return ok();
 
     DenseParams p{};
     p.rows = static_cast<int32_t>(rows);

@@ -146,6 +146,8 @@ def restore_paged(
         offs = _as_device(cu[:-1] * out.stride(0), dev, torch.int64)
     else:
         offs = _as_device(out_offsets, dev, torch.int64)
+    if lens_host is not None and total == 0:
+        return k_out, v_out, cu
     status = _status_word(dev)
     flags = _lib.SC_FLAG_FP32_INTERMEDIATE if fp32_intermediate else 0
     # The kernel bounds every write by the extent of the output's storage from its data_ptr.

@@ -413,3 +413,99 @@ def test_quantize_ties_and_near_ties_bit_exact(scb, oracle, rows):
     torch.cuda.synchronize()
     assert bits_equal(s.cpu(), s_ref)
     assert torch.equal(q.cpu(), q_ref)
+
+
+def test_fp32_scales_dense_and_quantize(scb, oracle):
+    # float32 scales (an extension): x = fp16(fp32(q * s)) exactly as the reference's
+    # arithmetic would do with float32 scales; quantize with float32 scale output skips the
+    # fp16 rounding of the scale.
+    t, h, d = 50, 4, 128
+    g = torch.Generator().manual_seed(21)
+    kq = torch.randint(-127, 128, (t, h, d), generator=g, dtype=torch.int8)
+    ks32 = torch.rand((t, h, 1), generator=g) * 0.05 + 1e-4
+    vq = torch.randint(-127, 128, (t, h, d), generator=g, dtype=torch.int8)
+    vs32 = torch.rand((t, h, 1), generator=g) * 0.05 + 1e-4
+    cos, sin = oracle.compute_rope_cos_sin_delta(77, d)
+    # the reference-named wrappers keep its fp16-scale contract; restore_layers takes both
+    k = scb.restore_layers(kq[None].to(DEV), ks32[None].to(DEV), vq[None].to(DEV), vs32[None].to(DEV),
+                           delta_p=77, out_dtype=torch.float16)
+    torch.cuda.synchronize()
+    k_ref = oracle.dequant_rope_shift(kq, ks32, cos, sin)
+    torch.testing.assert_close(k[0][0].cpu(), k_ref, rtol=1e-2, atol=1e-2)
+    assert bits_equal(k[1][0].cpu(), oracle.dequant_value(vq, vs32))
+    x = torch.randn((t, h, d), generator=g)
+    q, s = scb.quantize_kv_int8(x.to(DEV), scale_dtype=torch.float32)
+    torch.cuda.synchronize()
+    s_ref = torch.clamp(x.abs().amax(-1, keepdim=True) / 127.0, min=1e-5)
+    q_ref = torch.clamp(torch.round(x / s_ref), -127, 127).to(torch.int8)
+    assert s.dtype == torch.float32 and bits_equal(s.cpu(), s_ref)
+    assert torch.equal(q.cpu(), q_ref)
+
+
+def test_paged_fp32_intermediate_and_fp16(scb, oracle):
+    pkq, pks, pvq, pvs, table, lens, dps = _paged_case(oracle, 5, 32, 4, 64, 31, 150)
+    cos_ref = [oracle.compute_rope_cos_sin_delta(dp, 64) for dp in dps]
+    k, v, cu = scb.restore_paged(pkq.to(DEV), pks.to(DEV), pvq.to(DEV), pvs.to(DEV), table, lens,
+                                 dps, out_dtype=torch.float16, fp32_intermediate=True)
+    torch.cuda.synchronize()
+    for r in range(len(lens)):
+        n = (lens[r] + 31) // 32
+        ids = table[r, :n].tolist()
+        kq = oracle.gather_blocks(pkq, ids)[: lens[r]]
+        ks = oracle.gather_blocks(pks, ids)[: lens[r]]
+        ref = oracle.dequant_rope_shift(kq, ks, *cos_ref[r], fp16_intermediate=False)
+        torch.testing.assert_close(k[cu[r]:cu[r + 1]].cpu(), ref, rtol=1e-2, atol=1e-2)
+
+
+def test_empty_inputs_are_no_ops(scb):
+    k = torch.zeros((0, 8, 128), dtype=torch.int8, device=DEV)
+    s = torch.zeros((0, 8, 1), dtype=torch.float16, device=DEV)
+    out = scb.triton_fused_k_dequant_rope_shift(k, s, delta_p=5)
+    v = scb.dequant_value(k, s)
+    q, sc = scb.quantize_kv_int8(torch.zeros((0, 8, 128), device=DEV))
+    torch.cuda.synchronize()
+    assert out.shape == (0, 8, 128) and v.shape == (0, 8, 128) and q.shape == (0, 8, 128)
+    kp, vp, cu = scb.restore_paged(torch.zeros((2, 16, 2, 64), dtype=torch.int8, device=DEV),
+                                   torch.ones((2, 16, 2, 1), dtype=torch.float16, device=DEV),
+                                   None, None, torch.zeros((3, 2), dtype=torch.int32),
+                                   [0, 0, 0], [1, 2, 3])
+    torch.cuda.synchronize()
+    assert kp.shape == (0, 2, 64) and vp is None and cu.tolist() == [0, 0, 0, 0]
+
+
+def test_concurrent_host_threads_on_separate_streams(scb, oracle):
+    import threading
+
+    t, h, d = 2048, 8, 128
+    g = torch.Generator().manual_seed(33)
+    cases = []
+    for i in range(4):
+        kq, ks = oracle.quantize_kv_int8(torch.randn((t, h, d), generator=g))
+        cases.append((kq, ks, 100 * i - 150))
+    results = [None] * len(cases)
+    errors = []
+
+    def work(i):
+        try:
+            kq, ks, dp = cases[i]
+            stream = torch.cuda.Stream(device=DEV)
+            with torch.cuda.stream(stream):
+                kd, sd = kq.to(DEV, non_blocking=False), ks.to(DEV, non_blocking=False)
+                outs = [scb.triton_fused_k_dequant_rope_shift(kd, sd, delta_p=dp + k)
+                        for k in range(8)]
+            stream.synchronize()
+            results[i] = [o.cpu() for o in outs]
+        except Exception as exc:  # pragma: no cover - reported below
+            errors.append(exc)
+
+    threads = [threading.Thread(target=work, args=(i,)) for i in range(len(cases))]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    assert not errors, errors
+    for i, (kq, ks, dp) in enumerate(cases):
+        for k in range(8):
+            c, s = oracle.compute_rope_cos_sin_delta(dp + k, d)
+            torch.testing.assert_close(results[i][k], oracle.dequant_rope_shift(kq, ks, c, s),
+                                       rtol=1e-2, atol=1e-2)

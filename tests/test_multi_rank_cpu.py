@@ -61,7 +61,7 @@ def _worker(rank: int, world: int, port: int, out: dict) -> None:
 
 def test_two_gloo_ranks_shard_heads_without_exchange():
     world = 2
-    with mp.Manager() as mgr:
+    with mp.get_context("spawn").Manager() as mgr:
         out = mgr.dict()
         mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world,
                            start_method="spawn")

@@ -454,7 +454,8 @@ def bench_llama8b(args, scb, dist: Dist, cfg: dict):
     if args.skip_e2e:
         return line
     n_blocks = t // CHUNK
-    with KVRestorePipeline(layers, n_blocks, CHUNK, h, d, device=dev, n_slots=3) as pipe:
+    with KVRestorePipeline(layers, n_blocks, CHUNK, h, d, device=dev, n_slots=3,
+                           write_combined=args.write_combined) as pipe:
         pipe.k_quant.view(layers, t, h, d).copy_(kq.cpu())
         pipe.v_quant.view(layers, t, h, d).copy_(vq.cpu())
         pipe.k_scale.view(layers, t, h, 1).copy_(ks.cpu())
@@ -602,7 +603,8 @@ def bench_llama70b(args, scb, dist: Dist, cfg: dict):
     v_out = torch.empty_like(k_out)
     rows = layers * t * h
     nbytes = restore_bytes(rows, d)
-    with KVRestorePipeline(layers, n_blocks, CHUNK, h, d, device=dev, n_slots=3) as pipe:
+    with KVRestorePipeline(layers, n_blocks, CHUNK, h, d, device=dev, n_slots=3,
+                           write_combined=args.write_combined) as pipe:
         for layer in range(layers):  # this rank's head shard of every layer
             for q, s in ((pipe.k_quant, pipe.k_scale), (pipe.v_quant, pipe.v_scale)):
                 x = torch.randn((t, h, d), generator=gen, device=dev).to(torch.float16)
@@ -668,6 +670,8 @@ def main() -> None:
                          "profiling captures)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling aid: kernel leg only")
     ap.add_argument("--skip-cpu-baseline", action="store_true", help="profiling aid")
+    ap.add_argument("--write-combined", action="store_true",
+                    help="pin the host slabs write-combined (pipeline workloads)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

@@ -212,6 +212,8 @@ SC_API int32_t sc_restore_paged(int32_t n_requests, int32_t max_pages, int32_t p
 typedef struct sc_pipeline sc_pipeline;
 
 #define SC_PIPE_NUMA_LOCAL 0x1u /* allocate the slabs from a thread bound to the GPU's NUMA node */
+#define SC_PIPE_WRITE_COMBINED 0x2u /* pin the slabs write-combined: faster DMA reads on some
+                                       hosts, very slow host reads (write-only use) */
 
 SC_API int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t n_blocks,
                            int32_t chunk_size, int32_t n_heads, int32_t head_dim,

@@ -39,6 +39,7 @@ SC_STATUS_BAD_SEQ_LEN = 0x2
 SC_STATUS_BAD_OUT_OFFSET = 0x4
 
 SC_PIPE_NUMA_LOCAL = 0x1
+SC_PIPE_WRITE_COMBINED = 0x2
 
 DTYPE_CODE = {torch.float16: SC_DTYPE_F16, torch.bfloat16: SC_DTYPE_BF16, torch.float32: SC_DTYPE_F32}
 

@@ -203,16 +203,18 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
     const bool bound = (flags & SC_PIPE_NUMA_LOCAL) && bind_to_device_numa(device, &old);
     cudaError_t e = cudaSuccess;
     void* ptr = nullptr;
-    auto halloc = [&](size_t bytes, void** dst) {
+    const unsigned slab_flags = cudaHostAllocPortable |
+                                ((flags & SC_PIPE_WRITE_COMBINED) ? cudaHostAllocWriteCombined : 0u);
+    auto halloc = [&](size_t bytes, void** dst, unsigned hflags) {
         if (e != cudaSuccess) return;
-        e = cudaHostAlloc(dst, bytes, cudaHostAllocPortable);
+        e = cudaHostAlloc(dst, bytes, hflags);
         if (e == cudaSuccess) memset(*dst, 0, bytes);  // first touch on the bound thread
     };
-    halloc(slab_codes, &ptr), p->h_kq = static_cast<int8_t*>(ptr);
-    halloc(slab_scales * 2, &ptr), p->h_ks = static_cast<uint16_t*>(ptr);
-    halloc(slab_codes, &ptr), p->h_vq = static_cast<int8_t*>(ptr);
-    halloc(slab_scales * 2, &ptr), p->h_vs = static_cast<uint16_t*>(ptr);
-    halloc(meta_bytes(max_restore_blocks), &ptr), p->h_meta = static_cast<Meta*>(ptr);
+    halloc(slab_codes, &ptr, slab_flags), p->h_kq = static_cast<int8_t*>(ptr);
+    halloc(slab_scales * 2, &ptr, slab_flags), p->h_ks = static_cast<uint16_t*>(ptr);
+    halloc(slab_codes, &ptr, slab_flags), p->h_vq = static_cast<int8_t*>(ptr);
+    halloc(slab_scales * 2, &ptr, slab_flags), p->h_vs = static_cast<uint16_t*>(ptr);
+    halloc(meta_bytes(max_restore_blocks), &ptr, cudaHostAllocPortable), p->h_meta = static_cast<Meta*>(ptr);
     if (bound) sched_setaffinity(0, sizeof(cpu_set_t), &old);
     if (e != cudaSuccess) {
         const int32_t rc = set_error(SC_ERR_HOST_ALLOC, "cudaHostAlloc of %zu-byte slabs failed: %s",

@@ -157,14 +157,37 @@ __device__ __forceinline__ float scale_to_float<float>(float s) {
 }
 
 // cos/sin of one relative shift for frequency f, rounded like the reference's tables:
-// angle = fp32(dp * inv_freq) (one fp32 multiply); cos/sin evaluated in double, rounded
-// to fp32, then to fp16.  Returns the fp16 values widened back to fp32.
+// angle = fp32(dp * inv_freq) (one fp32 multiply); cos/sin of the angle rounded to fp16.
+// Returns the fp16 values widened back to fp32.
+//
+// Fast path: sincosf is within 2 ulp of the true value, so when v - 4 ulp and v + 4 ulp
+// round to the same fp16 value, that value is the fp16 rounding of the true cos/sin.
+// Otherwise (the value lies next to an fp16 rounding tie) both are evaluated in double,
+// rounded to fp32 and then to fp16.  Both paths give the same fp16 values as evaluating
+// in double everywhere.
+__device__ __forceinline__ bool fp16_settled(float v, __half& out) {
+    const float margin = fmaxf(fabsf(v) * 4.76837158203125e-07f, 1.0e-30f);  // >= 4 ulp
+    const __half lo = __float2half_rn(v - margin);
+    const __half hi = __float2half_rn(v + margin);
+    out = __float2half_rn(v);
+    return __half_as_ushort(lo) == __half_as_ushort(hi);
+}
+
 __device__ __forceinline__ void rope_cs(float dp, float inv_freq, float& c, float& s) {
     const float angle = __fmul_rn(dp, inv_freq);
-    double sd, cd;
-    sincos(static_cast<double>(angle), &sd, &cd);
-    c = __half2float(__float2half_rn(static_cast<float>(cd)));
-    s = __half2float(__float2half_rn(static_cast<float>(sd)));
+    float sf, cf;
+    sincosf(angle, &sf, &cf);
+    __half ch, sh;
+    const bool ok_c = fp16_settled(cf, ch);
+    const bool ok_s = fp16_settled(sf, sh);
+    if (!(ok_c && ok_s)) {
+        double sd, cd;
+        sincos(static_cast<double>(angle), &sd, &cd);
+        ch = __float2half_rn(static_cast<float>(cd));
+        sh = __float2half_rn(static_cast<float>(sd));
+    }
+    c = __half2float(ch);
+    s = __half2float(sh);
 }
 
 // cos/sin of a 16-frequency slice, read four at a time.

@@ -23,11 +23,16 @@ constexpr int kPThreads = 256;
 #define SC_PAGED_MIN_BLOCKS 4
 #endif
 #ifndef SC_PAGED_ROWS_PER_THREAD
-#define SC_PAGED_ROWS_PER_THREAD 2
+#define SC_PAGED_ROWS_PER_THREAD 1
+#endif
+// Build the block's cos/sin table before issuing the page loads (1) or while they are in
+// flight (0).
+#ifndef SC_PAGED_TABLE_FIRST
+#define SC_PAGED_TABLE_FIRST 1
 #endif
 // Consecutive row groups a block walks (its cos/sin table is built once for all of them).
 #ifndef SC_PAGED_ROUNDS
-#define SC_PAGED_ROUNDS 1
+#define SC_PAGED_ROUNDS 2
 #endif
 
 struct PagedParams {
@@ -135,6 +140,13 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
             return;
         }
     }
+#if SC_PAGED_TABLE_FIRST
+    if (has_k) {
+        const float dp = p.dp[p.dp_per_page ? task : r];
+        for (int f = threadIdx.x; f < half; f += blockDim.x) rope_cs(dp, p.inv_freq[f], s_cos[f], s_sin[f]);
+        __syncthreads();
+    }
+#endif
     const CsShared cs{reinterpret_cast<const float4*>(s_cos + j * 16),
                       reinterpret_cast<const float4*>(s_sin + j * 16)};
     const int64_t pbase = static_cast<int64_t>(page_id) * p.page * p.H * p.D;
@@ -146,7 +158,7 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
 #pragma unroll
     for (int k = 0; k < RT; ++k)
         load_page_row(p, group + k * RB + rl, rows, j, half, pbase, sbase, has_k, has_v, buf[k]);
-    if (round == 0 && has_k) {
+    if (!SC_PAGED_TABLE_FIRST && round == 0 && has_k) {
         // The table is built while the first loads are in flight.
         const float dp = p.dp[p.dp_per_page ? task : r];
         for (int f = threadIdx.x; f < half; f += blockDim.x) rope_cs(dp, p.inv_freq[f], s_cos[f], s_sin[f]);

@@ -382,7 +382,7 @@ METRIC = ("dequant+RoPE-shift GB/s (algorithmic bytes) & % of B200 HBM peak; "
           "T=8192 KV restore ms")
 
 
-def workload_config(workload: str, cfg: dict, world: int) -> dict:
+def workload_config(workload: str, cfg: dict, world: int, gather: bool = False) -> dict:
     if workload == "llama8b":
         return {"workload": "llama3-8b KV restore: 32 layers x (K,V), T=8192, 8 KV heads x 128 "
                             "per GPU, theta=5e5, one delta_p in [1,4096], bf16 per-layer caches",
@@ -405,7 +405,8 @@ def workload_config(workload: str, cfg: dict, world: int) -> dict:
                 "delta_p": cfg["delta_p"], "parallelism": f"replicas x{world} (weak)",
                 "l2": "3.4 GB per step > L2 (no flush needed)"}
     return {"workload": "llama3-70b KV restore from pinned host: 80 layers, T=32768, 8 KV heads "
-                        "x 128 sharded over the GPUs, delta_p 8192, theta=5e5, bf16",
+                        "x 128 sharded over the GPUs, delta_p 8192, theta=5e5, bf16"
+                        + ("; all heads gathered on GPU 0" if gather else ""),
             "layers": cfg["layers"], "seq_len": cfg["tokens"], "kv_heads_total": cfg["heads"],
             "kv_heads_per_gpu": cfg["heads"] // world, "head_dim": cfg["head_dim"],
             "parallelism": f"kv-head shards x{world} (strong)", "l2": "pinned host source"}
@@ -589,7 +590,7 @@ def bench_roundtrip(args, scb, dist: Dist, cfg: dict):
 
 
 def bench_llama70b(args, scb, dist: Dist, cfg: dict):
-    from speccache_b200.cache import KVRestorePipeline
+    from speccache_b200.cache import HeadShardGather, KVRestorePipeline
 
     dev = dist.device
     layers, t, d = cfg["layers"], cfg["tokens"], cfg["head_dim"]
@@ -599,10 +600,18 @@ def bench_llama70b(args, scb, dist: Dist, cfg: dict):
     n_blocks = t // CHUNK
     gen = torch.Generator(device=dev)
     gen.manual_seed(SEED + dist.rank)
-    k_out = torch.empty((layers, t, h, d), dtype=cfg["out"], device=dev)
-    v_out = torch.empty_like(k_out)
     rows = layers * t * h
     nbytes = restore_bytes(rows, d)
+    gather = None
+    k_out = v_out = None
+    if args.gather:
+        # all heads land on GPU 0: its full caches, written by every rank's kernels
+        if dist.rank == 0:
+            k_out = torch.empty((layers, t, cfg["heads"], d), dtype=cfg["out"], device=dev)
+            v_out = torch.empty_like(k_out)
+    else:
+        k_out = torch.empty((layers, t, h, d), dtype=cfg["out"], device=dev)
+        v_out = torch.empty_like(k_out)
     with KVRestorePipeline(layers, n_blocks, CHUNK, h, d, device=dev, n_slots=3,
                            write_combined=args.write_combined) as pipe:
         for layer in range(layers):  # this rank's head shard of every layer
@@ -611,23 +620,35 @@ def bench_llama70b(args, scb, dist: Dist, cfg: dict):
                 qd, sd = scb.quantize_kv_int8(x)
                 q[layer].view(t, h, d).copy_(qd.cpu())
                 s[layer].view(t, h, 1).copy_(sd.cpu())
-        ko = [k_out[i] for i in range(layers)]
-        vo = [v_out[i] for i in range(layers)]
         ids, shifts = list(range(n_blocks)), [cfg["delta_p"]] * n_blocks
+        if args.gather:
+            gather = HeadShardGather(pipe, k_out, v_out, owner=0, rank=dist.rank,
+                                     world_size=dist.world, num_kv_heads=cfg["heads"])
+        else:
+            ko = [k_out[i] for i in range(layers)]
+            vo = [v_out[i] for i in range(layers)]
         tail = torch.empty((2, h, d), dtype=cfg["out"]).pin_memory()
 
         def step():
-            pipe.restore(ids, shifts, ko, vo, theta=cfg["theta"])
-            tail[0].copy_(k_out[layers - 1, t - 1], non_blocking=True)
-            tail[1].copy_(v_out[layers - 1, t - 1], non_blocking=True)
+            if gather is not None:
+                gather.restore(ids, shifts, theta=cfg["theta"])
+            else:
+                pipe.restore(ids, shifts, ko, vo, theta=cfg["theta"])
+            if k_out is not None:
+                tail[0].copy_(k_out[layers - 1, t - 1, :h], non_blocking=True)
+                tail[1].copy_(v_out[layers - 1, t - 1, :h], non_blocking=True)
 
         total_ms, _ = time_steps(step, args.steps, args.warmup, dist, per_step_events=False)
         status = pipe.status()
+        if gather is not None:
+            dist.barrier()  # the owner's buffers stay alive until every writer is done
+            gather.close()
     h2d = h2d_bytes(rows, d)
+    path = ("each rank's kernels store its head shard into GPU 0's caches over NVLink"
+            if args.gather else "sc_pipeline_restore from pinned host slabs (bytes of all ranks)")
     e2e = e2e_line(nbytes, total_ms, args.steps, dist.world, h2d,
-                   tail.numel() * tail.element_size(), layers * args.steps,
-                   "sc_pipeline_restore from pinned host slabs (bytes of all ranks)",
-                   {"device_status": status})
+                   tail.numel() * tail.element_size() if k_out is not None else 0,
+                   layers * args.steps, path, {"device_status": status})
     return {"value": e2e["value"], "ms_per_step": total_ms / args.steps, "scaling": "strong",
             "gpu_launches": layers * args.steps, "e2e": e2e,
             "roofline": {"bound": "pcie-h2d", "achieved": e2e["h2d_gbs"] / dist.world,
@@ -649,7 +670,7 @@ def run_ours(args) -> None:
                 "scaling": part.pop("scaling", "weak"), "vs_baseline": None,
                 "dtype": "int8 in, fp32 math, " + str(cfg["out"]).replace("torch.", "") + " out",
                 "data": "synthetic: seeded, see config",
-                "config": workload_config(args.workload, cfg, dist.world)}
+                "config": workload_config(args.workload, cfg, dist.world, args.gather)}
         line.update(part)
         line["clocks"] = clocks.summary()
         if dist.world == 1 and not args.skip_cpu_baseline:
@@ -672,6 +693,8 @@ def main() -> None:
     ap.add_argument("--skip-cpu-baseline", action="store_true", help="profiling aid")
     ap.add_argument("--write-combined", action="store_true",
                     help="pin the host slabs write-combined (pipeline workloads)")
+    ap.add_argument("--gather", action="store_true",
+                    help="llama70b: restore every rank's head shard into GPU 0's caches (NVLink)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

@@ -265,6 +265,25 @@ SC_API int32_t sc_pipeline_status(sc_pipeline* p, int32_t* status_bits);
 
 SC_API int32_t sc_pipeline_destroy(sc_pipeline* p);
 
+/*
+ * Sharing a device buffer between the processes of one box (CUDA IPC), for the gather of
+ * head shards onto one GPU: the owner exports the buffer, each other rank imports it and
+ * passes the returned pointer (plus its shard's head offset) as the output of its restore,
+ * so its kernel stores the shard into the owner's memory over NVLink.  No counterpart in
+ * the reference (it has no multi-GPU path); this is the optional last row of the restore's
+ * multi-GPU design.  Order the owner's reads after the writers' completion on the host
+ * (writer stream synchronised, then a barrier).
+ *
+ *  sc_ipc_export: handle_out receives SC_IPC_HANDLE_BYTES bytes, offset_out the byte
+ *                 offset of dev_ptr inside its allocation
+ *  sc_ipc_import: maps the allocation on the current device with peer access enabled;
+ *                 base_out is what sc_ipc_close takes, ptr_out = base + offset
+ */
+#define SC_IPC_HANDLE_BYTES 64
+SC_API int32_t sc_ipc_export(const void* dev_ptr, void* handle_out, int64_t* offset_out);
+SC_API int32_t sc_ipc_import(const void* handle, int64_t offset, void** base_out, void** ptr_out);
+SC_API int32_t sc_ipc_close(void* base);
+
 #ifdef __cplusplus
 }
 #endif

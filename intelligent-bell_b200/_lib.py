@@ -41,6 +41,8 @@ SC_STATUS_BAD_OUT_OFFSET = 0x4
 SC_PIPE_NUMA_LOCAL = 0x1
 SC_PIPE_WRITE_COMBINED = 0x2
 
+SC_IPC_HANDLE_BYTES = 64
+
 DTYPE_CODE = {torch.float16: SC_DTYPE_F16, torch.bfloat16: SC_DTYPE_BF16, torch.float32: SC_DTYPE_F32}
 
 # Every symbol the header declares, with its ctypes signature.
@@ -80,6 +82,9 @@ _SIGNATURES = {
     "sc_pipeline_synchronize": (_i32, [_vp, _f64]),
     "sc_pipeline_status": (_i32, [_vp, _vp]),
     "sc_pipeline_destroy": (_i32, [_vp]),
+    "sc_ipc_export": (_i32, [_vp, _vp, _vp]),
+    "sc_ipc_import": (_i32, [_vp, _i64, _vp, _vp]),
+    "sc_ipc_close": (_i32, [_vp]),
 }
 
 _lock = threading.Lock()

@@ -115,12 +115,34 @@ class KVRestorePipeline:
                     f"views on {self.device} sharing one layout")
         numel = min(o.untyped_storage().nbytes() // o.element_size() - o.storage_offset()
                     for o in list(k_out) + list(v_out))
-        kp = (ctypes.c_void_p * self.num_layers)(*[o.data_ptr() for o in k_out])
-        vp = (ctypes.c_void_p * self.num_layers)(*[o.data_ptr() for o in v_out])
+        self._restore(ids, dps32, [o.data_ptr() for o in k_out], [o.data_ptr() for o in v_out],
+                      ref.stride(), numel, ref.dtype, theta)
+
+    def restore_into(self, block_ids, delta_ps, k_ptrs: list[int], v_ptrs: list[int],
+                     out_strides: tuple[int, int, int], out_numel: int,
+                     out_dtype: torch.dtype, *, theta: float = 10000.0) -> None:
+        """:meth:`restore` into raw device addresses (e.g. another GPU's buffer mapped with
+        :class:`~speccache_b200.cache.peer.SharedBuffer`): layer l's token i, head h goes to
+        ``k_ptrs[l] + (i * out_strides[0] + h * out_strides[1] + d) * itemsize``; the kernel
+        refuses to write beyond ``out_numel`` elements from each pointer."""
+        ids = np.ascontiguousarray(np.asarray(block_ids, dtype=np.int32).reshape(-1))
+        dps = np.ascontiguousarray(np.asarray(delta_ps, dtype=np.int64).reshape(-1))
+        if ids.size != dps.size:
+            raise ValueError(f"{ids.size} block ids but {dps.size} shifts")
+        if len(k_ptrs) != self.num_layers or len(v_ptrs) != self.num_layers:
+            raise ValueError(f"need {self.num_layers} K and V pointers")
+        self._restore(ids, dps.astype(np.int32), list(k_ptrs), list(v_ptrs), tuple(out_strides),
+                      int(out_numel), out_dtype, theta)
+
+    def _restore(self, ids, dps32, k_ptrs, v_ptrs, strides, numel, dtype, theta) -> None:
+        if dtype not in (torch.float16, torch.bfloat16):
+            raise TypeError(f"outputs must be float16 or bfloat16, got {dtype}")
+        kp = (ctypes.c_void_p * self.num_layers)(*k_ptrs)
+        vp = (ctypes.c_void_p * self.num_layers)(*v_ptrs)
         rc = self._lib.sc_pipeline_restore(
             self._h, ids.ctypes.data, dps32.ctypes.data, int(ids.size), float(theta),
-            _lib.inv_freq_ptr(self.head_dim, theta), kp, vp, _lib.strides(*ref.stride()), numel,
-            _lib.DTYPE_CODE[ref.dtype], _lib.stream_handle(self.device))
+            _lib.inv_freq_ptr(self.head_dim, theta), kp, vp, _lib.strides(*strides), numel,
+            _lib.DTYPE_CODE[dtype], _lib.stream_handle(self.device))
         _lib.check(rc, "sc_pipeline_restore")
 
     def offload(self, layer: int, block_ids, k: torch.Tensor, v: torch.Tensor) -> None:

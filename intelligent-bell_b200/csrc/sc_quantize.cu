@@ -4,9 +4,9 @@
 //   scale = fp16(max(amax / 127, eps))      IEEE fp32 division by 127
 //   q     = clamp(round_half_even(x / float(scale)), -127, 127)   IEEE fp32 division
 //
-// Vector path: a row is G lanes x 32 bytes (G = head_dim * sizeof(x) / 32, a power of two
-// <= 32, one 256-bit load per lane); the absmax is reduced with G-lane xor shuffles; each
-// lane writes 32/sizeof(x) codes with one store.  Codes come from x * (1/scale) in packed
+// Vector path: a row is G lanes x V x 32 bytes (G = head_dim * sizeof(x) / (32 V), a power of
+// two <= 32, V 256-bit loads per lane); the absmax is reduced with G-lane xor shuffles; each
+// lane writes 32 V / sizeof(x) codes with 32-byte (or smaller) stores.  Codes come from x * (1/scale) in packed
 // fp32x2 arithmetic, exact unless the quotient lies within 2^-14 of a half-integer, where
 // the lane redoes the IEEE division; rounding to an integer is done by adding 1.5 * 2^23
 // (the fp32 add rounds half to even and leaves the integer in the low mantissa byte).
@@ -19,6 +19,29 @@ namespace sc {
 namespace {
 
 constexpr int kQThreads = 256;
+
+#ifndef SC_QUANT_MAX_V
+#define SC_QUANT_MAX_V 2
+#endif
+// Resident blocks per SM the vector kernel is compiled for, per input type (the register
+// cap follows; 0 leaves the register count to the compiler).
+#ifndef SC_QUANT_MB_F16
+#define SC_QUANT_MB_F16 5
+#endif
+#ifndef SC_QUANT_MB_BF16
+#define SC_QUANT_MB_BF16 0
+#endif
+#ifndef SC_QUANT_MB_F32
+#define SC_QUANT_MB_F32 1
+#endif
+template <typename InT>
+struct QuantMinBlocks {
+    static constexpr int value = std::is_same<InT, __half>::value           ? SC_QUANT_MB_F16
+                                 : std::is_same<InT, __nv_bfloat16>::value ? SC_QUANT_MB_BF16
+                                                                           : SC_QUANT_MB_F32;
+};
+static_assert(SC_QUANT_MAX_V == 1 || SC_QUANT_MAX_V == 2 || SC_QUANT_MAX_V == 4,
+              "SC_QUANT_MAX_V is 1, 2 or 4");
 
 struct QuantParams {
     int32_t rows;  // n_tokens * n_heads (< 2^31)
@@ -46,30 +69,6 @@ __device__ __forceinline__ float in_to_float<__nv_bfloat16>(__nv_bfloat16 v) {
 template <>
 __device__ __forceinline__ float in_to_float<float>(float v) {
     return v;
-}
-
-// Unpack one 16-byte vector into E = 16 / sizeof(InT) floats.
-template <typename InT>
-__device__ __forceinline__ void unpack16(const uint4& v, float* f) {
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    if constexpr (std::is_same<InT, float>::value) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) f[k] = __uint_as_float(w[k]);
-    } else if constexpr (std::is_same<InT, __half>::value) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float2 p = __half22float2(bit_cast_u32<__half2>(w[k]));
-            f[2 * k] = p.x;
-            f[2 * k + 1] = p.y;
-        }
-    } else {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            // bf16 -> fp32 is a 16-bit left shift of the bit pattern.
-            f[2 * k] = __uint_as_float(w[k] << 16);
-            f[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
-        }
-    }
 }
 
 __device__ __forceinline__ float quant_scale(float amax, float eps, bool f16_scale) {
@@ -122,18 +121,57 @@ __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint3
 }
 
 // 32-byte non-coherent load (one 256-bit access; the address must be 32-byte aligned).
-__device__ __forceinline__ void ld_stream_v8(const void* p, uint32_t (&w)[8]) {
+__device__ __forceinline__ void ld_stream_v8(const void* p, uint32_t* w) {
     asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                  : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]),
                    "=r"(w[6]), "=r"(w[7])
                  : "l"(p));
 }
 
-// Vector path: each lane owns 32 bytes of a row (E = 32 / sizeof(x) elements); G lanes
-// (a power of two <= 32) cover the row.
-template <typename InT, typename ScaleT>
-__global__ void __launch_bounds__(kQThreads) quant_vec(const __grid_constant__ QuantParams p) {
-    constexpr int E = 32 / sizeof(InT);
+// Largest |x| of the elements packed in w (fp32 words or 16-bit pairs).  For 16-bit types
+// the maximum is taken in the input type, which is exact (widening to fp32 is monotone).
+template <typename InT, int NW>
+__device__ __forceinline__ float lane_absmax(const uint32_t (&w)[NW]) {
+    if constexpr (std::is_same<InT, float>::value) {
+        float m = 0.0f;
+#pragma unroll
+        for (int k = 0; k < NW; ++k) m = fmaxf(m, fabsf(__uint_as_float(w[k])));
+        return m;
+    } else if constexpr (std::is_same<InT, __half>::value) {
+        __half2 m = __habs2(bit_cast_u32<__half2>(w[0]));
+#pragma unroll
+        for (int k = 1; k < NW; ++k) m = __hmax2(m, __habs2(bit_cast_u32<__half2>(w[k])));
+        return fmaxf(__low2float(m), __high2float(m));
+    } else {
+        __nv_bfloat162 m = __habs2(*reinterpret_cast<const __nv_bfloat162*>(&w[0]));
+#pragma unroll
+        for (int k = 1; k < NW; ++k)
+            m = __hmax2(m, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&w[k])));
+        return fmaxf(__low2float(m), __high2float(m));
+    }
+}
+
+// Elements k and k+1 (k even) of the packed words as floats.
+template <typename InT>
+__device__ __forceinline__ float2 pair_at(const uint32_t* w, int k) {
+    if constexpr (std::is_same<InT, float>::value) {
+        return make_float2(__uint_as_float(w[k]), __uint_as_float(w[k + 1]));
+    } else if constexpr (std::is_same<InT, __half>::value) {
+        return __half22float2(bit_cast_u32<__half2>(w[k / 2]));
+    } else {
+        // bf16 -> fp32 is a 16-bit left shift of the bit pattern.
+        const uint32_t u = w[k / 2];
+        return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+    }
+}
+
+// Vector path: each lane owns V x 32 bytes of a row (E = 32 V / sizeof(x) elements, V
+// 256-bit loads in flight per lane); G lanes (a power of two <= 32) cover the row.  Larger
+// V shares the per-row work (scale, reciprocal, shuffles, addressing) among more elements.
+template <typename InT, typename ScaleT, int V>
+__global__ void __launch_bounds__(kQThreads, QuantMinBlocks<InT>::value) quant_vec(const __grid_constant__ QuantParams p) {
+    constexpr int NW = 8 * V;
+    constexpr int E = 32 * V / static_cast<int>(sizeof(InT));
     const int G = p.G;
     const int lane = threadIdx.x % G;
     const int RB = blockDim.x / G;
@@ -142,20 +180,18 @@ __global__ void __launch_bounds__(kQThreads) quant_vec(const __grid_constant__ Q
          base += static_cast<int64_t>(gridDim.x) * RB) {
         const int64_t row = base + threadIdx.x / G;
         const bool active = row < p.rows;
-        float f[E];
+        uint32_t w[NW];
         int64_t t = 0, h = 0;
         float m = 0.0f;
         if (active) {
             const uint32_t ti = fdiv(static_cast<uint32_t>(row), p.divH);
             t = ti;
             h = static_cast<int64_t>(static_cast<uint32_t>(row) - ti * static_cast<uint32_t>(p.H));
-            const InT* xp = reinterpret_cast<const InT*>(p.x) + t * p.x_t + h * p.x_h + lane * E;
-            uint32_t w[8];
-            ld_stream_v8(xp, w);
-            unpack16<InT>(make_uint4(w[0], w[1], w[2], w[3]), f);
-            unpack16<InT>(make_uint4(w[4], w[5], w[6], w[7]), f + E / 2);
+            const char* xp = reinterpret_cast<const char*>(
+                reinterpret_cast<const InT*>(p.x) + t * p.x_t + h * p.x_h + lane * E);
 #pragma unroll
-            for (int k = 0; k < E; ++k) m = fmaxf(m, fabsf(f[k]));
+            for (int v = 0; v < V; ++v) ld_stream_v8(xp + 32 * v, w + 8 * v);
+            m = lane_absmax<InT>(w);
         }
         for (int o = G >> 1; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if (!active) continue;
@@ -163,23 +199,37 @@ __global__ void __launch_bounds__(kQThreads) quant_vec(const __grid_constant__ Q
         const float rcp = __frcp_rn(sc);
         const float2 rcp2 = make_float2(rcp, rcp);
         bool tie = !(sc > 0.0f && sc < 3.0e38f);  // non-finite or zero scale: exact path
-        uint32_t tw[E];
-#pragma unroll
-        for (int k = 0; k < E; k += 2)
-            fast_codes2(make_float2(f[k], f[k + 1]), rcp2, tw[k], tw[k + 1], tie);
-        if (tie) {
-#pragma unroll
-            for (int k = 0; k < E; ++k) tw[k] = code_byte(f[k], sc);
-        }
+        // Codes are packed four to a word as they are made, so only the packed words stay live.
         uint32_t packed[E / 4];
 #pragma unroll
-        for (int k = 0; k < E / 4; ++k)
-            packed[k] = pack_low_bytes(tw[4 * k], tw[4 * k + 1], tw[4 * k + 2], tw[4 * k + 3]);
+        for (int k = 0; k < E; k += 4) {
+            uint32_t c0, c1, c2, c3;
+            fast_codes2(pair_at<InT>(w, k), rcp2, c0, c1, tie);
+            fast_codes2(pair_at<InT>(w, k + 2), rcp2, c2, c3, tie);
+            packed[k / 4] = pack_low_bytes(c0, c1, c2, c3);
+        }
+        if (tie) {  // rare: reload the lane's input (keeps the fast path's registers free)
+            const char* xp = reinterpret_cast<const char*>(
+                reinterpret_cast<const InT*>(p.x) + t * p.x_t + h * p.x_h + lane * E);
+#pragma unroll
+            for (int v = 0; v < V; ++v) ld_stream_v8(xp + 32 * v, w + 8 * v);
+#pragma unroll
+            for (int k = 0; k < E; k += 4) {
+                const float2 x0 = pair_at<InT>(w, k), x1 = pair_at<InT>(w, k + 2);
+                packed[k / 4] = pack_low_bytes(code_byte(x0.x, sc), code_byte(x0.y, sc),
+                                               code_byte(x1.x, sc), code_byte(x1.y, sc));
+            }
+        }
         int8_t* qp = p.q + t * p.q_t + h * p.q_h + lane * E;
-        if constexpr (E == 16)
+        if constexpr (E >= 32) {
+#pragma unroll
+            for (int c = 0; c < E / 32; ++c)
+                st_v8(qp + 32 * c, *reinterpret_cast<const uint32_t(*)[8]>(packed + 8 * c));
+        } else if constexpr (E == 16) {
             st_v4(qp, make_uint4(packed[0], packed[1], packed[2], packed[3]));
-        else
+        } else {
             st_v2(qp, make_uint2(packed[0], packed[1]));
+        }
         if (lane == 0) {
             ScaleT* sp = reinterpret_cast<ScaleT*>(p.s) + t * p.s_t + h * p.s_h;
             if constexpr (kF16Scale)
@@ -225,26 +275,29 @@ int resident_blocks(K kernel) {
 }
 
 // Grids are sized to exactly the resident blocks (no partial wave) or to the work.
-template <typename InT, typename ScaleT>
-cudaError_t launch_quant(const QuantParams& p, bool vec, cudaStream_t stream) {
-    if (vec) {
-        auto kern = quant_vec<InT, ScaleT>;
-        const int rb = kQThreads / p.G;
-        const int64_t need = (static_cast<int64_t>(p.rows) + rb - 1) / rb;
-        const int64_t cap = static_cast<int64_t>(sm_count()) * resident_blocks(kern);
-        kern<<<static_cast<int>(need < cap ? need : cap), kQThreads, 0, stream>>>(p);
-    } else {
-        auto kern = quant_generic<InT, ScaleT>;
-        const int64_t need = (static_cast<int64_t>(p.rows) + 7) / 8;
-        const int64_t cap = static_cast<int64_t>(sm_count()) * resident_blocks(kern);
-        kern<<<static_cast<int>(need < cap ? need : cap), kQThreads, 0, stream>>>(p);
-    }
+template <typename K>
+cudaError_t launch_persistent(K kern, const QuantParams& p, int rows_per_block, cudaStream_t stream) {
+    const int64_t need = (static_cast<int64_t>(p.rows) + rows_per_block - 1) / rows_per_block;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * resident_blocks(kern);
+    kern<<<static_cast<int>(need < cap ? need : cap), kQThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
+// v = 0: generic path; v = 1, 2, 4: vector path with v 32-byte vectors per lane.
+template <typename InT, typename ScaleT>
+cudaError_t launch_quant(const QuantParams& p, int v, cudaStream_t stream) {
+    const int rb = kQThreads / p.G;
+    switch (v) {
+        case 1: return launch_persistent(quant_vec<InT, ScaleT, 1>, p, rb, stream);
+        case 2: return launch_persistent(quant_vec<InT, ScaleT, 2>, p, rb, stream);
+        case 4: return launch_persistent(quant_vec<InT, ScaleT, 4>, p, rb, stream);
+        default: return launch_persistent(quant_generic<InT, ScaleT>, p, kQThreads / 32, stream);
+    }
+}
+
 template <typename InT>
-cudaError_t launch_quant_s(const QuantParams& p, bool vec, bool f16_scale, cudaStream_t s) {
-    return f16_scale ? launch_quant<InT, __half>(p, vec, s) : launch_quant<InT, float>(p, vec, s);
+cudaError_t launch_quant_s(const QuantParams& p, int v, bool f16_scale, cudaStream_t s) {
+    return f16_scale ? launch_quant<InT, __half>(p, v, s) : launch_quant<InT, float>(p, v, s);
 }
 
 }  // namespace
@@ -290,29 +343,36 @@ extern "C" int32_t sc_quantize_int8(int64_t n_tokens, int32_t n_heads, int32_t h
     p.s_t = s_strides[0], p.s_h = s_strides[1];
     p.eps = eps;
 
-    // Vector path: 32 bytes of input per lane (one 256-bit load), G = row_bytes / 32 lanes
-    // per row (a power of two <= 32), 32-byte aligned input rows, E-byte aligned code rows.
+    // Vector path: V x 32 bytes of input per lane (V 256-bit loads), G = row_bytes / (32 V)
+    // lanes per row (a power of two <= 32), 32-byte aligned input rows, code rows aligned to
+    // the lane's store (E = 32 V / sizeof(x) bytes, at most 32).  The largest V that fits
+    // (up to SC_QUANT_MAX_V) is taken.
     const int es = x_dtype == SC_DTYPE_F32 ? 4 : 2;
-    const int E = 32 / es;
     const int64_t row_bytes = static_cast<int64_t>(head_dim) * es;
-    int G = static_cast<int>(row_bytes / 32);
-    bool vec = !(flags & SC_FLAG_FORCE_GENERIC) && row_bytes % 32 == 0 && G >= 1 && G <= 32 &&
-               (G & (G - 1)) == 0;
     auto al = [](const void* ptr, int a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; };
     auto st_ok = [](int64_t st, int64_t size, int64_t a) { return size <= 1 || st % a == 0; };
-    if (vec) {
-        vec = p.x_d == 1 && al(x, 32) && st_ok(p.x_t * es, n_tokens, 32) &&
-              st_ok(p.x_h * es, n_heads, 32) && p.q_d == 1 && al(q_out, E) &&
-              st_ok(p.q_t, n_tokens, E) && st_ok(p.q_h, n_heads, E);
+    const bool in_ok = p.x_d == 1 && al(x, 32) && st_ok(p.x_t * es, n_tokens, 32) &&
+                       st_ok(p.x_h * es, n_heads, 32) && p.q_d == 1;
+    int v = 0;
+    for (int cand = SC_QUANT_MAX_V; cand >= 1 && v == 0 && in_ok && !(flags & SC_FLAG_FORCE_GENERIC);
+         cand /= 2) {
+        const int64_t lane_bytes = 32 * cand;
+        const int64_t g = row_bytes / lane_bytes;
+        const int qa = static_cast<int>(lane_bytes / es < 32 ? lane_bytes / es : 32);
+        if (row_bytes % lane_bytes == 0 && g >= 1 && g <= 32 && (g & (g - 1)) == 0 &&
+            al(q_out, qa) && st_ok(p.q_t, n_tokens, qa) && st_ok(p.q_h, n_heads, qa)) {
+            v = cand;
+            p.G = static_cast<int>(g);
+        }
     }
-    p.G = vec ? G : 32;
+    if (v == 0) p.G = 32;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const bool f16s = scale_dtype == SC_DTYPE_F16;
     cudaError_t e;
     switch (x_dtype) {
-        case SC_DTYPE_F16: e = launch_quant_s<__half>(p, vec, f16s, s); break;
-        case SC_DTYPE_BF16: e = launch_quant_s<__nv_bfloat16>(p, vec, f16s, s); break;
-        default: e = launch_quant_s<float>(p, vec, f16s, s); break;
+        case SC_DTYPE_F16: e = launch_quant_s<__half>(p, v, f16s, s); break;
+        case SC_DTYPE_BF16: e = launch_quant_s<__nv_bfloat16>(p, v, f16s, s); break;
+        default: e = launch_quant_s<float>(p, v, f16s, s); break;
     }
     if (e != cudaSuccess) return cuda_error(e, "quantize launch");
     return ok();

@@ -16,6 +16,7 @@ from __future__ import annotations
 import torch
 
 from .. import _lib
+from .staging import host_array, to_device
 from .validation import require_cuda
 
 _STATUS: dict[int, torch.Tensor] = {}
@@ -43,13 +44,6 @@ def paged_status(device: torch.device | str | int | None = None, reset: bool = T
     if reset:
         w.zero_()
     return v
-
-
-def _as_device(x, device, dtype) -> torch.Tensor:
-    t = torch.as_tensor(x)
-    if t.device != device or t.dtype != dtype or not t.is_contiguous():
-        t = t.to(device=device, dtype=dtype).contiguous()
-    return t
 
 
 def restore_paged(
@@ -102,7 +96,7 @@ def restore_paged(
             raise ValueError("pool scales must be contiguous float16 [n_pages, page, H(, 1)]")
         if not q.is_contiguous():
             raise ValueError("pools must be contiguous")
-    table = _as_device(page_table, dev, torch.int32)
+    table = host_array(page_table, torch.int32)
     if table.ndim != 2:
         raise ValueError(f"page_table must be [R, max_pages], got {tuple(table.shape)}")
     n_req, max_pages = table.shape
@@ -115,8 +109,8 @@ def restore_paged(
             raise ValueError(f"seq_lens has {lens_host.numel()} entries for {n_req} requests")
         if (lens_host < 0).any() or (lens_host > max_pages * page).any():
             raise ValueError(f"seq_lens must lie in [0, {max_pages * page}]")
-    lens = _as_device(seq_lens, dev, torch.int32)
-    dps = _as_device(delta_ps, dev, torch.float32)
+    lens = host_array(seq_lens if lens_dev else lens_host, torch.int32)
+    dps = host_array(delta_ps, torch.float32)
     expect = n_req * max_pages if delta_p_per_page else n_req
     if dps.numel() != expect:
         raise ValueError(f"delta_ps has {dps.numel()} entries, expected {expect}")
@@ -143,11 +137,12 @@ def restore_paged(
     if out_offsets is None:
         if lens_host is None:
             raise ValueError("out_offsets are required when seq_lens live on the device")
-        offs = _as_device(cu[:-1] * out.stride(0), dev, torch.int64)
+        offs = cu[:-1] * out.stride(0)
     else:
-        offs = _as_device(out_offsets, dev, torch.int64)
+        offs = host_array(out_offsets, torch.int64)
     if lens_host is not None and total == 0:
         return k_out, v_out, cu
+    table, lens, dps, offs = to_device([table, lens, dps, offs], dev)
     status = _status_word(dev)
     flags = _lib.SC_FLAG_FP32_INTERMEDIATE if fp32_intermediate else 0
     # The kernel bounds every write by the extent of the output's storage from its data_ptr.

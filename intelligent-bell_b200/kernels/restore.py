@@ -20,6 +20,7 @@ from __future__ import annotations
 import torch
 
 from .. import _lib
+from .staging import host_array, to_device
 from .validation import (
     OUT_DTYPES,
     require_cuda,
@@ -53,7 +54,7 @@ def compute_rope_cos_sin_delta(
             f"SpecCache B200 kernels require an NVIDIA CUDA device, got device: {dev}.")
     if dev.index is None:
         dev = torch.device("cuda", torch.cuda.current_device())
-    dp = dp.reshape(-1).to(device=dev, dtype=torch.float32)
+    (dp,) = to_device([host_array(dp.reshape(-1), torch.float32)], dev)
     n = dp.numel()
     half = head_dim // 2
     cos = torch.empty((n, half), dtype=dtype, device=dev)

@@ -5,7 +5,8 @@
   output layout (contiguous or model layout [H, T, D] viewed as [T, H, D]);
 * dense restore with the shift expanded in the kernel: within the reference tolerance;
 * quantize: bit-exact codes and scales for random shapes, dtypes, magnitudes and layouts;
-* paged restore: V bit-exact and K within tolerance for random ragged batches.
+* paged restore: V bit-exact and K within tolerance for random ragged batches, and the same
+  bits whether the page table, lengths and shifts come as host lists or device tensors.
 """
 
 from __future__ import annotations
@@ -112,6 +113,15 @@ def test_paged_matches_oracle(scb, oracle, n_req, page, h, d, max_len, out_dtype
                                    dps, out_dtype=out_dtype)
     torch.cuda.synchronize()
     assert scb.paged_status(DEV) == 0
+    # the same call with every argument already on the device gives the same bits
+    kd, vd = torch.empty_like(kk), torch.empty_like(vv)
+    offs = (cu[:-1] * kk.stride(0)).to(DEV)
+    scb.restore_paged(pkq.to(DEV), pks.to(DEV), pvq.to(DEV), pvs.to(DEV), table.to(DEV),
+                      torch.tensor(lens, dtype=torch.int32, device=DEV),
+                      torch.tensor(dps, dtype=torch.float32, device=DEV), out_dtype=out_dtype,
+                      k_out=kd, v_out=vd, out_offsets=offs)
+    torch.cuda.synchronize()
+    assert bits_equal(kd.cpu(), kk.cpu()) and bits_equal(vd.cpu(), vv.cpu())
     ref = oracle.restore_paged(pkq, pks, pvq, pvs, table, lens, dps, out_dtype=out_dtype)
     for r, (kr, vr) in enumerate(ref):
         torch.testing.assert_close(kk[cu[r]:cu[r + 1]].cpu().float(), kr.float(), rtol=1e-2, atol=1e-2)

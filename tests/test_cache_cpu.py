@@ -133,3 +133,28 @@ def test_dynamic_cache_append_views_are_model_layout(scb):
     cache.commit(0, 12)
     assert torch.equal(cache[0][0], src.permute(1, 0, 2).unsqueeze(0))
     assert torch.equal(cache[0][1], (src * 2).permute(1, 0, 2).unsqueeze(0))
+
+
+def test_routing_decisions_select_reusable_blocks(scb, oracle):
+    # reference speccache/cache/engine.py:449-460: only exact/semantic reuse with a block id
+    from speccache_b200.cache import (ChunkRoutingDecision, ChunkRoutingStatus, PinnedKVPool,
+                                      RestoreEngine, reusable)
+
+    chunk, h, d = 16, 2, 32
+    pool = PinnedKVPool(4, chunk, h, d, None, *_slabs(4, chunk, h, d))
+    engine = RestoreEngine(pool=pool)
+    assert (engine.chunk_size, engine.num_kv_heads, engine.head_dim) == (chunk, h, d)
+    with pytest.raises(ValueError, match="must equal chunk_size"):
+        engine.register_chunk(range(chunk - 1), 0, *_chunk(oracle, chunk, h, d, 1))
+    ids = [engine.register_chunk(range(i * chunk, (i + 1) * chunk), 64 * i,
+                                 *_chunk(oracle, chunk, h, d, 10 + i)) for i in range(3)]
+    assert [pool.get_start_pos(b) for b in ids] == [0, 64, 128]
+    assert pool._active_lru[ids[1]].token_ids == tuple(range(chunk, 2 * chunk))
+    S = ChunkRoutingStatus
+    ds = [ChunkRoutingDecision(i, 0, chunk, (), st, block_id=b, delta_p=5 * i)
+          for i, (st, b) in enumerate([(S.EXACT_REUSE, ids[0]), (S.CACHE_MISS, ids[1]),
+                                       (S.SEMANTIC_REUSE, ids[2]), (S.SPECULATIVE_DRAFT, ids[0]),
+                                       (S.EXACT_REUSE, None)])]
+    assert [d.chunk_index for d in reusable(ds)] == [0, 2]
+    assert ChunkRoutingDecision(0, 0, 1, (), S.CACHE_MISS).continuation_tokens == []
+    assert S("SEMANTIC_REUSE") is S.SEMANTIC_REUSE and S.EXACT_REUSE == "EXACT_REUSE"

@@ -2,7 +2,8 @@
 reference's own injector outputs (golden vectors).
 
 Mirrors tests/test_phase3_serving.py:137-235 (multi-layer shifted injection) and
-tests/test_phase2_engine.py:297-359 (multi-chunk pipeline parity) of the reference.
+tests/test_phase2_engine.py:297-359 (multi-chunk pipeline parity, through the pool and through
+routing decisions) of the reference.
 K is compared with the reference tolerance (the kernels build cos/sin from delta_p, one
 fp16 ulp apart from torch's tables in rare entries), V bit for bit.
 """
@@ -163,6 +164,54 @@ def test_pool_async_dma_multi_chunk_parity(scb, oracle):
     torch.testing.assert_close(k.cpu(), kr, rtol=1e-2, atol=1e-2)
     assert bits_equal(v.cpu(), vr)
     pool.close()
+
+
+def test_engine_routing_decisions_multi_chunk_parity(scb, oracle):
+    # reference tests/test_phase2_engine.py:297-359 through the decision records of
+    # speccache/cache/engine.py:54-67: chunk c cached at c*128, wanted at c*256; decisions
+    # that are not reuse (or have no block) are skipped, empty input gives [0, H, D] fp16
+    from speccache_b200.cache import ChunkRoutingDecision, ChunkRoutingStatus, RestoreEngine
+
+    chunk, h, d, n = 64, 4, 64, 4
+    S = ChunkRoutingStatus
+    with RestoreEngine(chunk_size=chunk, num_kv_heads=h, head_dim=d, max_blocks=16,
+                       device=DEV) as engine:
+        g = torch.Generator().manual_seed(200)
+        data = []
+        for c in range(n):
+            kq, ks = oracle.quantize_kv_int8(torch.randn((chunk, h, d), generator=g))
+            vq, vs = oracle.quantize_kv_int8(torch.randn((chunk, h, d), generator=g))
+            toks = list(range(c * 500, c * 500 + chunk))
+            bid = engine.register_chunk(toks, c * 128, kq, ks, vq, vs)
+            data.append((bid, kq, ks, vq, vs, c * 256 - c * 128))
+        decisions = []
+        for c, (bid, *_, dp) in enumerate(data):
+            st = S.EXACT_REUSE if c % 2 == 0 else S.SEMANTIC_REUSE
+            decisions.append(ChunkRoutingDecision(c, c * 256, c * 256 + chunk, (), st,
+                                                  block_id=bid, cached_position=c * 128,
+                                                  delta_p=dp))
+            decisions.append(ChunkRoutingDecision(c, 0, chunk, (), S.CACHE_MISS))
+        decisions.insert(3, ChunkRoutingDecision(9, 0, chunk, (), S.SPECULATIVE_DRAFT,
+                                                 block_id=data[0][0], delta_p=7))
+        k_out, v_out = engine.execute_async_dma_and_rope(decisions)
+        assert k_out.shape == (n * chunk, h, d) and k_out.dtype == torch.float16
+        for i, (bid, kq, ks, vq, vs, dp) in enumerate(data):
+            cos, sin = oracle.compute_rope_cos_sin_delta(dp, d)
+            k_ref = oracle.dequant_rope_shift(kq, ks, cos, sin)
+            sl = slice(i * chunk, (i + 1) * chunk)
+            torch.testing.assert_close(k_out[sl].cpu(), k_ref, rtol=1e-2, atol=1e-2)
+            assert bits_equal(v_out[sl].cpu(), oracle.dequant_value(vq, vs))
+        # caller-given bf16 destinations are written in place
+        kd = torch.empty((n * chunk, h, d), dtype=torch.bfloat16, device=DEV)
+        vd = torch.empty_like(kd)
+        k2, v2 = engine.execute_async_dma_and_rope(decisions, kd, vd)
+        assert k2.data_ptr() == kd.data_ptr() and v2.data_ptr() == vd.data_ptr()
+        for i, (bid, kq, ks, vq, vs, dp) in enumerate(data):
+            sl = slice(i * chunk, (i + 1) * chunk)
+            assert bits_equal(v2[sl].cpu(), oracle.dequant_value(vq, vs, torch.bfloat16))
+        misses = [x for x in decisions if x.status in (S.CACHE_MISS, S.SPECULATIVE_DRAFT)]
+        e_k, e_v = engine.execute_async_dma_and_rope(misses)
+        assert e_k.shape == (0, h, d) and e_v.dtype == torch.float16 and e_k.device == DEV
 
 
 def test_reconstruct_layer_chunk(scb, oracle):

@@ -2,13 +2,14 @@
 // shift, written straight into contiguous per-request caches.
 //
 // Work unit: one block per (request, page, chunk of the page's rows) - one-shot blocks,
-// no persistent loop (on B200 one-shot tiles stream 9-10 % faster).  A block whose page
-// lies past its request's length exits at once.  Each thread first issues the loads of its
-// SC_PAGED_ROWS_PER_THREAD 16-frequency slices of the page's rows (two 16-byte loads per
-// tensor, rotate-half partner in the same thread); while they are in flight the block
-// builds the cos/sin table of the request's (or page's) shift in shared memory (double
-// cos/sin rounded like the reference's fp16 tables); then it converts and stores (one
-// 32-byte store per 16 outputs).
+// no persistent loop (on B200 one-shot tiles stream 9-10 % faster).  A block first reads
+// its request's length and exits at once if its page lies past it; otherwise it reads the
+// page id, output offset and shift together (one memory latency for the three), builds
+// the cos/sin table of the request's (or page's) shift in shared memory (single-precision
+// sincos, double precision only where the fp16 rounding is not settled, rounded like the
+// reference's fp16 tables), then walks SC_PAGED_ROUNDS groups of rows: each thread loads
+// its 16-frequency slice of a row (two 16-byte loads per tensor, rotate-half partner in
+// the same thread), converts it and stores it (one 32-byte store per 16 outputs).
 //
 // Device-side checks never fault: a page id outside the pool, a bad sequence length or an
 // output range outside out_numel makes the block skip the work and OR a status bit into
@@ -34,6 +35,30 @@ constexpr int kPThreads = 256;
 #ifndef SC_PAGED_ROUNDS
 #define SC_PAGED_ROUNDS 2
 #endif
+// The block's metadata loads: each where it is first needed (0); all four (length, page
+// id, output offset, shift) together at the start (1); the length alone, then - once the
+// block knows it has work - the other three together (2).
+#ifndef SC_PAGED_HOIST_META
+#define SC_PAGED_HOIST_META 2
+#endif
+
+// Read-only scalar loads kept in program order (volatile), so that metadata loads issued
+// together are not sunk past the early-exit branches that follow them.
+__device__ __forceinline__ int32_t ld_meta(const int32_t* ptr) {
+    int32_t v;
+    asm volatile("ld.global.nc.b32 %0, [%1];" : "=r"(v) : "l"(ptr));
+    return v;
+}
+__device__ __forceinline__ int64_t ld_meta(const int64_t* ptr) {
+    int64_t v;
+    asm volatile("ld.global.nc.b64 %0, [%1];" : "=l"(v) : "l"(ptr));
+    return v;
+}
+__device__ __forceinline__ float ld_meta(const float* ptr) {
+    float v;
+    asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(ptr));
+    return v;
+}
 
 struct PagedParams {
     int32_t R, max_pages, page, H, D, P;
@@ -113,7 +138,15 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
     const int r = static_cast<int>(task / p.max_pages);
     const int pg = static_cast<int>(task - static_cast<int64_t>(r) * p.max_pages);
     const bool reporter = chunk == 0 && threadIdx.x == 0;
+#if SC_PAGED_HOIST_META == 1
+    // All four addresses are in bounds by construction (r < R, pg < max_pages <= stride).
+    const int len = ld_meta(p.seq_lens + r);
+    const int32_t page_id = ld_meta(p.table + static_cast<int64_t>(r) * p.table_stride + pg);
+    const int64_t off = ld_meta(p.out_off + r);
+    const float dp_blk = has_k ? ld_meta(p.dp + (p.dp_per_page ? task : r)) : 0.0f;
+#else
     const int len = p.seq_lens[r];
+#endif
     if (len < 0 || static_cast<int64_t>(len) > static_cast<int64_t>(p.max_pages) * p.page) {
         if (reporter && pg == 0) atomicOr(p.status, SC_STATUS_BAD_SEQ_LEN);
         return;
@@ -124,12 +157,20 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
     const int64_t rows = static_cast<int64_t>(n_tok) * p.H;
     const int64_t row_begin = static_cast<int64_t>(chunk) * RB * RT * SC_PAGED_ROUNDS;
     if (row_begin >= rows) return;
+#if SC_PAGED_HOIST_META == 2
+    const int32_t page_id = ld_meta(p.table + static_cast<int64_t>(r) * p.table_stride + pg);
+    const int64_t off = ld_meta(p.out_off + r);
+    const float dp_blk = has_k ? ld_meta(p.dp + (p.dp_per_page ? task : r)) : 0.0f;
+#elif SC_PAGED_HOIST_META == 0
     const int32_t page_id = p.table[static_cast<int64_t>(r) * p.table_stride + pg];
+#endif
     if (page_id < 0 || page_id >= p.n_pool_pages) {
         if (reporter) atomicOr(p.status, SC_STATUS_BAD_PAGE_ID);
         return;
     }
+#if SC_PAGED_HOIST_META == 0
     const int64_t off = p.out_off[r];
+#endif
     {
         // Output range of this page: rows tok0 .. tok0+n_tok-1, heads 0 .. H-1.
         const int64_t first = off + static_cast<int64_t>(tok0) * p.o_t;
@@ -140,9 +181,14 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
             return;
         }
     }
+#if SC_PAGED_HOIST_META
+    auto block_dp = [&] { return dp_blk; };
+#else
+    auto block_dp = [&] { return p.dp[p.dp_per_page ? task : r]; };
+#endif
 #if SC_PAGED_TABLE_FIRST
     if (has_k) {
-        const float dp = p.dp[p.dp_per_page ? task : r];
+        const float dp = block_dp();
         for (int f = threadIdx.x; f < half; f += blockDim.x) rope_cs(dp, p.inv_freq[f], s_cos[f], s_sin[f]);
         __syncthreads();
     }
@@ -160,7 +206,7 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
         load_page_row(p, group + k * RB + rl, rows, j, half, pbase, sbase, has_k, has_v, buf[k]);
     if (!SC_PAGED_TABLE_FIRST && round == 0 && has_k) {
         // The table is built while the first loads are in flight.
-        const float dp = p.dp[p.dp_per_page ? task : r];
+        const float dp = block_dp();
         for (int f = threadIdx.x; f < half; f += blockDim.x) rope_cs(dp, p.inv_freq[f], s_cos[f], s_sin[f]);
         __syncthreads();
     }

@@ -63,7 +63,8 @@ bool bind_to_device_numa(int device, cpu_set_t* old) {
     cpu_set_t set;
     CPU_ZERO(&set);
     int count = 0;
-    for (char* tok = strtok(list, ",\n"); tok; tok = strtok(nullptr, ",\n")) {
+    char* save = nullptr;  // strtok_r: pipelines may be created from several threads at once
+    for (char* tok = strtok_r(list, ",\n", &save); tok; tok = strtok_r(nullptr, ",\n", &save)) {
         int a = 0, b = 0;
         if (sscanf(tok, "%d-%d", &a, &b) == 2) {
             for (int c = a; c <= b && c < CPU_SETSIZE; ++c) CPU_SET(c, &set), ++count;

@@ -204,10 +204,12 @@ SC_API int32_t sc_restore_paged(int32_t n_requests, int32_t max_pages, int32_t p
  * Host slabs (pinned, owned by the pipeline), per layer l and block b:
  *    k_quant/v_quant  int8 [n_layers, n_blocks, chunk_size, n_heads, head_dim]
  *    k_scale/v_scale  fp16 [n_layers, n_blocks, chunk_size, n_heads]
- * A restore copies, for each layer, the requested blocks (one cudaMemcpyAsync per run of
- * consecutive block ids and tensor) on the pipeline's transfer stream into one of n_slots
- * device staging slots, and runs the restore kernel for that layer on compute_stream once
- * its copy event has fired, so layer l+1's copy overlaps layer l's kernel.
+ * The v_quant slab directly follows the k_quant slab in one allocation, and v_scale follows
+ * k_scale.  A restore copies on the pipeline's transfer stream, per run of consecutive block
+ * ids, the scales of every layer (one 2-D copy), then for each layer the K and V codes (one
+ * 2-D copy of two rows) into one of n_slots device staging slots, and runs the restore kernel
+ * for that layer on compute_stream once its copy event has fired, so layer l+1's copy
+ * overlaps layer l's kernel.
  */
 typedef struct sc_pipeline sc_pipeline;
 

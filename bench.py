@@ -586,7 +586,32 @@ def bench_roundtrip(args, scb, dist: Dist, cfg: dict):
     line["e2e"] = e2e_line(nbytes, e2e_ms, args.steps, dist.world,
                            2 * hk.numel() * hk.element_size(), tail.numel() * tail.element_size(),
                            3 * args.steps, "fp16 K/V H2D from pinned host, quantize, restore")
+    line["offload"] = offload_line(args, dist, xk.view(layers, t, h, d), xv.view(layers, t, h, d))
     return line
+
+
+def offload_line(args, dist: Dist, xk: torch.Tensor, xv: torch.Tensor) -> dict:
+    """The cold-miss direction: every layer's fp16 K/V quantized on the GPU and copied into
+    the pinned host slabs (sc_pipeline_offload), timed on the current stream through
+    sc_pipeline_join (no host wait inside the step)."""
+    from speccache_b200.cache import KVRestorePipeline
+
+    layers, t, h, d = xk.shape
+    ids = list(range(t // CHUNK))
+    with KVRestorePipeline(layers, len(ids), CHUNK, h, d, device=dist.device) as pipe:
+        def step():
+            for layer in range(layers):
+                pipe.offload(layer, ids, xk[layer], xv[layer])
+            pipe.join()
+
+        ms, _ = time_steps(step, args.steps, args.warmup, dist, per_step_events=False)
+    rows = layers * t * h
+    d2h = 2 * rows * (d + 2)  # int8 codes and fp16 scales of K and V
+    return {"ms_per_step": ms / args.steps,
+            "d2h_gbs": d2h * dist.world * args.steps / (ms / 1e3) / 1e9,
+            "quantize_gbs": quantize_bytes(rows, d) * dist.world * args.steps / (ms / 1e3) / 1e9,
+            "d2h_bytes_per_step": d2h, "gpu_launches": 2 * layers * args.steps,
+            "path": "quantize on the GPU into a staging slot, 2-D D2H copies into the pinned slabs"}
 
 
 def bench_llama70b(args, scb, dist: Dist, cfg: dict):

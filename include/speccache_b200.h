@@ -242,9 +242,10 @@ SC_API int32_t sc_pipeline_restore(sc_pipeline* p, const int32_t* block_ids, con
 
 /*
  * Enqueue the offload of n_blocks freshly computed K/V blocks of one layer into the slabs:
- * quantize on the GPU (sc_quantize_int8 arithmetic, bit-exact with the reference) into a
- * device staging buffer on compute_stream, then copy codes and scales to the pinned slabs on
- * the pipeline's transfer stream.  Replaces the cold-miss offload of the reference runner:
+ * quantize on the GPU (sc_quantize_int8 arithmetic, bit-exact with the reference) into one of
+ * two device staging slots on compute_stream, then copy codes and scales to the pinned slabs
+ * on the pipeline's transfer stream (K and V as the two rows of one 2-D copy), so the next
+ * layer's quantize overlaps this layer's copies.  Replaces the cold-miss offload of the reference runner:
  * quantize_kv_int8 + .cpu() + PinnedKVPool.write_block (speccache/serving/pipeline.py:506-524,
  * speccache/cache/pinned_pool.py:275-367).
  *  k, v       device [n_blocks * chunk_size, n_heads, head_dim], dtype x_dtype (F16|BF16|F32),
@@ -261,6 +262,12 @@ SC_API int32_t sc_pipeline_offload(sc_pipeline* p, int32_t layer, const int32_t*
 /* Wait (bounded by timeout_s, polling) for the last restore and offload; SC_ERR_TIMEOUT if
  * it ran out. */
 SC_API int32_t sc_pipeline_synchronize(sc_pipeline* p, double timeout_s);
+
+/* Make `stream` wait on the GPU (the host does not wait) until the restores and offloads
+ * enqueued so far have completed, their copies included: work enqueued on `stream` afterwards
+ * sees the restored caches and the offloaded slabs.  No counterpart in the reference (its
+ * loops synchronise the device instead). */
+SC_API int32_t sc_pipeline_join(sc_pipeline* p, void* stream);
 
 /* Read and clear the device status word of the pipeline's kernels (synchronises). */
 SC_API int32_t sc_pipeline_status(sc_pipeline* p, int32_t* status_bits);

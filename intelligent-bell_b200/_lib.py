@@ -80,6 +80,7 @@ _SIGNATURES = {
                                    _vp]),
     "sc_pipeline_offload": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _i32, _vp]),
     "sc_pipeline_synchronize": (_i32, [_vp, _f64]),
+    "sc_pipeline_join": (_i32, [_vp, _vp]),
     "sc_pipeline_status": (_i32, [_vp, _vp]),
     "sc_pipeline_destroy": (_i32, [_vp]),
     "sc_ipc_export": (_i32, [_vp, _vp, _vp]),

@@ -174,6 +174,12 @@ class KVRestorePipeline:
         ``timeout`` seconds."""
         _lib.check(self._lib.sc_pipeline_synchronize(self._h, float(timeout)), "sc_pipeline_synchronize")
 
+    def join(self, stream: torch.cuda.Stream | None = None) -> None:
+        """Make ``stream`` (default: the current stream) wait on the GPU for the restores and
+        offloads enqueued so far, copies included; the host does not wait."""
+        handle = stream.cuda_stream if stream is not None else _lib.stream_handle(self.device)
+        _lib.check(self._lib.sc_pipeline_join(self._h, handle), "sc_pipeline_join")
+
     def status(self) -> int:
         """Device status bits of the restore kernels (0 = clean); reading clears them."""
         bits = ctypes.c_int32(0)

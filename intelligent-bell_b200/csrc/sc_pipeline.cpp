@@ -123,10 +123,14 @@ struct sc_pipeline {
     std::vector<bool> slot_used;
     cudaEvent_t meta_uploaded = nullptr, done = nullptr;
     bool any_restore = false;
-    // offload: quantize into a device staging buffer, then D2H into the slabs
-    int8_t *o_kq = nullptr, *o_vq = nullptr;
-    uint16_t *o_ks = nullptr, *o_vs = nullptr;
-    cudaEvent_t o_ready = nullptr, o_done = nullptr;
+    // offload: quantize into one of two device staging slots (K then V codes in one
+    // allocation, K then V scales in another), then D2H into the slabs
+    int8_t* o_codes[2] = {nullptr, nullptr};
+    uint16_t* o_scales[2] = {nullptr, nullptr};
+    cudaEvent_t o_ready[2] = {nullptr, nullptr}, o_free[2] = {nullptr, nullptr};
+    bool o_used[2] = {false, false};
+    int o_next = 0, o_last = 0;
+    bool offload_scales_2d = false;
     bool any_offload = false;
 };
 
@@ -139,15 +143,15 @@ void release(sc_pipeline* p) {
     if (p->done && p->any_restore) cudaEventSynchronize(p->done);
     for (auto e : p->ready) cudaEventDestroy(e);
     for (auto e : p->slot_free) cudaEventDestroy(e);
-    if (p->o_done && p->any_offload) cudaEventSynchronize(p->o_done);
+    if (p->any_offload && p->o_free[p->o_last]) cudaEventSynchronize(p->o_free[p->o_last]);
     if (p->meta_uploaded) cudaEventDestroy(p->meta_uploaded);
     if (p->done) cudaEventDestroy(p->done);
-    if (p->o_ready) cudaEventDestroy(p->o_ready);
-    if (p->o_done) cudaEventDestroy(p->o_done);
-    cudaFree(p->o_kq);
-    cudaFree(p->o_vq);
-    cudaFree(p->o_ks);
-    cudaFree(p->o_vs);
+    for (int s = 0; s < 2; ++s) {
+        if (p->o_ready[s]) cudaEventDestroy(p->o_ready[s]);
+        if (p->o_free[s]) cudaEventDestroy(p->o_free[s]);
+        cudaFree(p->o_codes[s]);
+        cudaFree(p->o_scales[s]);
+    }
     if (p->transfer) cudaStreamDestroy(p->transfer);
     for (auto x : p->d_kq) cudaFree(x);  // d_vq[s] lies in the same allocation
     cudaFree(p->d_sc);
@@ -240,6 +244,7 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
         const size_t mp = static_cast<size_t>(max_pitch);
         p->codes_2d = slab_codes <= mp && stage_codes <= mp;
         p->scales_2d = static_cast<size_t>(n_blocks) * row * 2 <= mp && stage_scales * 2 <= mp;
+        p->offload_scales_2d = slab_scales * 2 <= mp && stage_scales * 2 <= mp;
     }
     if (e == cudaSuccess) e = cudaMalloc(&p->d_table, sizeof(int32_t) * max_restore_blocks);
     if (e == cudaSuccess) e = cudaMalloc(&p->d_meta, meta_bytes(max_restore_blocks));
@@ -260,12 +265,12 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
     }
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->meta_uploaded, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->done, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->o_ready, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->o_done, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaMalloc(&p->o_kq, stage_codes);
-    if (e == cudaSuccess) e = cudaMalloc(&p->o_vq, stage_codes);
-    if (e == cudaSuccess) e = cudaMalloc(&p->o_ks, stage_scales * 2);
-    if (e == cudaSuccess) e = cudaMalloc(&p->o_vs, stage_scales * 2);
+    for (int s = 0; s < 2 && e == cudaSuccess; ++s) {
+        e = cudaEventCreateWithFlags(&p->o_ready[s], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->o_free[s], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaMalloc(&p->o_codes[s], 2 * stage_codes);
+        if (e == cudaSuccess) e = cudaMalloc(&p->o_scales[s], 2 * stage_scales * 2);
+    }
     if (e != cudaSuccess) {
         const int32_t rc = cuda_error(e, "pipeline device set-up");
         release(p);
@@ -436,43 +441,69 @@ extern "C" int32_t sc_pipeline_offload(sc_pipeline* p, int32_t layer, const int3
     cudaStream_t cs = static_cast<cudaStream_t>(compute_stream);
     const int64_t n_tok = static_cast<int64_t>(n_blocks) * p->chunk;
     cudaError_t e = cudaSuccess;
-    // the staging buffer may still feed the previous offload's copies
-    if (p->any_offload) e = cudaStreamWaitEvent(cs, p->o_done, 0);
-    if (e != cudaSuccess) return cuda_error(e, "ordering the offload staging buffer");
-    const int64_t q_st[3] = {static_cast<int64_t>(p->H) * p->D, p->D, 1};
-    const int64_t s_st[2] = {p->H, 1};
-    int32_t rc = sc_quantize_int8(n_tok, p->H, p->D, k, x_dtype, k_strides, 1e-5f, p->o_kq, q_st,
-                                  p->o_ks, SC_DTYPE_F16, s_st, 0, cs);
-    if (rc != SC_OK) return rc;
-    rc = sc_quantize_int8(n_tok, p->H, p->D, v, x_dtype, v_strides, 1e-5f, p->o_vq, q_st, p->o_vs,
-                          SC_DTYPE_F16, s_st, 0, cs);
-    if (rc != SC_OK) return rc;
-    e = cudaEventRecord(p->o_ready, cs);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(p->transfer, p->o_ready, 0);
     const size_t row = static_cast<size_t>(p->chunk) * p->H;
     const size_t blk_codes = row * p->D, blk_scales = row;
+    const size_t stage_codes = static_cast<size_t>(p->max_blocks) * blk_codes;
+    const size_t stage_scales = static_cast<size_t>(p->max_blocks) * blk_scales;
+    const size_t slab_codes = static_cast<size_t>(p->L) * p->B * blk_codes;
+    const size_t slab_scales = static_cast<size_t>(p->L) * p->B * blk_scales;
+    // Staging slot s may still feed the copies of the offload before last: wait for them
+    // on the compute stream (layer l+1's quantize overlaps layer l's copies).
+    const int s = p->o_next;
+    if (p->o_used[s]) e = cudaStreamWaitEvent(cs, p->o_free[s], 0);
+    if (e != cudaSuccess) return cuda_error(e, "ordering the offload staging slot");
+    int8_t* okq = p->o_codes[s];
+    int8_t* ovq = okq + stage_codes;
+    uint16_t* oks = p->o_scales[s];
+    uint16_t* ovs = oks + stage_scales;
+    const int64_t q_st[3] = {static_cast<int64_t>(p->H) * p->D, p->D, 1};
+    const int64_t s_st[2] = {p->H, 1};
+    int32_t rc = sc_quantize_int8(n_tok, p->H, p->D, k, x_dtype, k_strides, 1e-5f, okq, q_st,
+                                  oks, SC_DTYPE_F16, s_st, 0, cs);
+    if (rc != SC_OK) return rc;
+    rc = sc_quantize_int8(n_tok, p->H, p->D, v, x_dtype, v_strides, 1e-5f, ovq, q_st, ovs,
+                          SC_DTYPE_F16, s_st, 0, cs);
+    if (rc != SC_OK) return rc;
+    e = cudaEventRecord(p->o_ready[s], cs);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(p->transfer, p->o_ready[s], 0);
     const size_t lay_codes = static_cast<size_t>(layer) * p->B * blk_codes;
     const size_t lay_scales = static_cast<size_t>(layer) * p->B * blk_scales;
+    // Per run: K and V codes as the two rows of one 2-D copy (host pitch slab_codes, device
+    // pitch stage_codes), and the same for the scales.
     for (int32_t i = 0; i < n_blocks && e == cudaSuccess;) {
         int32_t n = 1;
         while (i + n < n_blocks && block_ids[i + n] == block_ids[i] + n) ++n;
         const size_t b0 = static_cast<size_t>(block_ids[i]);
         const size_t src = static_cast<size_t>(i);
-        e = cudaMemcpyAsync(p->h_kq + lay_codes + b0 * blk_codes, p->o_kq + src * blk_codes,
-                            n * blk_codes, cudaMemcpyDeviceToHost, p->transfer);
-        if (e == cudaSuccess)
-            e = cudaMemcpyAsync(p->h_vq + lay_codes + b0 * blk_codes, p->o_vq + src * blk_codes,
-                                n * blk_codes, cudaMemcpyDeviceToHost, p->transfer);
-        if (e == cudaSuccess)
-            e = cudaMemcpyAsync(p->h_ks + lay_scales + b0 * blk_scales, p->o_ks + src * blk_scales,
-                                n * blk_scales * 2, cudaMemcpyDeviceToHost, p->transfer);
-        if (e == cudaSuccess)
-            e = cudaMemcpyAsync(p->h_vs + lay_scales + b0 * blk_scales, p->o_vs + src * blk_scales,
-                                n * blk_scales * 2, cudaMemcpyDeviceToHost, p->transfer);
+        int8_t* hc = p->h_kq + lay_codes + b0 * blk_codes;
+        const int8_t* dc = okq + src * blk_codes;
+        if (p->codes_2d) {
+            e = cudaMemcpy2DAsync(hc, slab_codes, dc, stage_codes, n * blk_codes, 2,
+                                  cudaMemcpyDeviceToHost, p->transfer);
+        } else {
+            e = cudaMemcpyAsync(hc, dc, n * blk_codes, cudaMemcpyDeviceToHost, p->transfer);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(hc + slab_codes, dc + stage_codes, n * blk_codes,
+                                    cudaMemcpyDeviceToHost, p->transfer);
+        }
+        uint16_t* hs = p->h_ks + lay_scales + b0 * blk_scales;
+        const uint16_t* ds = oks + src * blk_scales;
+        if (e == cudaSuccess && p->offload_scales_2d) {
+            e = cudaMemcpy2DAsync(hs, slab_scales * 2, ds, stage_scales * 2, n * blk_scales * 2, 2,
+                                  cudaMemcpyDeviceToHost, p->transfer);
+        } else if (e == cudaSuccess) {
+            e = cudaMemcpyAsync(hs, ds, n * blk_scales * 2, cudaMemcpyDeviceToHost, p->transfer);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(hs + slab_scales, ds + stage_scales, n * blk_scales * 2,
+                                    cudaMemcpyDeviceToHost, p->transfer);
+        }
         i += n;
     }
-    if (e == cudaSuccess) e = cudaEventRecord(p->o_done, p->transfer);
+    if (e == cudaSuccess) e = cudaEventRecord(p->o_free[s], p->transfer);
     if (e != cudaSuccess) return cuda_error(e, "offload enqueue");
+    p->o_used[s] = true;
+    p->o_last = s;
+    p->o_next = (s + 1) % 2;
     p->any_offload = true;
     return sc::ok();
 }
@@ -499,9 +530,20 @@ extern "C" int32_t sc_pipeline_synchronize(sc_pipeline* p, double timeout_s) {
         if (rc != SC_OK) return rc;
     }
     if (p->any_offload) {
-        const int32_t rc = wait_event(p->o_done, deadline, timeout_s, "offload");
+        const int32_t rc = wait_event(p->o_free[p->o_last], deadline, timeout_s, "offload");
         if (rc != SC_OK) return rc;
     }
+    return sc::ok();
+}
+
+extern "C" int32_t sc_pipeline_join(sc_pipeline* p, void* stream) {
+    if (!p) return set_error(SC_ERR_INVALID_ARGUMENT, "null pipeline");
+    DeviceGuard g(p->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSuccess;
+    if (p->any_restore) e = cudaStreamWaitEvent(st, p->done, 0);
+    if (e == cudaSuccess && p->any_offload) e = cudaStreamWaitEvent(st, p->o_free[p->o_last], 0);
+    if (e != cudaSuccess) return cuda_error(e, "joining the pipeline");
     return sc::ok();
 }
 

@@ -144,6 +144,34 @@ def test_offload_then_restore_round_trip(scb, oracle):
     inj.close()
 
 
+def test_offload_staging_ring_and_join(scb, oracle):
+    # successive offloads alternate two staging slots (the third reuses the first); join makes
+    # the current stream wait for their copies on the GPU, after which the slabs hold the
+    # oracle's codes and scales
+    from speccache_b200.cache import KVRestorePipeline
+
+    layers, blocks, chunk, h, d = 3, 8, 32, 4, 128
+    ids = [[5, 6, 7, 1], [0, 2], [3, 4, 5, 6, 7, 0]]  # a run plus a lone block; scattered; runs
+    g = torch.Generator().manual_seed(21)
+    with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV) as pipe:
+        xs = []
+        for layer, b in enumerate(ids):
+            k = torch.randn((len(b) * chunk, h, d), generator=g).to(torch.bfloat16)
+            v = torch.randn((len(b) * chunk, h, d), generator=g).to(torch.bfloat16)
+            xs.append((k, v))
+            pipe.offload(layer, b, k.to(DEV), v.to(DEV))
+        pipe.join()
+        torch.cuda.current_stream().synchronize()
+        for layer, b in enumerate(ids):
+            for x, q_slab, s_slab in ((xs[layer][0], pipe.k_quant, pipe.k_scale),
+                                      (xs[layer][1], pipe.v_quant, pipe.v_scale)):
+                q_ref, s_ref = oracle.quantize_kv_int8(x)
+                got_q = torch.cat([q_slab[layer, blk] for blk in b])
+                got_s = torch.cat([s_slab[layer, blk] for blk in b])
+                assert torch.equal(got_q, q_ref)
+                assert bits_equal(got_s.reshape(s_ref.shape), s_ref)
+
+
 def test_pool_async_dma_multi_chunk_parity(scb, oracle):
     # reference tests/test_phase2_engine.py:297-359: 4 chunks with distinct shifts
     from speccache_b200.cache import PinnedKVPool

@@ -149,6 +149,29 @@ SC_API int32_t sc_dequant_rope_kv_token_shifts_noalloc(
     void* v_out, const int64_t* vo_strides, int32_t out_dtype, uint32_t flags, void* stream);
 
 /*
+ * Relative RoPE shift of already dequantised keys (float16 / bfloat16 in and out).
+ * Replaces the rotation of MultiLayerKVInjector.apply_rope_shift
+ * (speccache/serving/kv_injector.py:246-283), which inject_layer_kv applies before appending
+ * keys to the cache (kv_injector.py:285-301).
+ *
+ *  x, out     [n_tokens, n_heads, head_dim] (head_dim even), dtypes x_dtype / out_dtype
+ *             (F16 | BF16), element strides [token, head, dim]; out may be x itself (same
+ *             strides) for an in-place shift, no other overlap
+ *  cos_delta/sin_delta  fp16 tables, strides [token, dim]; token stride 0 broadcasts one row
+ *             ([1, D/2]), a non-zero one gives one row per token ([T, D/2]); NULL for both to
+ *             use delta_p (the table as sc_rope_cos_sin_delta computes it from theta_base,
+ *             inv_freq)
+ *  out = cvt(RN(x * cos) -/+ RN(x_partner * sin)): the reference's fp32 arithmetic, each
+ *  product and the sum rounded once, bit-exact given the same tables.
+ */
+SC_API int32_t sc_rope_shift_keys(int64_t n_tokens, int32_t n_heads, int32_t head_dim,
+                                  const void* x, int32_t x_dtype, const int64_t* x_strides,
+                                  const void* cos_delta, const void* sin_delta,
+                                  const int64_t* cs_strides, double delta_p, double theta_base,
+                                  const float* inv_freq, void* out, int32_t out_dtype,
+                                  const int64_t* out_strides, void* stream);
+
+/*
  * Per-(token, head) absmax INT8 quantisation (the offload twin).
  * Replaces quantize_kv_int8 / quantize_symmetric_int8 (speccache/kernels/reference.py:179-209).
  *

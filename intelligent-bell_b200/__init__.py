@@ -31,6 +31,7 @@ from .kernels import (
     quantize_symmetric_int8,
     restore_layers,
     restore_paged,
+    rope_shift_keys,
     rotate_half,
     triton_fused_k_dequant_rope_shift,
     validate_key_inputs,
@@ -54,6 +55,7 @@ __all__ = [
     "quantize_symmetric_int8",
     "restore_layers",
     "restore_paged",
+    "rope_shift_keys",
     "rotate_half",
     "triton_fused_k_dequant_rope_shift",
     "validate_key_inputs",

@@ -66,6 +66,8 @@ _SIGNATURES = {
                                                        _i32, _vp, _f64, _vp,  # dtype, shifts
                                                        _vp, _vp, _vp, _vp,  # outputs
                                                        _i32, _u32, _vp]),
+    "sc_rope_shift_keys": (_i32, [_i64, _i32, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _f64, _f64,
+                                  _vp, _vp, _i32, _vp, _vp]),
     "sc_quantize_int8": (_i32, [_i64, _i32, _i32, _vp, _i32, _vp, _f32, _vp, _vp, _vp, _i32,
                                 _vp, _u32, _vp]),
     "sc_restore_paged": (_i32, [_i32, _i32, _i32, _i32, _i32, _i64,

@@ -28,6 +28,13 @@ int sm_count();
 // when the caller gives none.  `out` has room for head_dim/2 values.
 void default_inv_freq(int32_t head_dim, double theta, float* out);
 
+// cos/sin of one shift as the reference tabulates them (angle = fp32(dp * inv_freq), cos and
+// sin in double rounded to fp32 then fp16), packed as half2(cos, sin) per frequency into
+// tab[head_dim / 2]; inv_freq may be null (then 1/theta^(2i/D)).  Recent tables are cached
+// per host thread.
+void host_cos_sin_table(int head_dim, float dp, double theta, const float* inv_freq,
+                        uint32_t* tab);
+
 // Largest head_dim handled by any kernel (the inverse-frequency table travels as a
 // kernel parameter of head_dim/2 floats).
 constexpr int kMaxHeadDim = 1024;

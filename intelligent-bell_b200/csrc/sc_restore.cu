@@ -316,7 +316,7 @@ uint64_t hash_freqs(const float* f, int n) {
     return h;
 }
 
-void fill_host_table(DenseParams& p, int head_dim, float dp, double theta, const float* inv_freq) {
+void fill_host_table(uint32_t* out_tab, int head_dim, float dp, double theta, const float* inv_freq) {
     float tmp[kMaxHeadDim / 2];
     if (inv_freq == nullptr) {
         default_inv_freq(head_dim, theta, tmp);
@@ -332,7 +332,7 @@ void fill_host_table(DenseParams& p, int head_dim, float dp, double theta, const
     for (int e = 0; e < kEntries; ++e) {
         const HostTable& c = cache[e];
         if (c.valid && c.dp_bits == dp_bits && c.head_dim == head_dim && c.freq_hash == fh) {
-            memcpy(p.tab, c.tab, sizeof(uint32_t) * half);
+            memcpy(out_tab, c.tab, sizeof(uint32_t) * half);
             return;
         }
     }
@@ -349,7 +349,7 @@ void fill_host_table(DenseParams& p, int head_dim, float dp, double theta, const
     c.head_dim = head_dim;
     c.freq_hash = fh;
     c.valid = true;
-    memcpy(p.tab, c.tab, sizeof(uint32_t) * half);
+    memcpy(out_tab, c.tab, sizeof(uint32_t) * half);
 }
 
 template <typename K>
@@ -411,6 +411,12 @@ cudaError_t dispatch(const DenseParams& p, const GenericStrides& g, bool vec, bo
 }
 
 }  // namespace
+
+void host_cos_sin_table(int head_dim, float dp, double theta, const float* inv_freq,
+                        uint32_t* tab) {
+    fill_host_table(tab, head_dim, dp, theta, inv_freq);
+}
+
 }  // namespace sc
 
 using namespace sc;
@@ -539,7 +545,7 @@ extern "C" int32_t sc_dequant_rope_kv(
             fill_inv_freq(p, head_dim, theta_base, inv_freq);
         } else {
             p.cs_kind = 3;
-            fill_host_table(p, head_dim, static_cast<float>(delta_p), theta_base, inv_freq);
+            fill_host_table(p.tab, head_dim, static_cast<float>(delta_p), theta_base, inv_freq);
         }
     }
 

@@ -16,6 +16,7 @@ from .restore import (
     restore_layers,
     triton_fused_k_dequant_rope_shift,
 )
+from .shift import rope_shift_keys
 from .validation import rotate_half, validate_key_inputs, validate_value_inputs
 
 # The reference exports its Triton kernel object under this name; here it names the
@@ -33,6 +34,7 @@ __all__ = [
     "quantize_symmetric_int8",
     "restore_layers",
     "restore_paged",
+    "rope_shift_keys",
     "rotate_half",
     "triton_fused_k_dequant_rope_shift",
     "validate_key_inputs",

@@ -24,6 +24,7 @@ import torch
 from ..cache.pinned_pool import PinnedKVPool
 from ..cache.pipeline import KVRestorePipeline
 from ..kernels.restore import dequant_kv_cache
+from ..kernels.shift import rope_shift_keys, token_major
 
 
 class SpecDynamicCache:
@@ -170,6 +171,45 @@ class MultiLayerKVInjector:
         if x.ndim == 3:
             return x
         raise ValueError(f"Unexpected tensor ndim={x.ndim}, expected 3 or 4.")
+
+    def apply_rope_shift(self, k_fp16: torch.Tensor, delta_p: int) -> torch.Tensor:
+        """Rotate dequantised keys (``[T, H, D]`` or ``[1, H, T, D]``, float16/bfloat16) by
+        ``delta_p``; same layout and dtype, a zero shift returns ``k_fp16`` itself
+        (kv_injector.py:246-283).  One kernel launch, no layout copies."""
+        if delta_p == 0:
+            return k_fp16
+        return rope_shift_keys(k_fp16, delta_p, theta=self.theta)
+
+    def inject_layer_kv(self, cache: SpecDynamicCache, layer_idx: int, k_tensor: torch.Tensor,
+                        v_tensor: torch.Tensor, delta_p: int = 0) -> None:
+        """Append ``[T, H, D]`` or ``[1, H, T, D]`` keys/values to a cache layer, keys shifted
+        by ``delta_p`` (kv_injector.py:285-301).  The shift kernel writes straight into the
+        cache's next slots; without a shift the tokens are copied there."""
+        if k_tensor.ndim == 4 and k_tensor.shape[0] != 1 and delta_p == 0:
+            cache.update(k_tensor, v_tensor, layer_idx=layer_idx)  # batched model layout
+            return
+        kt, vt = token_major(k_tensor), token_major(v_tensor)
+        if kt.shape != vt.shape or kt.dtype != vt.dtype or kt.device != vt.device:
+            raise ValueError(f"keys {tuple(kt.shape)} {kt.dtype} and values {tuple(vt.shape)} "
+                             f"{vt.dtype} differ")
+        t, h, d = kt.shape
+        cache.reserve(layer_idx, t, batch=1, heads=h, head_dim=d, dtype=kt.dtype, device=kt.device)
+        k_dst, v_dst = cache.append_views(layer_idx, t)
+        if delta_p != 0:
+            rope_shift_keys(kt, delta_p, theta=self.theta, out=k_dst)
+        else:
+            k_dst.copy_(kt)
+        v_dst.copy_(vt)
+        cache.commit(layer_idx, t)
+
+    def inject_multi_layer(self, cache: SpecDynamicCache, layer_k_list: Sequence[torch.Tensor],
+                           layer_v_list: Sequence[torch.Tensor], delta_p: int = 0) -> None:
+        """:meth:`inject_layer_kv` for every layer (kv_injector.py:303-322)."""
+        if len(layer_k_list) != len(layer_v_list):
+            raise ValueError(f"Mismatch in layer counts: {len(layer_k_list)} keys vs "
+                             f"{len(layer_v_list)} values")
+        for layer_idx, (k, v) in enumerate(zip(layer_k_list, layer_v_list, strict=True)):
+            self.inject_layer_kv(cache, layer_idx, k, v, delta_p=delta_p)
 
     def reconstruct_layer_chunk(self, layer_idx: int, block_id: int, delta_p: int,
                                 cos_delta: torch.Tensor | None = None,

@@ -18,6 +18,8 @@ Reference functions exercised (``path:line`` in the reference project):
 * speccache/kernels/reference.py:283-307  dequant_value_ref
 * speccache/cache/pinned_pool.py:392-464  PinnedKVPool.get_coalesced_views
 * speccache/serving/kv_injector.py:392-498 MultiLayerKVInjector.reconstruct_and_inject_multi_layer (CPU path)
+* speccache/serving/kv_injector.py:246-322 MultiLayerKVInjector.apply_rope_shift, inject_layer_kv,
+  inject_multi_layer (CPU path)
 """
 
 from __future__ import annotations
@@ -192,6 +194,42 @@ def make_pool_and_injector(ref_root: str, out: dict) -> None:
     out["inj_vq"], out["inj_vs"] = _t2n(inj.unified_v_quant), _t2n(inj.unified_v_scale)
 
 
+def make_key_shift_and_inject(ref_root: str, out: dict) -> None:
+    """RoPE shift of dequantised keys and the cache injection built on it, run by the reference."""
+    sys.path.insert(0, ref_root)
+    logging.disable(logging.CRITICAL)
+    from speccache.serving.kv_injector import MultiLayerKVInjector, SpecDynamicCache  # noqa: E402
+
+    g = torch.Generator().manual_seed(11)
+    cases = [("f16_d64", torch.float16, 24, 3, 64, [-384, 1, 4095, 70000]),
+             ("f16_d128", torch.float16, 17, 2, 128, [-8192, 513]),
+             ("bf16_d128", torch.bfloat16, 9, 4, 128, [2048])]
+    for tag, dtype, t, h, d, dps in cases:
+        inj = MultiLayerKVInjector(1, h, d, device=torch.device("cpu"), max_blocks=1, chunk_size=8)
+        k = (torch.randn((t, h, d), generator=g) * 4).to(dtype)
+        out[f"ks_{tag}_k"] = _t2n(k)
+        out[f"ks_{tag}_dps"] = np.array(dps, dtype=np.int64)
+        for i, dp in enumerate(dps):
+            out[f"ks_{tag}_out{i}"] = _t2n(inj.apply_rope_shift(k, dp))
+        # the model layout [1, H, T, D] is shifted in the same layout
+        out[f"ks_{tag}_out4d"] = _t2n(inj.apply_rope_shift(inj.format_to_model_layout(k), dps[0]))
+    # injection: two appends to one layer (the second shifted), then a multi-layer injection
+    h, d, t = 2, 64, 12
+    inj = MultiLayerKVInjector(2, h, d, device=torch.device("cpu"), max_blocks=1, chunk_size=8)
+    ks = [torch.randn((t, h, d), generator=g).half() for _ in range(4)]
+    vs = [torch.randn((t, h, d), generator=g).half() for _ in range(4)]
+    cache = SpecDynamicCache()
+    inj.inject_layer_kv(cache, 0, ks[0], vs[0])
+    inj.inject_layer_kv(cache, 0, ks[1], vs[1], delta_p=-700)
+    out["inj1_k"], out["inj1_v"] = _t2n(cache[0][0]), _t2n(cache[0][1])
+    cache = SpecDynamicCache()
+    inj.inject_multi_layer(cache, ks[2:], vs[2:], delta_p=300)
+    for layer in range(2):
+        out[f"injm_k{layer}"], out[f"injm_v{layer}"] = _t2n(cache[layer][0]), _t2n(cache[layer][1])
+    for i in range(4):
+        out[f"inj_in_k{i}"], out[f"inj_in_v{i}"] = _t2n(ks[i]), _t2n(vs[i])
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -204,6 +242,7 @@ def main() -> None:
     make_tables(ref, out)
     make_shift(ref, out)
     make_pool_and_injector(args.reference, out)
+    make_key_shift_and_inject(args.reference, out)
     np.savez_compressed(args.out, **out)
     print(f"wrote {args.out}: {len(out)} arrays, {os.path.getsize(args.out)} bytes")
 

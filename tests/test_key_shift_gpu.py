@@ -1,0 +1,128 @@
+"""GPU tests of the RoPE shift of dequantised keys (sc_rope_shift_keys) and the cache
+injection built on it, against the oracle and the reference's own outputs (golden vectors).
+
+Mirrors MultiLayerKVInjector.apply_rope_shift / inject_layer_kv / inject_multi_layer
+(speccache/serving/kv_injector.py:246-322), which the reference runner calls on its
+reuse path (speccache/serving/pipeline.py:439-446).  With the reference's tables the kernel
+is bit-exact; with the shift expanded by the library (delta_p) K stays within the reference
+tolerance (rtol = atol = 1e-2) with at least 98 % of values bit-equal.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+from hypothesis import HealthCheck, given, settings
+from hypothesis import strategies as st
+
+from conftest import as_tensor, bits_equal
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0) if torch.cuda.is_available() else None
+CASES = ("f16_d64", "f16_d128", "bf16_d128")
+
+
+def _dt(tag):
+    return "bfloat16" if tag.startswith("bf16") else "float16"
+
+
+def _close_mostly_exact(got: torch.Tensor, ref: torch.Tensor) -> None:
+    got = got.cpu()
+    torch.testing.assert_close(got.float(), ref.float(), rtol=1e-2, atol=1e-2)
+    assert (got.view(torch.int16) == ref.view(torch.int16)).float().mean().item() >= 0.98
+
+
+def test_shift_with_reference_tables_is_bit_exact(scb, oracle, golden):
+    for tag in CASES:
+        k = as_tensor(golden[f"ks_{tag}_k"], _dt(tag))
+        d = k.shape[-1]
+        for i, dp in enumerate(golden[f"ks_{tag}_dps"].tolist()):
+            cos, sin = oracle.compute_rope_cos_sin_delta(dp, d)
+            got = scb.rope_shift_keys(k.to(DEV), cos_delta=cos.to(DEV), sin_delta=sin.to(DEV))
+            assert bits_equal(got.cpu(), as_tensor(golden[f"ks_{tag}_out{i}"], _dt(tag))), (tag, dp)
+
+
+def test_shift_by_delta_p_matches_reference(scb, golden):
+    from speccache_b200.serving import MultiLayerKVInjector
+
+    for tag in CASES:
+        k = as_tensor(golden[f"ks_{tag}_k"], _dt(tag))
+        t, h, d = k.shape
+        inj = MultiLayerKVInjector(1, h, d, device=DEV, max_blocks=1, chunk_size=8)
+        dps = golden[f"ks_{tag}_dps"].tolist()
+        for i, dp in enumerate(dps):
+            _close_mostly_exact(inj.apply_rope_shift(k.to(DEV), dp),
+                                as_tensor(golden[f"ks_{tag}_out{i}"], _dt(tag)))
+        # the model layout [1, H, T, D] is shifted in place of layout, no copies
+        k4 = k.permute(1, 0, 2).unsqueeze(0).contiguous().to(DEV)
+        out4 = inj.apply_rope_shift(k4, dps[0])
+        assert out4.shape == k4.shape and out4.is_contiguous()
+        _close_mostly_exact(out4, as_tensor(golden[f"ks_{tag}_out4d"], _dt(tag)))
+        assert inj.apply_rope_shift(k4, 0) is k4
+        inj.close()
+
+
+def test_injection_matches_reference(scb, golden):
+    from speccache_b200.serving import MultiLayerKVInjector, SpecDynamicCache
+
+    ks = [as_tensor(golden[f"inj_in_k{i}"]).to(DEV) for i in range(4)]
+    vs = [as_tensor(golden[f"inj_in_v{i}"]).to(DEV) for i in range(4)]
+    _, h, d = ks[0].shape
+    inj = MultiLayerKVInjector(2, h, d, device=DEV, max_blocks=1, chunk_size=8)
+    cache = SpecDynamicCache()
+    inj.inject_layer_kv(cache, 0, ks[0], vs[0])
+    inj.inject_layer_kv(cache, 0, ks[1], vs[1], delta_p=-700)
+    k, v = cache[0]
+    assert k.shape == (1, h, 2 * ks[0].shape[0], d)
+    _close_mostly_exact(k, as_tensor(golden["inj1_k"]))
+    assert bits_equal(v.cpu(), as_tensor(golden["inj1_v"]))
+    cache = SpecDynamicCache()
+    inj.inject_multi_layer(cache, ks[2:], vs[2:], delta_p=300)
+    for layer in range(2):
+        k, v = cache[layer]
+        _close_mostly_exact(k, as_tensor(golden[f"injm_k{layer}"]))
+        assert bits_equal(v.cpu(), as_tensor(golden[f"injm_v{layer}"]))
+    with pytest.raises(ValueError, match="Mismatch in layer counts"):
+        inj.inject_multi_layer(cache, ks[:2], vs[:1])
+    inj.close()
+
+
+def test_in_place_and_errors(scb, oracle):
+    g = torch.Generator().manual_seed(8)
+    k = (torch.randn((50, 4, 128), generator=g) * 3).half()
+    cos, sin = oracle.compute_rope_cos_sin_delta(-1234, 128)
+    kd = k.to(DEV)
+    out = scb.rope_shift_keys(kd, cos_delta=cos.to(DEV), sin_delta=sin.to(DEV), out=kd)
+    assert out.data_ptr() == kd.data_ptr()
+    assert bits_equal(kd.cpu(), oracle.rotate_keys(k, cos, sin))
+    with pytest.raises(ValueError, match="even"):
+        scb.rope_shift_keys(torch.zeros((2, 2, 7), dtype=torch.float16, device=DEV), 3)
+    with pytest.raises(TypeError):
+        scb.rope_shift_keys(torch.zeros((2, 2, 8), dtype=torch.float32, device=DEV), 3)
+    with pytest.raises(RuntimeError):
+        scb.rope_shift_keys(torch.zeros((2, 2, 8), dtype=torch.float16), 3)
+    with pytest.raises(ValueError, match="delta_p"):
+        scb.rope_shift_keys(torch.zeros((2, 2, 8), dtype=torch.float16, device=DEV))
+
+
+@settings(max_examples=40, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+@given(t=st.integers(1, 300), h=st.integers(1, 9), d=st.sampled_from([2, 8, 34, 64, 96, 128, 256]),
+       in_dtype=st.sampled_from([torch.float16, torch.bfloat16]),
+       out_dtype=st.sampled_from([torch.float16, torch.bfloat16]), model_layout=st.booleans(),
+       per_token=st.booleans(), seed=st.integers(0, 2**31 - 1))
+def test_shift_property_bit_exact(scb, oracle, t, h, d, in_dtype, out_dtype, model_layout,
+                                  per_token, seed):
+    g = torch.Generator().manual_seed(seed)
+    k = (torch.randn((t, h, d), generator=g) * 8).to(in_dtype)
+    dps = torch.randint(-70000, 70000, (t if per_token else 1,), generator=g)
+    cos, sin = oracle.compute_rope_cos_sin_delta(dps, d, 500000.0)
+    if model_layout:  # [1, H, T, D] in and out, handled through strides
+        kin = k.permute(1, 0, 2).unsqueeze(0).contiguous().to(DEV)
+        out = torch.empty(kin.shape, dtype=out_dtype, device=DEV)
+    else:
+        kin = k.to(DEV)
+        out = torch.empty((t, h, d), dtype=out_dtype, device=DEV)
+    scb.rope_shift_keys(kin, cos_delta=cos.to(DEV), sin_delta=sin.to(DEV), out=out)
+    got = out[0].permute(1, 0, 2) if model_layout else out
+    assert bits_equal(got.cpu().contiguous(), oracle.rotate_keys(k, cos, sin, out_dtype))

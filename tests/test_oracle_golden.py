@@ -93,3 +93,33 @@ def test_restore_paged_equals_per_request_blocks(oracle):
         n = (lens[r] + page - 1) // page
         kb, vb = oracle.restore_blocks(pkq, pks, pvq, pvs, table[r, :n].tolist(), [dps[r]] * n)
         assert bits_equal(k, kb[: lens[r]]) and bits_equal(v, vb[: lens[r]])
+
+
+KEY_SHIFT_CASES = ("f16_d64", "f16_d128", "bf16_d128")
+
+
+def test_key_shift_matches_reference(golden, oracle):
+    # MultiLayerKVInjector.apply_rope_shift (kv_injector.py:246-283), both layouts
+    for tag in KEY_SHIFT_CASES:
+        dt = "bfloat16" if tag.startswith("bf16") else "float16"
+        k = as_tensor(golden[f"ks_{tag}_k"], dt)
+        dps = golden[f"ks_{tag}_dps"].tolist()
+        for i, dp in enumerate(dps):
+            assert bits_equal(oracle.apply_rope_shift(k, dp), as_tensor(golden[f"ks_{tag}_out{i}"], dt))
+        k4 = oracle.to_model_layout(k)
+        assert bits_equal(oracle.apply_rope_shift(k4, dps[0]), as_tensor(golden[f"ks_{tag}_out4d"], dt))
+        assert oracle.apply_rope_shift(k, 0) is k
+
+
+def test_injection_matches_reference(golden, oracle):
+    # inject_layer_kv / inject_multi_layer (kv_injector.py:285-322): model layout, shift, append
+    ks = [as_tensor(golden[f"inj_in_k{i}"]) for i in range(4)]
+    vs = [as_tensor(golden[f"inj_in_v{i}"]) for i in range(4)]
+    k1 = torch.cat([oracle.to_model_layout(ks[0]),
+                    oracle.apply_rope_shift(oracle.to_model_layout(ks[1]), -700)], dim=-2)
+    v1 = torch.cat([oracle.to_model_layout(vs[0]), oracle.to_model_layout(vs[1])], dim=-2)
+    assert bits_equal(k1, as_tensor(golden["inj1_k"])) and bits_equal(v1, as_tensor(golden["inj1_v"]))
+    for layer in range(2):
+        k = oracle.apply_rope_shift(oracle.to_model_layout(ks[2 + layer]), 300)
+        assert bits_equal(k, as_tensor(golden[f"injm_k{layer}"]))
+        assert bits_equal(oracle.to_model_layout(vs[2 + layer]), as_tensor(golden[f"injm_v{layer}"]))

@@ -93,7 +93,9 @@ __device__ __forceinline__ uint32_t code_byte(float x, float scale) {
 // Fast codes.  y = RN(x * RN(1/scale)) is within 2^-16 of the true quotient x / scale
 // whenever |x / scale| < 128 (two roundings of 2^-24 relative each), and RN(x / scale)
 // is within half an ulp (<= 2^-18) of the true quotient, so when y is farther than
-// kTieBand from every half-integer both round to the same integer.  For a finite row the
+// kTieBand from every half-integer both round to the same integer.  Scales outside
+// [2^-126, 2^125] (whose reciprocal would be subnormal, with fewer bits) always take the
+// exact path.  For a finite row the
 // quotient is also below 127.5 in magnitude (the fp16 scale is amax/127 up to a relative
 // 2^-11, or 0.3 % in the fp16 subnormal range, or the larger eps), so the rounded value
 // needs no clamp.  n = (y + 1.5*2^23) - 1.5*2^23 is y rounded half to even, the sum's
@@ -198,7 +200,8 @@ __global__ void __launch_bounds__(kQThreads, QuantMinBlocks<InT>::value) quant_v
         const float sc = quant_scale(m, p.eps, kF16Scale);
         const float rcp = __frcp_rn(sc);
         const float2 rcp2 = make_float2(rcp, rcp);
-        bool tie = !(sc > 0.0f && sc < 3.0e38f);  // non-finite or zero scale: exact path
+        // zero, tiny, huge or non-finite scale: exact path
+        bool tie = !(sc >= 0x1p-126f && sc <= 0x1p125f);
         // Codes are packed four to a word as they are made, so only the packed words stay live.
         uint32_t packed[E / 4];
 #pragma unroll

@@ -440,6 +440,18 @@ def test_fp32_scales_dense_and_quantize(scb, oracle):
     q_ref = torch.clamp(torch.round(x / s_ref), -127, 127).to(torch.int8)
     assert s.dtype == torch.float32 and bits_equal(s.cpu(), s_ref)
     assert torch.equal(q.cpu(), q_ref)
+    # eps = 0 with float32 scales: rows of subnormal values get subnormal scales (whose
+    # reciprocal overflows float32), handled by the exact division
+    xs = torch.randn((t, h, d), generator=g) * 1e-39
+    xs[3, 1] = 0.0
+    q, s = scb.quantize_kv_int8(xs.to(DEV), eps=0.0, scale_dtype=torch.float32)
+    torch.cuda.synchronize()
+    s_ref = torch.clamp(xs.abs().amax(-1, keepdim=True) / 127.0, min=0.0)
+    with torch.no_grad():
+        q_ref = torch.clamp(torch.round(xs / s_ref), -127, 127).nan_to_num(0.0).to(torch.int8)
+    assert bits_equal(s.cpu(), s_ref)
+    nz = s_ref.expand_as(xs) != 0  # the all-zero row divides 0 by 0 (outside the contract)
+    assert torch.equal(q.cpu()[nz], q_ref[nz])
 
 
 def test_paged_fp32_intermediate_and_fp16(scb, oracle):

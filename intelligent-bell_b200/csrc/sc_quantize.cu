@@ -167,79 +167,91 @@ __device__ __forceinline__ float2 pair_at(const uint32_t* w, int k) {
     }
 }
 
+// The lane's V x 32 input bytes of `row` into w, and the row's token and head.
+template <typename InT, int V>
+__device__ __forceinline__ void fetch_row(const QuantParams& p, int64_t row, int lane,
+                                          uint32_t* w, int64_t& t, int64_t& h) {
+    constexpr int E = 32 * V / static_cast<int>(sizeof(InT));
+    const uint32_t ti = fdiv(static_cast<uint32_t>(row), p.divH);
+    t = ti;
+    h = static_cast<int64_t>(static_cast<uint32_t>(row) - ti * static_cast<uint32_t>(p.H));
+    const char* xp = reinterpret_cast<const char*>(
+        reinterpret_cast<const InT*>(p.x) + t * p.x_t + h * p.x_h + lane * E);
+#pragma unroll
+    for (int v = 0; v < V; ++v) ld_stream_v8(xp + 32 * v, w + 8 * v);
+}
+
+// Codes and scale of one row from the lane's words w and the row's absmax m.
+template <typename InT, typename ScaleT, int V>
+__device__ __forceinline__ void convert_store(const QuantParams& p, uint32_t* w, float m,
+                                              int64_t t, int64_t h, int lane) {
+    constexpr int E = 32 * V / static_cast<int>(sizeof(InT));
+    constexpr bool kF16Scale = std::is_same<ScaleT, __half>::value;
+    const float sc = quant_scale(m, p.eps, kF16Scale);
+    const float rcp = __frcp_rn(sc);
+    const float2 rcp2 = make_float2(rcp, rcp);
+    // zero, tiny, huge or non-finite scale: exact path
+    bool tie = !(sc >= 0x1p-126f && sc <= 0x1p125f);
+    // Codes are packed four to a word as they are made, so only the packed words stay live.
+    uint32_t packed[E / 4];
+#pragma unroll
+    for (int k = 0; k < E; k += 4) {
+        uint32_t c0, c1, c2, c3;
+        fast_codes2(pair_at<InT>(w, k), rcp2, c0, c1, tie);
+        fast_codes2(pair_at<InT>(w, k + 2), rcp2, c2, c3, tie);
+        packed[k / 4] = pack_low_bytes(c0, c1, c2, c3);
+    }
+    if (tie) {  // rare: reload the lane's input (keeps the fast path's registers free)
+        int64_t t2, h2;
+        fetch_row<InT, V>(p, t * p.H + h, lane, w, t2, h2);
+#pragma unroll
+        for (int k = 0; k < E; k += 4) {
+            const float2 x0 = pair_at<InT>(w, k), x1 = pair_at<InT>(w, k + 2);
+            packed[k / 4] = pack_low_bytes(code_byte(x0.x, sc), code_byte(x0.y, sc),
+                                           code_byte(x1.x, sc), code_byte(x1.y, sc));
+        }
+    }
+    int8_t* qp = p.q + t * p.q_t + h * p.q_h + lane * E;
+    if constexpr (E >= 32) {
+#pragma unroll
+        for (int c = 0; c < E / 32; ++c)
+            st_v8(qp + 32 * c, *reinterpret_cast<const uint32_t(*)[8]>(packed + 8 * c));
+    } else if constexpr (E == 16) {
+        st_v4(qp, make_uint4(packed[0], packed[1], packed[2], packed[3]));
+    } else {
+        st_v2(qp, make_uint2(packed[0], packed[1]));
+    }
+    if (lane == 0) {
+        ScaleT* sp = reinterpret_cast<ScaleT*>(p.s) + t * p.s_t + h * p.s_h;
+        if constexpr (kF16Scale)
+            *sp = __float2half_rn(sc);
+        else
+            *sp = sc;
+    }
+}
+
 // Vector path: each lane owns V x 32 bytes of a row (E = 32 V / sizeof(x) elements, V
 // 256-bit loads in flight per lane); G lanes (a power of two <= 32) cover the row.  Larger
 // V shares the per-row work (scale, reciprocal, shuffles, addressing) among more elements.
 template <typename InT, typename ScaleT, int V>
 __global__ void __launch_bounds__(kQThreads, QuantMinBlocks<InT>::value) quant_vec(const __grid_constant__ QuantParams p) {
     constexpr int NW = 8 * V;
-    constexpr int E = 32 * V / static_cast<int>(sizeof(InT));
     const int G = p.G;
     const int lane = threadIdx.x % G;
     const int RB = blockDim.x / G;
-    constexpr bool kF16Scale = std::is_same<ScaleT, __half>::value;
-    for (int64_t base = static_cast<int64_t>(blockIdx.x) * RB; base < p.rows;
-         base += static_cast<int64_t>(gridDim.x) * RB) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * RB;
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * RB; base < p.rows; base += stride) {
         const int64_t row = base + threadIdx.x / G;
         const bool active = row < p.rows;
         uint32_t w[NW];
         int64_t t = 0, h = 0;
         float m = 0.0f;
         if (active) {
-            const uint32_t ti = fdiv(static_cast<uint32_t>(row), p.divH);
-            t = ti;
-            h = static_cast<int64_t>(static_cast<uint32_t>(row) - ti * static_cast<uint32_t>(p.H));
-            const char* xp = reinterpret_cast<const char*>(
-                reinterpret_cast<const InT*>(p.x) + t * p.x_t + h * p.x_h + lane * E);
-#pragma unroll
-            for (int v = 0; v < V; ++v) ld_stream_v8(xp + 32 * v, w + 8 * v);
+            fetch_row<InT, V>(p, row, lane, w, t, h);
             m = lane_absmax<InT>(w);
         }
         for (int o = G >> 1; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (!active) continue;
-        const float sc = quant_scale(m, p.eps, kF16Scale);
-        const float rcp = __frcp_rn(sc);
-        const float2 rcp2 = make_float2(rcp, rcp);
-        // zero, tiny, huge or non-finite scale: exact path
-        bool tie = !(sc >= 0x1p-126f && sc <= 0x1p125f);
-        // Codes are packed four to a word as they are made, so only the packed words stay live.
-        uint32_t packed[E / 4];
-#pragma unroll
-        for (int k = 0; k < E; k += 4) {
-            uint32_t c0, c1, c2, c3;
-            fast_codes2(pair_at<InT>(w, k), rcp2, c0, c1, tie);
-            fast_codes2(pair_at<InT>(w, k + 2), rcp2, c2, c3, tie);
-            packed[k / 4] = pack_low_bytes(c0, c1, c2, c3);
-        }
-        if (tie) {  // rare: reload the lane's input (keeps the fast path's registers free)
-            const char* xp = reinterpret_cast<const char*>(
-                reinterpret_cast<const InT*>(p.x) + t * p.x_t + h * p.x_h + lane * E);
-#pragma unroll
-            for (int v = 0; v < V; ++v) ld_stream_v8(xp + 32 * v, w + 8 * v);
-#pragma unroll
-            for (int k = 0; k < E; k += 4) {
-                const float2 x0 = pair_at<InT>(w, k), x1 = pair_at<InT>(w, k + 2);
-                packed[k / 4] = pack_low_bytes(code_byte(x0.x, sc), code_byte(x0.y, sc),
-                                               code_byte(x1.x, sc), code_byte(x1.y, sc));
-            }
-        }
-        int8_t* qp = p.q + t * p.q_t + h * p.q_h + lane * E;
-        if constexpr (E >= 32) {
-#pragma unroll
-            for (int c = 0; c < E / 32; ++c)
-                st_v8(qp + 32 * c, *reinterpret_cast<const uint32_t(*)[8]>(packed + 8 * c));
-        } else if constexpr (E == 16) {
-            st_v4(qp, make_uint4(packed[0], packed[1], packed[2], packed[3]));
-        } else {
-            st_v2(qp, make_uint2(packed[0], packed[1]));
-        }
-        if (lane == 0) {
-            ScaleT* sp = reinterpret_cast<ScaleT*>(p.s) + t * p.s_t + h * p.s_h;
-            if constexpr (kF16Scale)
-                *sp = __float2half_rn(sc);
-            else
-                *sp = sc;
-        }
+        if (active) convert_store<InT, ScaleT, V>(p, w, m, t, h, lane);
     }
 }
 

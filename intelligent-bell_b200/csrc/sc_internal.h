@@ -67,4 +67,11 @@ struct PagedArgs {
 
 int32_t launch_paged(const PagedArgs& a);
 
+// Load the kernels the pipeline launches (paged restore; quantize with fp16 scales) on the
+// current device now.  CUDA loads a kernel's module lazily at its first launch, and that
+// load waits for the device to go idle, which would make a first restore or offload enqueued
+// behind other work block the host.
+cudaError_t preload_paged_kernels();
+cudaError_t preload_quantize_kernels();
+
 }  // namespace sc

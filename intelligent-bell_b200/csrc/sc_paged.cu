@@ -237,6 +237,15 @@ cudaError_t launch(const PagedParams& p, cudaStream_t stream) {
 
 }  // namespace
 
+cudaError_t preload_paged_kernels() {
+    cudaFuncAttributes attr;
+    cudaError_t e = cudaFuncGetAttributes(&attr, paged_restore<__half, true>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__half, false>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__nv_bfloat16, true>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__nv_bfloat16, false>);
+    return e;
+}
+
 int32_t launch_paged(const PagedArgs& a) {
     if (a.n_requests < 0 || a.max_pages < 0 || a.page_size <= 0 || a.n_heads <= 0 ||
         a.n_pool_pages < 0)

@@ -211,8 +211,19 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
     void* ptr = nullptr;
     const unsigned slab_flags = cudaHostAllocPortable |
                                 ((flags & SC_PIPE_WRITE_COMBINED) ? cudaHostAllocWriteCombined : 0u);
+    // Host-side fault injection for tests: with SC_FAILPOINT_HOST_ALLOC=k set, the k-th pinned
+    // allocation of this call reports failure (the error and clean-up paths run as for a real
+    // cudaHostAlloc failure).
+    const char* fp = getenv("SC_FAILPOINT_HOST_ALLOC");
+    const int fail_at = fp ? atoi(fp) : 0;
+    int n_alloc = 0;
     auto halloc = [&](size_t bytes, void** dst, unsigned hflags) {
+        *dst = nullptr;  // a failed allocation must not leave the previous address behind
         if (e != cudaSuccess) return;
+        if (++n_alloc == fail_at) {
+            e = cudaErrorMemoryAllocation;
+            return;
+        }
         e = cudaHostAlloc(dst, bytes, hflags);
         if (e == cudaSuccess) memset(*dst, 0, bytes);  // first touch on the bound thread
     };
@@ -256,6 +267,8 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
         e = cudaMemcpy(p->d_table, ident.data(), sizeof(int32_t) * ident.size(),
                        cudaMemcpyHostToDevice);
     }
+    if (e == cudaSuccess) e = sc::preload_paged_kernels();
+    if (e == cudaSuccess) e = sc::preload_quantize_kernels();
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->transfer, cudaStreamNonBlocking);
     for (int s = 0; s < n_slots && e == cudaSuccess; ++s) {
         cudaEvent_t a = nullptr, b = nullptr;

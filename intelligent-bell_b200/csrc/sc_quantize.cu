@@ -315,7 +315,25 @@ cudaError_t launch_quant_s(const QuantParams& p, int v, bool f16_scale, cudaStre
     return f16_scale ? launch_quant<InT, __half>(p, v, s) : launch_quant<InT, float>(p, v, s);
 }
 
+template <typename InT>
+cudaError_t preload_quant_in() {
+    cudaFuncAttributes attr;
+    cudaError_t e = cudaFuncGetAttributes(&attr, quant_vec<InT, __half, 1>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, quant_vec<InT, __half, 2>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, quant_vec<InT, __half, 4>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, quant_generic<InT, __half>);
+    return e;
+}
+
 }  // namespace
+
+cudaError_t preload_quantize_kernels() {
+    cudaError_t e = preload_quant_in<__half>();
+    if (e == cudaSuccess) e = preload_quant_in<__nv_bfloat16>();
+    if (e == cudaSuccess) e = preload_quant_in<float>();
+    return e;
+}
+
 }  // namespace sc
 
 using namespace sc;

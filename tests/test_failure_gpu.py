@@ -1,0 +1,133 @@
+"""Failure handling and stream ordering of the restore pipeline, with the failures made on
+the host (nothing here faults, traps or hangs the GPU):
+
+* a pinned-allocation failure (host failpoint ``SC_FAILPOINT_HOST_ALLOC``) is reported as an
+  error, cleans up what was allocated, and leaves the library usable;
+* a stalled stream (torch's bounded ``_sleep`` kernel ahead of the restore) does not block the
+  enqueue (the pipeline loads its kernels at creation) and makes
+  ``synchronize`` with a short deadline raise ``TimeoutError``; a later wait completes and the
+  results are right;
+* stream hazards: back-to-back restores and offloads that reuse the staging slots, the shift
+  metadata and the offload slots, with random GPU-side delays on the compute stream and random
+  host delays between enqueues, all checked against the oracle.
+"""
+
+from __future__ import annotations
+
+import os
+import random
+import time
+
+import pytest
+import torch
+
+from conftest import bits_equal
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0) if torch.cuda.is_available() else None
+CYCLES_PER_MS = 2_000_000  # the sleep kernel counts SM clock cycles (about 2 GHz)
+
+
+def _fill(pipe, seed):
+    g = torch.Generator().manual_seed(seed)
+    for t in (pipe.k_quant, pipe.v_quant):
+        t.copy_(torch.randint(-127, 128, tuple(t.shape), generator=g, dtype=torch.int8))
+    for t in (pipe.k_scale, pipe.v_scale):
+        t.copy_((torch.rand(tuple(t.shape), generator=g) * 0.05 + 1e-3).half())
+
+
+def _check_layers(oracle, pipe, k_out, v_out, ids, dps, theta=10000.0):
+    for layer in range(pipe.num_layers):
+        kr, vr = oracle.restore_blocks(pipe.k_quant[layer], pipe.k_scale[layer], pipe.v_quant[layer],
+                                       pipe.v_scale[layer], ids, dps, theta, k_out[layer].dtype)
+        torch.testing.assert_close(k_out[layer].cpu().float(), kr.float(), rtol=1e-2, atol=1e-2)
+        assert bits_equal(v_out[layer].cpu(), vr), layer
+
+
+@pytest.mark.parametrize("fail_at", [1, 2, 3])
+def test_pinned_allocation_failure_is_reported_and_cleaned_up(scb, fail_at):
+    from speccache_b200.cache import KVRestorePipeline
+
+    os.environ["SC_FAILPOINT_HOST_ALLOC"] = str(fail_at)
+    try:
+        with pytest.raises(RuntimeError, match="cudaHostAlloc"):
+            KVRestorePipeline(2, 4, 16, 2, 128, device=DEV)
+    finally:
+        del os.environ["SC_FAILPOINT_HOST_ALLOC"]
+    with KVRestorePipeline(2, 4, 16, 2, 128, device=DEV) as pipe:  # the library still works
+        assert pipe.k_quant.shape == (2, 4, 16, 2, 128)
+
+
+def test_synchronize_times_out_on_a_stalled_stream(scb, oracle):
+    from speccache_b200.cache import KVRestorePipeline
+
+    layers, blocks, chunk, h, d = 3, 6, 32, 4, 128
+    with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV) as pipe:
+        _fill(pipe, 3)
+        ids, dps = [5, 0, 1], [-50, 7, 7]
+        k_out = torch.empty((layers, len(ids) * chunk, h, d), dtype=torch.bfloat16, device=DEV)
+        v_out = torch.empty_like(k_out)
+        torch.cuda._sleep(1000 * CYCLES_PER_MS)  # about one second of bounded delay
+        # the pipeline loaded its kernels when it was created, so this first restore is
+        # enqueued without waiting for the device (a lazy module load at the first launch
+        # would block until the delay is over)
+        t0 = time.perf_counter()
+        pipe.restore(ids, dps, list(k_out), list(v_out))
+        assert time.perf_counter() - t0 < 0.3
+        with pytest.raises(TimeoutError):
+            pipe.synchronize(timeout=0.05)
+        pipe.synchronize(timeout=60.0)
+        assert pipe.status() == 0
+        _check_layers(oracle, pipe, k_out, v_out, ids, dps)
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_stream_hazards_under_random_delays(scb, oracle, seed):
+    from speccache_b200.cache import KVRestorePipeline
+
+    rng = random.Random(seed)
+    layers, blocks, chunk, h, d = 6, 12, 32, 4, 128
+    with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV, n_slots=2) as pipe:
+        _fill(pipe, 10 + seed)
+        jobs = []
+        for _ in range(4):  # restores that reuse the slots and the shift metadata
+            ids = rng.sample(range(blocks), rng.randint(1, 8))
+            dps = [rng.randint(-5000, 5000) for _ in ids]
+            k_out = torch.empty((layers, len(ids) * chunk, h, d), dtype=torch.float16, device=DEV)
+            v_out = torch.empty_like(k_out)
+            torch.cuda._sleep(rng.randint(0, 50) * CYCLES_PER_MS // 10)
+            pipe.restore(ids, dps, list(k_out), list(v_out))
+            time.sleep(rng.random() * 0.005)
+            jobs.append((ids, dps, k_out, v_out))
+        # the slabs as the restores read them (the offloads below overwrite other blocks)
+        snapshot = [t.clone() for t in (pipe.k_quant, pipe.k_scale, pipe.v_quant, pipe.v_scale)]
+        # offloads that reuse both offload slots, each after a delay on the compute stream,
+        # then a restore of the offloaded blocks, ordered after them on the transfer stream
+        g = torch.Generator().manual_seed(seed)
+        off_ids = [blocks - 2, blocks - 1]
+        fresh = []
+        for layer in range(layers):
+            k = torch.randn((len(off_ids) * chunk, h, d), generator=g).half()
+            v = torch.randn((len(off_ids) * chunk, h, d), generator=g).half()
+            torch.cuda._sleep(rng.randint(0, 20) * CYCLES_PER_MS // 10)
+            pipe.offload(layer, off_ids, k.to(DEV), v.to(DEV))
+            fresh.append((k, v))
+        k_back = torch.empty((layers, len(off_ids) * chunk, h, d), dtype=torch.float16, device=DEV)
+        v_back = torch.empty_like(k_back)
+        pipe.restore(off_ids, [0, 0], list(k_back), list(v_back))
+        pipe.synchronize(timeout=60.0)
+        assert pipe.status() == 0
+        kq_s, ks_s, vq_s, vs_s = snapshot
+        for ids, dps, k_out, v_out in jobs:
+            for layer in range(layers):
+                kr, vr = oracle.restore_blocks(kq_s[layer], ks_s[layer], vq_s[layer], vs_s[layer],
+                                               ids, dps, 10000.0, torch.float16)
+                torch.testing.assert_close(k_out[layer].cpu().float(), kr.float(), rtol=1e-2, atol=1e-2)
+                assert bits_equal(v_out[layer].cpu(), vr)
+        for layer, (k, v) in enumerate(fresh):
+            kq, ks = oracle.quantize_kv_int8(k)
+            vq, vs = oracle.quantize_kv_int8(v)
+            assert bits_equal(v_back[layer].cpu(), oracle.dequant_value(vq, vs))
+            c, s = oracle.compute_rope_cos_sin_delta(0, d)
+            assert bits_equal(k_back[layer].cpu(), oracle.dequant_rope_shift(kq, ks, c, s))

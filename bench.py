@@ -330,11 +330,11 @@ def cpu_step_fn(workload: str, cfg: dict):
         f"1 of {cfg['layers']} layers (T={t}, H={h}, D={d}, K shift + V dequant)")
 
 
-def cpu_baseline(workload: str, cfg: dict, budget_s: float = 10.0) -> dict:
+def cpu_baseline(workload: str, cfg: dict, time_limit_s: float = 10.0) -> dict:
     torch.set_num_threads(os.cpu_count() or 1)
     fn, nbytes, what = cpu_step_fn(workload, cfg)
     times = []
-    t_end = time.perf_counter() + budget_s
+    t_end = time.perf_counter() + time_limit_s
     while len(times) < 5 or (time.perf_counter() < t_end and len(times) < 200):
         t0 = time.perf_counter()
         fn()

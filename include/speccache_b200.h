@@ -59,7 +59,7 @@ typedef enum sc_status {
     SC_ERR_OUT_OF_RANGE = 4,     /* a device-side index check tripped (page id, length)    */
     SC_ERR_TIMEOUT = 5,          /* a bounded wait ran out                                 */
     SC_ERR_HOST_ALLOC = 6,       /* pinned host allocation failed                          */
-    SC_ERR_UNSUPPORTED = 7       /* valid request this build does not implement            */
+    SC_ERR_UNSUPPORTED = 7       /* valid request the library does not implement           */
 } sc_status;
 
 /* Element type codes. */

@@ -298,7 +298,7 @@ SC_API int32_t sc_pipeline_status(sc_pipeline* p, int32_t* status_bits);
 SC_API int32_t sc_pipeline_destroy(sc_pipeline* p);
 
 /*
- * Sharing a device buffer between the processes of one box (CUDA IPC), for the gather of
+ * Sharing a device buffer between the processes of one machine (CUDA IPC), for the gather of
  * head shards onto one GPU: the owner exports the buffer, each other rank imports it and
  * passes the returned pointer (plus its shard's head offset) as the output of its restore,
  * so its kernel stores the shard into the owner's memory over NVLink.  No counterpart in

@@ -1,4 +1,4 @@
-"""KV-head sharding across the GPUs of one box.
+"""KV-head sharding across the GPUs of one machine.
 
 KV heads are independent in the dequant and in the RoPE rotation, so the restore shards
 by head with no exchange: GPU ``rank`` of ``world_size`` restores heads

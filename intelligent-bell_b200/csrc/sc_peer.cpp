@@ -1,4 +1,4 @@
-// sc_peer.cpp — share a GPU buffer with the other processes of one box (CUDA IPC), so that
+// sc_peer.cpp — share a GPU buffer with the other processes of one machine (CUDA IPC), so that
 // each GPU's restore kernel can store its KV-head shard straight into one consumer GPU's
 // cache over NVLink (a gather with no separate collective and no staging copy).
 //

@@ -84,6 +84,12 @@ SC_API const char* sc_last_error(void);
 /* SC_ABI_VERSION of the loaded library. */
 SC_API int32_t sc_abi_version(void);
 
+/* Load every kernel of the library on the current device now.  CUDA loads a kernel's module
+ * lazily at its first launch, and that load waits for the device to go idle, so a first call
+ * enqueued behind running work would block the calling thread until that work ends; call this
+ * once per device at start-up to avoid it (sc_pipeline_create does it for its own kernels). */
+SC_API int32_t sc_preload_kernels(void);
+
 /*
  * cos/sin tables for relative RoPE shifts.
  * Replaces compute_rope_cos_sin_delta (speccache/kernels/reference.py:122-165).

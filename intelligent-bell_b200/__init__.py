@@ -40,11 +40,27 @@ from .kernels import (
 
 __version__ = "0.1.0"
 
+
+def preload(device=None) -> None:
+    """Load every kernel of the library on ``device`` (default: the current device) now.
+
+    CUDA loads a kernel's module at its first launch, and that load waits for the device to
+    go idle: a first call enqueued behind running work would block until the work ends.  Call
+    this once per GPU at start-up (``KVRestorePipeline`` does it for its own kernels).
+    """
+    import torch
+
+    lib = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        _lib.check(lib.sc_preload_kernels(), "sc_preload_kernels")
+
 _sys.modules.setdefault("speccache_b200", _sys.modules[__name__])
 
 __all__ = [
     "LIB_PATH",
     "build_library",
+    "preload",
     "compute_rope_cos_sin_delta",
     "dequant_and_rope_key",
     "dequant_kv_cache",

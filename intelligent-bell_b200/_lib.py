@@ -51,6 +51,7 @@ _vp, _i32, _i64, _u32, _f32, _f64 = (ctypes.c_void_p, ctypes.c_int32, ctypes.c_i
 _SIGNATURES = {
     "sc_last_error": (ctypes.c_char_p, []),
     "sc_abi_version": (_i32, []),
+    "sc_preload_kernels": (_i32, []),
     "sc_rope_cos_sin_delta": (_i32, [_vp, _i64, _i32, _f64, _vp, _vp, _vp, _i32, _vp]),
     "sc_dequant_rope_kv": (_i32, [_i32, _i64, _i32, _i32,
                                   _vp, _vp, _vp, _vp,   # k_quant, kq_strides, k_scale, ks_strides

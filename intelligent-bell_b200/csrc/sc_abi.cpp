@@ -71,4 +71,13 @@ const char* sc_last_error(void) { return sc::g_last_error; }
 
 int32_t sc_abi_version(void) { return SC_ABI_VERSION; }
 
+int32_t sc_preload_kernels(void) {
+    cudaError_t e = sc::preload_dense_kernels();
+    if (e == cudaSuccess) e = sc::preload_paged_kernels();
+    if (e == cudaSuccess) e = sc::preload_quantize_kernels(true);
+    if (e == cudaSuccess) e = sc::preload_shift_kernels();
+    if (e != cudaSuccess) return sc::cuda_error(e, "loading the kernels");
+    return sc::ok();
+}
+
 }  // extern "C"

@@ -72,6 +72,8 @@ int32_t launch_paged(const PagedArgs& a);
 // load waits for the device to go idle, which would make a first restore or offload enqueued
 // behind other work block the host.
 cudaError_t preload_paged_kernels();
-cudaError_t preload_quantize_kernels();
+cudaError_t preload_quantize_kernels(bool f32_scales);  // fp16-scale kernels, + fp32 if asked
+cudaError_t preload_dense_kernels();
+cudaError_t preload_shift_kernels();
 
 }  // namespace sc

@@ -268,7 +268,7 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
                        cudaMemcpyHostToDevice);
     }
     if (e == cudaSuccess) e = sc::preload_paged_kernels();
-    if (e == cudaSuccess) e = sc::preload_quantize_kernels();
+    if (e == cudaSuccess) e = sc::preload_quantize_kernels(false);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->transfer, cudaStreamNonBlocking);
     for (int s = 0; s < n_slots && e == cudaSuccess; ++s) {
         cudaEvent_t a = nullptr, b = nullptr;

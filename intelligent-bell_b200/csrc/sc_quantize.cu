@@ -315,22 +315,27 @@ cudaError_t launch_quant_s(const QuantParams& p, int v, bool f16_scale, cudaStre
     return f16_scale ? launch_quant<InT, __half>(p, v, s) : launch_quant<InT, float>(p, v, s);
 }
 
-template <typename InT>
+template <typename InT, typename ScaleT>
 cudaError_t preload_quant_in() {
     cudaFuncAttributes attr;
-    cudaError_t e = cudaFuncGetAttributes(&attr, quant_vec<InT, __half, 1>);
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, quant_vec<InT, __half, 2>);
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, quant_vec<InT, __half, 4>);
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, quant_generic<InT, __half>);
+    cudaError_t e = cudaFuncGetAttributes(&attr, quant_vec<InT, ScaleT, 1>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, quant_vec<InT, ScaleT, 2>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, quant_vec<InT, ScaleT, 4>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, quant_generic<InT, ScaleT>);
     return e;
 }
 
 }  // namespace
 
-cudaError_t preload_quantize_kernels() {
-    cudaError_t e = preload_quant_in<__half>();
-    if (e == cudaSuccess) e = preload_quant_in<__nv_bfloat16>();
-    if (e == cudaSuccess) e = preload_quant_in<float>();
+cudaError_t preload_quantize_kernels(bool f32_scales) {
+    cudaError_t e = preload_quant_in<__half, __half>();
+    if (e == cudaSuccess) e = preload_quant_in<__nv_bfloat16, __half>();
+    if (e == cudaSuccess) e = preload_quant_in<float, __half>();
+    if (f32_scales) {
+        if (e == cudaSuccess) e = preload_quant_in<__half, float>();
+        if (e == cudaSuccess) e = preload_quant_in<__nv_bfloat16, float>();
+        if (e == cudaSuccess) e = preload_quant_in<float, float>();
+    }
     return e;
 }
 

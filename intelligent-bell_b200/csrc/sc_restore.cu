@@ -410,7 +410,37 @@ cudaError_t dispatch(const DenseParams& p, const GenericStrides& g, bool vec, bo
                : launch_generic<OutT, ScaleT, false>(p, g, stream);
 }
 
+template <typename K>
+cudaError_t load_kernel(K kern) {
+    cudaFuncAttributes attr;
+    return cudaFuncGetAttributes(&attr, kern);
+}
+
+template <typename OutT, typename ScaleT>
+cudaError_t preload_dense_ts() {
+    cudaError_t e = load_kernel(dense_restore_vec<OutT, ScaleT, true, kCsCopied>);
+    if (e == cudaSuccess) e = load_kernel(dense_restore_vec<OutT, ScaleT, false, kCsCopied>);
+    if (e == cudaSuccess) e = load_kernel(dense_restore_vec<OutT, ScaleT, true, kCsDevice>);
+    if (e == cudaSuccess) e = load_kernel(dense_restore_vec<OutT, ScaleT, false, kCsDevice>);
+    if (e == cudaSuccess) e = load_kernel(dense_restore_vec<OutT, ScaleT, true, kCsToken>);
+    if (e == cudaSuccess) e = load_kernel(dense_restore_vec<OutT, ScaleT, false, kCsToken>);
+    if (e == cudaSuccess) e = load_kernel(dense_restore_generic<OutT, ScaleT, true>);
+    if (e == cudaSuccess) e = load_kernel(dense_restore_generic<OutT, ScaleT, false>);
+    return e;
+}
+
 }  // namespace
+
+cudaError_t preload_dense_kernels() {
+    cudaError_t e = preload_dense_ts<__half, __half>();
+    if (e == cudaSuccess) e = preload_dense_ts<__half, float>();
+    if (e == cudaSuccess) e = preload_dense_ts<__nv_bfloat16, __half>();
+    if (e == cudaSuccess) e = preload_dense_ts<__nv_bfloat16, float>();
+    if (e == cudaSuccess) e = load_kernel(rope_table_kernel<__half>);
+    if (e == cudaSuccess) e = load_kernel(rope_table_kernel<__nv_bfloat16>);
+    if (e == cudaSuccess) e = load_kernel(rope_table_kernel<float>);
+    return e;
+}
 
 void host_cos_sin_table(int head_dim, float dp, double theta, const float* inv_freq,
                         uint32_t* tab) {

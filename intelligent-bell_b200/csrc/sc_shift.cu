@@ -151,7 +151,24 @@ cudaError_t launch_shift_in(const ShiftParams& p, int32_t out_dtype, bool vec, c
                                      : launch_shift<InT, __nv_bfloat16>(p, vec, s);
 }
 
+template <typename InT, typename OutT>
+cudaError_t preload_shift_io() {
+    cudaFuncAttributes attr;
+    cudaError_t e = cudaFuncGetAttributes(&attr, shift_vec<InT, OutT>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, shift_generic<InT, OutT>);
+    return e;
+}
+
 }  // namespace
+
+cudaError_t preload_shift_kernels() {
+    cudaError_t e = preload_shift_io<__half, __half>();
+    if (e == cudaSuccess) e = preload_shift_io<__half, __nv_bfloat16>();
+    if (e == cudaSuccess) e = preload_shift_io<__nv_bfloat16, __half>();
+    if (e == cudaSuccess) e = preload_shift_io<__nv_bfloat16, __nv_bfloat16>();
+    return e;
+}
+
 }  // namespace sc
 
 using namespace sc;

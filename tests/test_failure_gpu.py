@@ -7,6 +7,8 @@ the host (nothing here faults, traps or hangs the GPU):
   enqueue (the pipeline loads its kernels at creation) and makes
   ``synchronize`` with a short deadline raise ``TimeoutError``; a later wait completes and the
   results are right;
+* ``preload()`` loads every kernel up front, so a fresh process's first calls enqueued behind
+  running work do not wait for it;
 * stream hazards: back-to-back restores and offloads that reuse the staging slots, the shift
   metadata and the offload slots, with random GPU-side delays on the compute stream and random
   host delays between enqueues, all checked against the oracle.
@@ -80,6 +82,41 @@ def test_synchronize_times_out_on_a_stalled_stream(scb, oracle):
         pipe.synchronize(timeout=60.0)
         assert pipe.status() == 0
         _check_layers(oracle, pipe, k_out, v_out, ids, dps)
+
+
+PRELOAD_SCRIPT = r"""
+import importlib, sys, time, torch
+sys.path.insert(0, sys.argv[1])
+scb = importlib.import_module("intelligent-bell_b200")
+dev = torch.device("cuda", 0)
+torch.cuda.set_device(dev)
+x = torch.randn((64, 8, 128), device=dev).half()
+torch.cuda.synchronize()
+scb.preload()
+torch.cuda._sleep(1_000_000_000)  # about half a second of bounded delay
+t0 = time.perf_counter()
+q, s = scb.quantize_kv_int8(x)
+scb.restore_layers(q[None], s[None], q[None], s[None], delta_p=3)
+scb.dequant_kv_cache(q, s, q, s, delta_p=7)
+scb.rope_shift_keys(x, 5)
+dt = time.perf_counter() - t0
+torch.cuda.synchronize()
+print(f"first calls enqueued in {dt:.4f} s")
+"""
+
+
+def test_preloaded_first_calls_do_not_wait_for_the_device(scb):
+    # a fresh process: its first launches of the library's kernels come after the preload
+    import subprocess
+    import sys
+
+    from conftest import REPO
+
+    out = subprocess.run([sys.executable, "-c", PRELOAD_SCRIPT, REPO], capture_output=True,
+                         text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    dt = float(out.stdout.strip().split()[-2])
+    assert dt < 0.25, out.stdout
 
 
 @pytest.mark.parametrize("seed", [0, 1, 2])

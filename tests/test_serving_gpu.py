@@ -1,9 +1,10 @@
 """GPU tests of the pool, injector, cache sink and offload against the oracle and the
 reference's own injector outputs (golden vectors).
 
-Mirrors tests/test_phase3_serving.py:137-235 (multi-layer shifted injection) and
+Mirrors tests/test_phase3_serving.py:137-235 (multi-layer shifted injection),
 tests/test_phase2_engine.py:297-359 (multi-chunk pipeline parity, through the pool and through
-routing decisions) of the reference.
+routing decisions) and the restore half of tests/test_phase2_engine.py:57-147 (semantic shifted
+hit, delta_p = -384) of the reference.
 K is compared with the reference tolerance (the kernels build cos/sin from delta_p, one
 fp16 ulp apart from torch's tables in rare entries), V bit for bit.
 """
@@ -240,6 +241,40 @@ def test_engine_routing_decisions_multi_chunk_parity(scb, oracle):
         misses = [x for x in decisions if x.status in (S.CACHE_MISS, S.SPECULATIVE_DRAFT)]
         e_k, e_v = engine.execute_async_dma_and_rope(misses)
         assert e_k.shape == (0, h, d) and e_v.dtype == torch.float16 and e_k.device == DEV
+
+
+def test_engine_semantic_shifted_hit(scb, oracle):
+    # reference tests/test_phase2_engine.py:57-147 after routing: a chunk rotated at p = 512,
+    # reused at p = 128 through a SEMANTIC_REUSE decision (delta_p = -384); the routing itself
+    # (radix tree, semantic index) is the reference's and gives this decision
+    from speccache_b200.cache import ChunkRoutingDecision, ChunkRoutingStatus, RestoreEngine
+
+    chunk, heads, d = 128, 8, 128
+    g = torch.Generator().manual_seed(1234)
+    raw_k = torch.randn((chunk, heads, d), generator=g)
+    raw_v = torch.randn((chunk, heads, d), generator=g)
+    c512, s512 = oracle.compute_rope_cos_sin_delta(512, d)
+    cf = torch.cat([c512, c512], -1)[:, None, :].float()
+    sf = torch.cat([s512, s512], -1)[:, None, :].float()
+    k_rot_512 = (raw_k * cf + oracle.rotate_half(raw_k) * sf).to(torch.float16)
+    kq, ks = oracle.quantize_kv_int8(k_rot_512)
+    vq, vs = oracle.quantize_kv_int8(raw_v)
+    with RestoreEngine(chunk_size=chunk, num_kv_heads=heads, head_dim=d, max_blocks=16,
+                       device=DEV) as engine:
+        bid = engine.register_chunk(range(1000, 1000 + chunk), 512, kq, ks, vq, vs)
+        dec = ChunkRoutingDecision(0, 128, 128 + chunk, tuple(range(5000, 5000 + chunk)),
+                                   ChunkRoutingStatus.SEMANTIC_REUSE, similarity=0.96,
+                                   block_id=bid, cached_position=512, delta_p=128 - 512)
+        k_out, v_out = engine.execute_async_dma_and_rope([dec])
+        c, s = oracle.compute_rope_cos_sin_delta(-384, d)
+        torch.testing.assert_close(k_out.cpu(), oracle.dequant_rope_shift(kq, ks, c, s),
+                                   atol=1e-2, rtol=1e-2)
+        assert bits_equal(v_out.cpu(), oracle.dequant_value(vq, vs))
+        # and the restored keys are the raw keys rotated at the target position 128
+        c128, s128 = oracle.compute_rope_cos_sin_delta(128, d)
+        k_128 = raw_k * torch.cat([c128, c128], -1)[:, None, :].float() + \
+            oracle.rotate_half(raw_k) * torch.cat([s128, s128], -1)[:, None, :].float()
+        torch.testing.assert_close(k_out.cpu().float(), k_128, atol=5e-2, rtol=5e-2)
 
 
 def test_reconstruct_layer_chunk(scb, oracle):

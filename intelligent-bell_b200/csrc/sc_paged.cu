@@ -35,12 +35,6 @@ constexpr int kPThreads = 256;
 #ifndef SC_PAGED_ROUNDS
 #define SC_PAGED_ROUNDS 2
 #endif
-// The block's metadata loads: each where it is first needed (0); all four (length, page
-// id, output offset, shift) together at the start (1); the length alone, then - once the
-// block knows it has work - the other three together (2).
-#ifndef SC_PAGED_HOIST_META
-#define SC_PAGED_HOIST_META 2
-#endif
 
 // Read-only scalar loads kept in program order (volatile), so that metadata loads issued
 // together are not sunk past the early-exit branches that follow them.
@@ -138,15 +132,8 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
     const int r = static_cast<int>(task / p.max_pages);
     const int pg = static_cast<int>(task - static_cast<int64_t>(r) * p.max_pages);
     const bool reporter = chunk == 0 && threadIdx.x == 0;
-#if SC_PAGED_HOIST_META == 1
-    // All four addresses are in bounds by construction (r < R, pg < max_pages <= stride).
-    const int len = ld_meta(p.seq_lens + r);
-    const int32_t page_id = ld_meta(p.table + static_cast<int64_t>(r) * p.table_stride + pg);
-    const int64_t off = ld_meta(p.out_off + r);
-    const float dp_blk = has_k ? ld_meta(p.dp + (p.dp_per_page ? task : r)) : 0.0f;
-#else
+    // The length alone first: a block past its request's length exits after one load.
     const int len = p.seq_lens[r];
-#endif
     if (len < 0 || static_cast<int64_t>(len) > static_cast<int64_t>(p.max_pages) * p.page) {
         if (reporter && pg == 0) atomicOr(p.status, SC_STATUS_BAD_SEQ_LEN);
         return;
@@ -157,20 +144,15 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
     const int64_t rows = static_cast<int64_t>(n_tok) * p.H;
     const int64_t row_begin = static_cast<int64_t>(chunk) * RB * RT * SC_PAGED_ROUNDS;
     if (row_begin >= rows) return;
-#if SC_PAGED_HOIST_META == 2
+    // Page id, output offset and shift together: one memory latency for the three (all in
+    // bounds: r < R, pg < max_pages <= table stride).
     const int32_t page_id = ld_meta(p.table + static_cast<int64_t>(r) * p.table_stride + pg);
     const int64_t off = ld_meta(p.out_off + r);
     const float dp_blk = has_k ? ld_meta(p.dp + (p.dp_per_page ? task : r)) : 0.0f;
-#elif SC_PAGED_HOIST_META == 0
-    const int32_t page_id = p.table[static_cast<int64_t>(r) * p.table_stride + pg];
-#endif
     if (page_id < 0 || page_id >= p.n_pool_pages) {
         if (reporter) atomicOr(p.status, SC_STATUS_BAD_PAGE_ID);
         return;
     }
-#if SC_PAGED_HOIST_META == 0
-    const int64_t off = p.out_off[r];
-#endif
     {
         // Output range of this page: rows tok0 .. tok0+n_tok-1, heads 0 .. H-1.
         const int64_t first = off + static_cast<int64_t>(tok0) * p.o_t;
@@ -181,11 +163,7 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
             return;
         }
     }
-#if SC_PAGED_HOIST_META
     auto block_dp = [&] { return dp_blk; };
-#else
-    auto block_dp = [&] { return p.dp[p.dp_per_page ? task : r]; };
-#endif
 #if SC_PAGED_TABLE_FIRST
     if (has_k) {
         const float dp = block_dp();

@@ -21,7 +21,7 @@ from conftest import bits_equal
 pytestmark = pytest.mark.gpu
 
 DEV = torch.device("cuda", 0) if torch.cuda.is_available() else None
-SETTINGS = settings(max_examples=40, deadline=None,
+SETTINGS = settings(max_examples=60, deadline=None, derandomize=True,
                     suppress_health_check=[HealthCheck.function_scoped_fixture])
 
 head_dims = st.sampled_from([2, 8, 34, 64, 96, 128, 160, 256])

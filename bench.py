@@ -65,6 +65,8 @@ WORKLOADS = {
                       delta_p=2048, out=torch.float16),
     "llama70b": dict(layers=80, tokens=32768, heads=8, head_dim=128, theta=500000.0,
                      delta_p=8192, out=torch.bfloat16),
+    "keyshift": dict(layers=32, tokens=8192, heads=8, head_dim=128, theta=500000.0,
+                     delta_p=-384, out=torch.float16),
 }
 
 
@@ -76,6 +78,11 @@ def restore_bytes(rows: int, head_dim: int) -> int:
 def quantize_bytes(rows: int, head_dim: int) -> int:
     """Algorithmic bytes of quantizing K and V: 2-byte in, int8 + 2-byte scale out."""
     return 2 * rows * (3 * head_dim + 2)
+
+
+def shift_bytes(rows: int, head_dim: int) -> int:
+    """Algorithmic bytes of shifting dequantised 16-bit keys: 2-byte in, 2-byte out."""
+    return rows * 4 * head_dim
 
 
 def h2d_bytes(rows: int, head_dim: int) -> int:
@@ -98,7 +105,8 @@ def read_profiled_traffic(workload: str) -> float | None:
     """Per-launch DRAM bytes of the workload's dominant kernel, from the committed ncu
     summary (line ``dram_bytes_per_launch_full: <bytes>``); None if not profiled."""
     name = {"llama8b": "dense_restore_llama8b_t8192_ncu.txt",
-            "paged": "paged_restore_ragged64_ncu.txt"}.get(workload)
+            "paged": "paged_restore_ragged64_ncu.txt",
+            "keyshift": "key_shift_llama8b_t8192_ncu.txt"}.get(workload)
     if name is None:
         return None
     try:
@@ -211,9 +219,12 @@ class Dist:
             dist.destroy_process_group()
 
 
-def time_steps(fn, steps: int, warmup: int, dist: Dist, per_step_events: bool = True):
-    """W untimed steps, then K timed steps bracketed by barrier + synchronize; returns
-    (max-over-ranks total ms, per-step ms list of this rank)."""
+def time_steps(fn, steps: int, warmup: int, dist: Dist, per_step_events: bool = False):
+    """W untimed steps, then K timed steps bracketed by barrier + synchronize, with one CUDA
+    event pair around the K steps on the launching stream; returns (max-over-ranks total ms,
+    per-step ms list of this rank).  Per-step ms are total / K unless ``per_step_events`` asks
+    for an event after every step (each adds about 3 us between launches on B200, so the
+    default measures the steps back to back, as a caller runs them)."""
     stream = torch.cuda.current_stream(dist.device)
     for _ in range(warmup):
         fn()
@@ -228,8 +239,9 @@ def time_steps(fn, steps: int, warmup: int, dist: Dist, per_step_events: bool = 
             ev[i + 1].record(stream)
     torch.cuda.synchronize(dist.device)
     dist.barrier()
-    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)] if per_step_events else []
     total = ev[0].elapsed_time(ev[steps])
+    per = ([ev[i].elapsed_time(ev[i + 1]) for i in range(steps)] if per_step_events
+           else [total / steps] * steps)
     return dist.max(total), per
 
 
@@ -304,6 +316,15 @@ def cpu_step_fn(workload: str, cfg: dict):
             f"1 request of mean length {t} of the {cfg['requests']}-request batch "
             f"(H={h}, D={d}, K shift + V dequant)")
     t = cfg["tokens"]
+    if workload == "keyshift":
+        g = torch.Generator().manual_seed(SEED)
+        k = torch.randn((t, h, d), generator=g).to(torch.float16)
+
+        def fn():
+            oracle.apply_rope_shift(k, cfg["delta_p"], cfg["theta"])
+
+        return fn, shift_bytes(t * h, d), (
+            f"1 of {cfg['layers']} layers (T={t}, H={h}, D={d}: RoPE shift of fp16 keys)")
     if workload == "roundtrip":
         g = torch.Generator().manual_seed(SEED)
         xk = torch.randn((t, h, d), generator=g).to(torch.float16)
@@ -404,6 +425,14 @@ def workload_config(workload: str, cfg: dict, world: int, gather: bool = False) 
                 "kv_heads": cfg["heads"], "head_dim": cfg["head_dim"], "theta": cfg["theta"],
                 "delta_p": cfg["delta_p"], "parallelism": f"replicas x{world} (weak)",
                 "l2": "3.4 GB per step > L2 (no flush needed)"}
+    if workload == "keyshift":
+        return {"workload": "llama3-8b key shift: dequantised fp16 keys of 32 layers, T=8192, "
+                            "8 KV heads x 128, delta_p -384, theta=5e5 (the injector's "
+                            "apply_rope_shift), one launch", "layers": cfg["layers"],
+                "seq_len": cfg["tokens"], "kv_heads": cfg["heads"], "head_dim": cfg["head_dim"],
+                "delta_p": cfg["delta_p"], "theta": cfg["theta"],
+                "parallelism": f"replicas x{world} (weak)",
+                "l2": "1.07 GB per step > L2 (no flush needed)"}
     return {"workload": "llama3-70b KV restore from pinned host: 80 layers, T=32768, 8 KV heads "
                         "x 128 sharded over the GPUs, delta_p 8192, theta=5e5, bf16"
                         + ("; all heads gathered on GPU 0" if gather else ""),
@@ -471,7 +500,7 @@ def bench_llama8b(args, scb, dist: Dist, cfg: dict):
             tail[0].copy_(k_out[layers - 1, t - 1], non_blocking=True)
             tail[1].copy_(v_out[layers - 1, t - 1], non_blocking=True)
 
-        e2e_ms, _ = time_steps(e2e_step, args.steps, args.warmup, dist, per_step_events=False)
+        e2e_ms, _ = time_steps(e2e_step, args.steps, args.warmup, dist)
         # one restore on its own (latency, nothing overlapping it)
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -530,7 +559,7 @@ def bench_paged(args, scb, dist: Dist, cfg: dict):
         tail[0].copy_(k_out[total - 1], non_blocking=True)
         tail[1].copy_(v_out[total - 1], non_blocking=True)
 
-    e2e_ms, _ = time_steps(e2e_step, args.steps, args.warmup, dist, per_step_events=False)
+    e2e_ms, _ = time_steps(e2e_step, args.steps, args.warmup, dist)
     h2d = sum(x.numel() * x.element_size() for x in hosts)
     line["e2e"] = e2e_line(nbytes, e2e_ms, args.steps, dist.world, h2d,
                            tail.numel() * tail.element_size(), args.steps,
@@ -582,7 +611,7 @@ def bench_roundtrip(args, scb, dist: Dist, cfg: dict):
         tail[0].copy_(k_out[layers - 1, t - 1], non_blocking=True)
         tail[1].copy_(v_out[layers - 1, t - 1], non_blocking=True)
 
-    e2e_ms, _ = time_steps(e2e_step, args.steps, args.warmup, dist, per_step_events=False)
+    e2e_ms, _ = time_steps(e2e_step, args.steps, args.warmup, dist)
     line["e2e"] = e2e_line(nbytes, e2e_ms, args.steps, dist.world,
                            2 * hk.numel() * hk.element_size(), tail.numel() * tail.element_size(),
                            3 * args.steps, "fp16 K/V H2D from pinned host, quantize, restore")
@@ -604,7 +633,7 @@ def offload_line(args, dist: Dist, xk: torch.Tensor, xv: torch.Tensor) -> dict:
                 pipe.offload(layer, ids, xk[layer], xv[layer])
             pipe.join()
 
-        ms, _ = time_steps(step, args.steps, args.warmup, dist, per_step_events=False)
+        ms, _ = time_steps(step, args.steps, args.warmup, dist)
     rows = layers * t * h
     d2h = 2 * rows * (d + 2)  # int8 codes and fp16 scales of K and V
     return {"ms_per_step": ms / args.steps,
@@ -612,6 +641,40 @@ def offload_line(args, dist: Dist, xk: torch.Tensor, xv: torch.Tensor) -> dict:
             "quantize_gbs": quantize_bytes(rows, d) * dist.world * args.steps / (ms / 1e3) / 1e9,
             "d2h_bytes_per_step": d2h, "gpu_launches": 2 * layers * args.steps,
             "path": "quantize on the GPU into a staging slot, 2-D D2H copies into the pinned slabs"}
+
+
+def bench_keyshift(args, scb, dist: Dist, cfg: dict):
+    layers = args.layers if args.layers != WORKLOADS["llama8b"]["layers"] else cfg["layers"]
+    t, h, d = cfg["tokens"], cfg["heads"], cfg["head_dim"]
+    gen = torch.Generator(device=dist.device)
+    gen.manual_seed(SEED + dist.rank)
+    k = torch.randn((layers * t, h, d), generator=gen, device=dist.device).to(torch.float16)
+    out = torch.empty_like(k)
+    rows = layers * t * h
+    nbytes = shift_bytes(rows, d)
+
+    def step():
+        scb.rope_shift_keys(k, cfg["delta_p"], theta=cfg["theta"], out=out)
+
+    total_ms, per = time_steps(step, args.steps, args.warmup, dist)
+    line = {"value": nbytes * dist.world * args.steps / (total_ms / 1e3) / 1e9,
+            "ms_per_step": total_ms / args.steps, "roofline": roofline(nbytes, per, "keyshift"),
+            "gpu_launches": args.steps}
+    if args.skip_e2e:
+        return line
+    hk = k.cpu().pin_memory()
+    tail = torch.empty((1, h, d), dtype=torch.float16).pin_memory()
+
+    def e2e_step():
+        k.copy_(hk, non_blocking=True)
+        step()
+        tail.copy_(out[-1:], non_blocking=True)
+
+    e2e_ms, _ = time_steps(e2e_step, args.steps, args.warmup, dist)
+    line["e2e"] = e2e_line(nbytes, e2e_ms, args.steps, dist.world, hk.numel() * hk.element_size(),
+                           tail.numel() * tail.element_size(), args.steps,
+                           "fp16 keys H2D from pinned host, then sc_rope_shift_keys")
+    return line
 
 
 def bench_llama70b(args, scb, dist: Dist, cfg: dict):
@@ -663,7 +726,7 @@ def bench_llama70b(args, scb, dist: Dist, cfg: dict):
                 tail[0].copy_(k_out[layers - 1, t - 1, :h], non_blocking=True)
                 tail[1].copy_(v_out[layers - 1, t - 1, :h], non_blocking=True)
 
-        total_ms, _ = time_steps(step, args.steps, args.warmup, dist, per_step_events=False)
+        total_ms, _ = time_steps(step, args.steps, args.warmup, dist)
         status = pipe.status()
         if gather is not None:
             dist.barrier()  # the owner's buffers stay alive until every writer is done
@@ -685,7 +748,7 @@ def run_ours(args) -> None:
     scb = importlib.import_module("intelligent-bell_b200")
     cfg = WORKLOADS[args.workload]
     fn = {"llama8b": bench_llama8b, "paged": bench_paged, "roundtrip": bench_roundtrip,
-          "llama70b": bench_llama70b}[args.workload]
+          "llama70b": bench_llama70b, "keyshift": bench_keyshift}[args.workload]
     with ClockSampler(dist.device.index or 0) as clocks:
         part = fn(args, scb, dist, cfg)
     if dist.rank == 0:
@@ -693,7 +756,8 @@ def run_ours(args) -> None:
                 "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": part.pop("ms_per_step"), "higher_is_better": True,
                 "scaling": part.pop("scaling", "weak"), "vs_baseline": None,
-                "dtype": "int8 in, fp32 math, " + str(cfg["out"]).replace("torch.", "") + " out",
+                "dtype": ("fp16" if args.workload == "keyshift" else "int8") + " in, fp32 math, "
+                         + str(cfg["out"]).replace("torch.", "") + " out",
                 "data": "synthetic: seeded, see config",
                 "config": workload_config(args.workload, cfg, dist.world, args.gather)}
         line.update(part)
@@ -712,8 +776,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama8b")
     ap.add_argument("--layers", type=int, default=WORKLOADS["llama8b"]["layers"],
-                    help="llama8b layers per step (32 = the workload; fewer only for "
-                         "profiling captures)")
+                    help="llama8b / keyshift layers per step (32 = the workload; fewer only "
+                         "for profiling captures)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling aid: kernel leg only")
     ap.add_argument("--skip-cpu-baseline", action="store_true", help="profiling aid")
     ap.add_argument("--write-combined", action="store_true",

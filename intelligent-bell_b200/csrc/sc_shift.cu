@@ -10,8 +10,8 @@
 // with each product and the sum rounded separately (no contraction), so the result equals
 // the reference's bit for bit given the same tables, subnormal products included.
 //
-// Vector path: a thread owns 8 frequencies of one (token, head) row: two 16-byte loads (the
-// slice and its rotate-half partner), 16 outputs, two 16-byte stores; one-shot blocks.  The
+// Vector path: a thread owns F = 16 (or 8) frequencies of one (token, head) row: two 32-byte
+// (16-byte) loads - the slice and its rotate-half partner - and two stores; one-shot blocks.  The
 // table of a host-side shift travels in the kernel parameters and is copied to shared
 // memory; device tables ([1 | T, D/2] fp16) are read per row.  Generic path: one thread per
 // (row, frequency), any strides.  A thread reads both halves before writing them, so the
@@ -22,10 +22,14 @@ namespace sc {
 namespace {
 
 constexpr int kSThreads = 256;
+// Widest vector slice (frequencies per thread) the launcher may pick: 16 or 8.
+#ifndef SC_SHIFT_MAX_F
+#define SC_SHIFT_MAX_F 16
+#endif
 
 struct ShiftParams {
     int32_t rows;  // n_tokens * n_heads (< 2^31)
-    int32_t H, D, S;  // S = (D / 2) / 8 slices of 8 frequencies per row (vector path)
+    int32_t H, D, S;  // S = (D / 2) / F slices of F frequencies per row (vector path)
     FastDiv divH, divS;
     const void* x;
     int64_t x_t, x_h, x_d;
@@ -54,8 +58,38 @@ __device__ __forceinline__ void shift_pair(float x1, float x2, float c, float s,
     o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
 }
 
-template <typename InT, typename OutT>
+// 16 consecutive 16-bit values (32 bytes, 32-byte aligned).  A plain (coherent) load: the
+// shift may run in place.
+__device__ __forceinline__ void ld_v8(const void* p, uint32_t* w) {
+    asm volatile("ld.global.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]),
+                   "=r"(w[6]), "=r"(w[7])
+                 : "l"(p));
+}
+
+// F consecutive 16-bit values (F = 8: one 16-byte access, F = 16: one 32-byte access).
+template <int F>
+__device__ __forceinline__ void load_f(const void* p, uint32_t* w) {
+    if constexpr (F == 16) {
+        ld_v8(p, w);
+    } else {
+        const uint4 v = *reinterpret_cast<const uint4*>(p);
+        w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
+    }
+}
+
+template <int F>
+__device__ __forceinline__ void store_f(void* p, uint32_t* w) {
+    if constexpr (F == 16) {
+        st_v8(p, *reinterpret_cast<const uint32_t(*)[8]>(w));
+    } else {
+        *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+template <typename InT, typename OutT, int F>
 __global__ void __launch_bounds__(kSThreads) shift_vec(const __grid_constant__ ShiftParams p) {
+    constexpr int NW = F / 2;  // 32-bit words per half-slice
     __shared__ float s_cos[kMaxHeadDim / 2];
     __shared__ float s_sin[kMaxHeadDim / 2];
     const int half = p.D >> 1;
@@ -73,40 +107,39 @@ __global__ void __launch_bounds__(kSThreads) shift_vec(const __grid_constant__ S
     const int j = static_cast<int>(static_cast<uint32_t>(w) - row * static_cast<uint32_t>(p.S));
     const uint32_t t = fdiv(row, p.divH);
     const int64_t h = static_cast<int64_t>(row) - static_cast<int64_t>(t) * p.H;
-    const int f0 = j * 8;
+    const int f0 = j * F;
     const InT* xp = reinterpret_cast<const InT*>(p.x) + t * p.x_t + h * p.x_h + f0;
-    const uint4 a = *reinterpret_cast<const uint4*>(xp);
-    const uint4 b = *reinterpret_cast<const uint4*>(xp + half);
-    float c[8], s[8];
-    if (p.cos == nullptr) {
+    uint32_t aw[NW], bw[NW];
+    load_f<F>(xp, aw);
+    load_f<F>(xp + half, bw);
+    uint32_t cw[NW], sw[NW];
+    if (p.cos != nullptr) {
+        load_f<F>(p.cos + t * p.cs_t + f0, cw);
+        load_f<F>(p.sin + t * p.cs_t + f0, sw);
+    }
+    uint32_t lo[NW], hi[NW];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) c[k] = s_cos[f0 + k], s[k] = s_sin[f0 + k];
-    } else {
-        const uint4 cv = *reinterpret_cast<const uint4*>(p.cos + t * p.cs_t + f0);
-        const uint4 sv = *reinterpret_cast<const uint4*>(p.sin + t * p.cs_t + f0);
-        const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, sw[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < NW; ++k) {
+        float c0, c1, s0, s1;
+        if (p.cos == nullptr) {
+            c0 = s_cos[f0 + 2 * k], c1 = s_cos[f0 + 2 * k + 1];
+            s0 = s_sin[f0 + 2 * k], s1 = s_sin[f0 + 2 * k + 1];
+        } else {
             const float2 cc = __half22float2(bit_cast_u32<__half2>(cw[k]));
             const float2 ss = __half22float2(bit_cast_u32<__half2>(sw[k]));
-            c[2 * k] = cc.x, c[2 * k + 1] = cc.y, s[2 * k] = ss.x, s[2 * k + 1] = ss.y;
+            c0 = cc.x, c1 = cc.y, s0 = ss.x, s1 = ss.y;
         }
-    }
-    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
-    uint32_t lo[4], hi[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
         const InT* ap = reinterpret_cast<const InT*>(&aw[k]);
         const InT* bp = reinterpret_cast<const InT*>(&bw[k]);
         float o1a, o2a, o1b, o2b;
-        shift_pair(to_f(ap[0]), to_f(bp[0]), c[2 * k], s[2 * k], o1a, o2a);
-        shift_pair(to_f(ap[1]), to_f(bp[1]), c[2 * k + 1], s[2 * k + 1], o1b, o2b);
+        shift_pair(to_f(ap[0]), to_f(bp[0]), c0, s0, o1a, o2a);
+        shift_pair(to_f(ap[1]), to_f(bp[1]), c1, s1, o1b, o2b);
         lo[k] = pack2<OutT>(o1a, o1b);
         hi[k] = pack2<OutT>(o2a, o2b);
     }
     OutT* op = reinterpret_cast<OutT*>(p.out) + t * p.o_t + h * p.o_h + f0;
-    *reinterpret_cast<uint4*>(op) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    *reinterpret_cast<uint4*>(op + half) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    store_f<F>(op, lo);
+    store_f<F>(op + half, hi);
 }
 
 template <typename InT, typename OutT>
@@ -134,27 +167,31 @@ __global__ void __launch_bounds__(kSThreads) shift_generic(const __grid_constant
     op[(f + half) * p.o_d] = from_float<OutT>(o2);
 }
 
+// width: frequencies per thread of the vector path (16 or 8), or 0 for the generic path.
 template <typename InT, typename OutT>
-cudaError_t launch_shift(const ShiftParams& p, bool vec, cudaStream_t stream) {
-    const int64_t work = static_cast<int64_t>(p.rows) * (vec ? p.S : p.D / 2);
-    const int64_t blocks = (work + kSThreads - 1) / kSThreads;
-    if (vec)
-        shift_vec<InT, OutT><<<static_cast<unsigned>(blocks), kSThreads, 0, stream>>>(p);
+cudaError_t launch_shift(const ShiftParams& p, int width, cudaStream_t stream) {
+    const int64_t work = static_cast<int64_t>(p.rows) * (width ? p.S : p.D / 2);
+    const unsigned blocks = static_cast<unsigned>((work + kSThreads - 1) / kSThreads);
+    if (width == 16)
+        shift_vec<InT, OutT, 16><<<blocks, kSThreads, 0, stream>>>(p);
+    else if (width == 8)
+        shift_vec<InT, OutT, 8><<<blocks, kSThreads, 0, stream>>>(p);
     else
-        shift_generic<InT, OutT><<<static_cast<unsigned>(blocks), kSThreads, 0, stream>>>(p);
+        shift_generic<InT, OutT><<<blocks, kSThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
 template <typename InT>
-cudaError_t launch_shift_in(const ShiftParams& p, int32_t out_dtype, bool vec, cudaStream_t s) {
-    return out_dtype == SC_DTYPE_F16 ? launch_shift<InT, __half>(p, vec, s)
-                                     : launch_shift<InT, __nv_bfloat16>(p, vec, s);
+cudaError_t launch_shift_in(const ShiftParams& p, int32_t out_dtype, int width, cudaStream_t s) {
+    return out_dtype == SC_DTYPE_F16 ? launch_shift<InT, __half>(p, width, s)
+                                     : launch_shift<InT, __nv_bfloat16>(p, width, s);
 }
 
 template <typename InT, typename OutT>
 cudaError_t preload_shift_io() {
     cudaFuncAttributes attr;
-    cudaError_t e = cudaFuncGetAttributes(&attr, shift_vec<InT, OutT>);
+    cudaError_t e = cudaFuncGetAttributes(&attr, shift_vec<InT, OutT, 16>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, shift_vec<InT, OutT, 8>);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, shift_generic<InT, OutT>);
     return e;
 }
@@ -217,20 +254,27 @@ extern "C" int32_t sc_rope_shift_keys(int64_t n_tokens, int32_t n_heads, int32_t
     } else {
         host_cos_sin_table(head_dim, static_cast<float>(delta_p), theta_base, inv_freq, p.tab);
     }
-    // Vector path: 8 frequencies per thread, 16-byte aligned slices of x, out and the tables.
+    // Vector path: 16 (or 8) frequencies per thread, 32-byte (16-byte) aligned slices of x,
+    // out and the tables; otherwise the generic path.
     const int half = head_dim / 2;
-    auto al = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
-    auto st8 = [](int64_t st, int64_t size) { return size <= 1 || st % 8 == 0; };
-    bool vec = half % 8 == 0 && p.x_d == 1 && p.o_d == 1 && al(x) && al(out) &&
-               st8(p.x_t, n_tokens) && st8(p.x_h, n_heads) && st8(p.o_t, n_tokens) &&
-               st8(p.o_h, n_heads);
-    if (vec && cos_delta)
-        vec = p.cs_d == 1 && al(cos_delta) && al(sin_delta) && st8(p.cs_t, n_tokens);
-    p.S = half / 8 > 0 ? half / 8 : 1;
+    auto fits = [&](int f) {
+        const int bytes = 2 * f;
+        auto al = [&](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) % bytes) == 0; };
+        auto st = [&](int64_t stride, int64_t size) { return size <= 1 || stride % f == 0; };
+        bool ok = half % f == 0 && p.x_d == 1 && p.o_d == 1 && al(x) && al(out) &&
+                  st(p.x_t, n_tokens) && st(p.x_h, n_heads) && st(p.o_t, n_tokens) &&
+                  st(p.o_h, n_heads);
+        if (ok && cos_delta)
+            ok = p.cs_d == 1 && al(cos_delta) && al(sin_delta) && st(p.cs_t, n_tokens);
+        return ok;
+    };
+    const int width = SC_SHIFT_MAX_F >= 16 && fits(16) ? 16 : (fits(8) ? 8 : 0);
+    p.S = width ? half / width : 1;
     p.divS = make_fastdiv(static_cast<uint32_t>(p.S));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const cudaError_t e = x_dtype == SC_DTYPE_F16 ? launch_shift_in<__half>(p, out_dtype, vec, s)
-                                                  : launch_shift_in<__nv_bfloat16>(p, out_dtype, vec, s);
+    const cudaError_t e = x_dtype == SC_DTYPE_F16
+                              ? launch_shift_in<__half>(p, out_dtype, width, s)
+                              : launch_shift_in<__nv_bfloat16>(p, out_dtype, width, s);
     if (e != cudaSuccess) return cuda_error(e, "key shift launch");
     return ok();
 }

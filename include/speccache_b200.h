@@ -238,13 +238,17 @@ SC_API int32_t sc_restore_paged(int32_t n_requests, int32_t max_pages, int32_t p
  * ids, the scales of every layer (one 2-D copy), then for each layer the K and V codes (one
  * 2-D copy of two rows) into one of n_slots device staging slots, and runs the restore kernel
  * for that layer on compute_stream once its copy event has fired, so layer l+1's copy
- * overlaps layer l's kernel.
+ * overlaps layer l's kernel.  A small restore (K and V codes of all layers within 64 MiB) is
+ * instead copied with one 3-D copy per run and restored by one launch for all layers, which
+ * saves the per-layer launches and events (unless SC_PIPE_PER_LAYER is set).
  */
 typedef struct sc_pipeline sc_pipeline;
 
 #define SC_PIPE_NUMA_LOCAL 0x1u /* allocate the slabs from a thread bound to the GPU's NUMA node */
 #define SC_PIPE_WRITE_COMBINED 0x2u /* pin the slabs write-combined: faster DMA reads on some
                                        hosts, very slow host reads (write-only use) */
+#define SC_PIPE_PER_LAYER 0x4u /* always restore layer by layer (no all-layers launch for small
+                                  restores); for comparisons and tests */
 
 SC_API int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t n_blocks,
                            int32_t chunk_size, int32_t n_heads, int32_t head_dim,

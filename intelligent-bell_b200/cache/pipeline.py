@@ -41,12 +41,16 @@ class KVRestorePipeline:
         numa_local: allocate the slabs from a thread bound to the GPU's NUMA node.
         write_combined: pin the slabs write-combined (host writes and GPU reads only; host
             reads of the slab views become very slow).
+        per_layer: always restore layer by layer; by default a small restore (K and V codes
+            of all layers within 64 MiB) is copied with one 3-D copy per run of blocks and
+            restored by one launch for all layers.
     """
 
     def __init__(self, num_layers: int, num_blocks: int, chunk_size: int, num_kv_heads: int,
                  head_dim: int, *, device: torch.device | str | int | None = None,
                  max_restore_blocks: int | None = None, n_slots: int = 2,
-                 numa_local: bool = True, write_combined: bool = False) -> None:
+                 numa_local: bool = True, write_combined: bool = False,
+                 per_layer: bool = False) -> None:
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device())
         device = torch.device(device if not isinstance(device, int) else f"cuda:{device}")
@@ -61,7 +65,8 @@ class KVRestorePipeline:
         self._lib = _lib.load()
         handle = ctypes.c_void_p()
         flags = (_lib.SC_PIPE_NUMA_LOCAL if numa_local else 0) | (
-            _lib.SC_PIPE_WRITE_COMBINED if write_combined else 0)
+            _lib.SC_PIPE_WRITE_COMBINED if write_combined else 0) | (
+            _lib.SC_PIPE_PER_LAYER if per_layer else 0)
         rc = self._lib.sc_pipeline_create(device.index, self.num_layers, self.num_blocks,
                                           self.chunk_size, self.num_kv_heads, self.head_dim,
                                           self.max_restore_blocks, int(n_slots), flags,

@@ -56,6 +56,10 @@ struct PagedArgs {
     const float* inv_freq;  // host, may be null
     void* k_out;
     void* v_out;
+    // Per-request output buffers (device arrays of n_requests addresses, 32-byte aligned); when
+    // given, request r writes from offset 0 of its own buffers and out_offsets is not read.
+    const uint64_t* k_out_ptrs;
+    const uint64_t* v_out_ptrs;
     const int64_t* out_offsets;
     int64_t out_strides[3];
     int64_t out_numel;

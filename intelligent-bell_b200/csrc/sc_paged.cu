@@ -70,6 +70,8 @@ struct PagedParams {
     int32_t dp_per_page;
     void* ko;
     void* vo;
+    const uint64_t* ko_ptrs;  // per-request output buffers (device), or null: ko/vo + out_off
+    const uint64_t* vo_ptrs;
     const int64_t* out_off;
     int64_t o_t, o_h;
     int64_t out_numel;
@@ -147,7 +149,15 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
     // Page id, output offset and shift together: one memory latency for the three (all in
     // bounds: r < R, pg < max_pages <= table stride).
     const int32_t page_id = ld_meta(p.table + static_cast<int64_t>(r) * p.table_stride + pg);
-    const int64_t off = ld_meta(p.out_off + r);
+    void* ko = p.ko;
+    void* vo = p.vo;
+    int64_t off = 0;
+    if (p.ko_ptrs != nullptr) {  // request r writes its own buffers from offset 0
+        if (has_k) ko = reinterpret_cast<void*>(ld_meta(reinterpret_cast<const int64_t*>(p.ko_ptrs) + r));
+        if (has_v) vo = reinterpret_cast<void*>(ld_meta(reinterpret_cast<const int64_t*>(p.vo_ptrs) + r));
+    } else {
+        off = ld_meta(p.out_off + r);
+    }
     const float dp_blk = has_k ? ld_meta(p.dp + (p.dp_per_page ? task : r)) : 0.0f;
     if (page_id < 0 || page_id >= p.n_pool_pages) {
         if (reporter) atomicOr(p.status, SC_STATUS_BAD_PAGE_ID);
@@ -158,7 +168,9 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
         const int64_t first = off + static_cast<int64_t>(tok0) * p.o_t;
         const int64_t last = first + static_cast<int64_t>(n_tok - 1) * p.o_t +
                              static_cast<int64_t>(p.H - 1) * p.o_h + p.D;
-        if ((off & 15) != 0 || first < 0 || last > p.out_numel || p.o_t < 0 || p.o_h < 0) {
+        const bool misaligned = ((reinterpret_cast<uintptr_t>(ko) | reinterpret_cast<uintptr_t>(vo)) & 31) != 0;
+        if ((off & 15) != 0 || misaligned || first < 0 || last > p.out_numel || p.o_t < 0 ||
+            p.o_h < 0) {
             if (reporter) atomicOr(p.status, SC_STATUS_BAD_OUT_OFFSET);
             return;
         }
@@ -193,11 +205,11 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
         if (buf[k].row < 0) continue;
         const int64_t oo = page_out_offset(p, buf[k].row, j, off, tok0);
         if (has_k) {
-            OutT* o = reinterpret_cast<OutT*>(p.ko) + oo;
+            OutT* o = reinterpret_cast<OutT*>(ko) + oo;
             rope_slice_store<OutT, __half, X16>(buf[k].ka, buf[k].kb, buf[k].ksc, cs, o, o + half);
         }
         if (has_v) {
-            OutT* o = reinterpret_cast<OutT*>(p.vo) + oo;
+            OutT* o = reinterpret_cast<OutT*>(vo) + oo;
             value_slice_store<OutT, __half>(buf[k].va, buf[k].vsc, o);
             value_slice_store<OutT, __half>(buf[k].vb, buf[k].vsc, o + half);
         }
@@ -238,9 +250,12 @@ int32_t launch_paged(const PagedArgs& a) {
     if (a.n_requests == 0 || a.max_pages == 0) return ok();
     const bool has_k = a.pool_kq != nullptr, has_v = a.pool_vq != nullptr;
     if (!has_k && !has_v) return set_error(SC_ERR_INVALID_ARGUMENT, "neither K nor V given");
-    if ((has_k && (!a.pool_ks || !a.k_out)) || (has_v && (!a.pool_vs || !a.v_out)))
+    const bool ptrs = a.k_out_ptrs != nullptr || a.v_out_ptrs != nullptr;
+    if ((has_k && (!a.pool_ks || !(ptrs ? a.k_out_ptrs : a.k_out))) ||
+        (has_v && (!a.pool_vs || !(ptrs ? a.v_out_ptrs : a.v_out))))
         return set_error(SC_ERR_INVALID_ARGUMENT, "pool tensor given without scale or output");
-    if (!a.page_table || !a.seq_lens || !a.out_offsets || !a.status || (has_k && !a.delta_p))
+    if (!a.page_table || !a.seq_lens || (!ptrs && !a.out_offsets) || !a.status ||
+        (has_k && !a.delta_p))
         return set_error(SC_ERR_INVALID_ARGUMENT, "null page table / lengths / offsets / status");
     if (a.page_table_stride < a.max_pages)
         return set_error(SC_ERR_INVALID_ARGUMENT, "page_table_stride %lld < max_pages %d",
@@ -249,8 +264,8 @@ int32_t launch_paged(const PagedArgs& a) {
         return set_error(SC_ERR_INVALID_ARGUMENT,
                          "output strides must be [t, h, 1] with t, h multiples of 16 elements");
     auto al = [](const void* ptr, uintptr_t n) { return (reinterpret_cast<uintptr_t>(ptr) % n) == 0; };
-    if ((has_k && (!al(a.pool_kq, 16) || !al(a.k_out, 32))) ||
-        (has_v && (!al(a.pool_vq, 16) || !al(a.v_out, 32))))
+    if ((has_k && (!al(a.pool_kq, 16) || (!ptrs && !al(a.k_out, 32)))) ||
+        (has_v && (!al(a.pool_vq, 16) || (!ptrs && !al(a.v_out, 32)))))
         return set_error(SC_ERR_INVALID_ARGUMENT,
                          "pools must be 16-byte and outputs 32-byte aligned");
     if (static_cast<int64_t>(a.page_size) * a.n_heads >= (int64_t(1) << 31))
@@ -284,6 +299,8 @@ int32_t launch_paged(const PagedArgs& a) {
     p.dp_per_page = a.delta_p_per_page;
     p.ko = a.k_out;
     p.vo = a.v_out;
+    p.ko_ptrs = a.k_out_ptrs;
+    p.vo_ptrs = a.v_out_ptrs;
     p.out_off = a.out_offsets;
     p.o_t = a.out_strides[0];
     p.o_h = a.out_strides[1];

@@ -38,6 +38,12 @@ struct Meta {  // one upload per restore: identity-table length and per-block sh
     float delta_p[1];  // [max_restore_blocks]
 };
 
+// Staging for the all-layers mode: a restore whose K and V codes over all layers fit here is
+// copied with one 3-D copy per run of blocks and restored by one kernel launch (per-layer
+// launches and events cost about 8 us of host time per layer, more than the copies of a
+// restore of a few blocks take).
+constexpr size_t kAllLayerBytes = size_t(64) << 20;
+
 size_t meta_bytes(int64_t max_blocks) {
     return sizeof(Meta) + sizeof(float) * static_cast<size_t>(max_blocks > 1 ? max_blocks - 1 : 0);
 }
@@ -123,6 +129,16 @@ struct sc_pipeline {
     std::vector<bool> slot_used;
     cudaEvent_t meta_uploaded = nullptr, done = nullptr;
     bool any_restore = false;
+    // all-layers mode (small restores): K and V codes of every layer in one staging buffer
+    // [2][L][n][block], one 3-D copy per run, one kernel launch with one request per layer
+    int8_t* d_all = nullptr;
+    int64_t all_cap_pages = 0;  // capacity in (layer, block) pages; 0 = mode unavailable
+    bool codes_3d = false;
+    uint8_t* h_all_meta = nullptr;  // seq[L] | dps[all_cap_pages] | k_out[L] | v_out[L]
+    uint8_t* d_all_meta = nullptr;
+    size_t all_meta_bytes = 0, off_dps = 0, off_kp = 0, off_vp = 0;
+    cudaEvent_t all_meta_uploaded = nullptr;
+    bool any_all = false;
     // offload: quantize into one of two device staging slots (K then V codes in one
     // allocation, K then V scales in another), then D2H into the slabs
     int8_t* o_codes[2] = {nullptr, nullptr};
@@ -145,6 +161,10 @@ void release(sc_pipeline* p) {
     for (auto e : p->slot_free) cudaEventDestroy(e);
     if (p->any_offload && p->o_free[p->o_last]) cudaEventSynchronize(p->o_free[p->o_last]);
     if (p->meta_uploaded) cudaEventDestroy(p->meta_uploaded);
+    if (p->all_meta_uploaded) cudaEventDestroy(p->all_meta_uploaded);
+    cudaFree(p->d_all);
+    cudaFree(p->d_all_meta);
+    cudaFreeHost(p->h_all_meta);
     if (p->done) cudaEventDestroy(p->done);
     for (int s = 0; s < 2; ++s) {
         if (p->o_ready[s]) cudaEventDestroy(p->o_ready[s]);
@@ -256,14 +276,38 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
         p->codes_2d = slab_codes <= mp && stage_codes <= mp;
         p->scales_2d = static_cast<size_t>(n_blocks) * row * 2 <= mp && stage_scales * 2 <= mp;
         p->offload_scales_2d = slab_scales * 2 <= mp && stage_scales * 2 <= mp;
+        // all-layers mode: up to kAllLayerBytes of K and V codes staged for one launch
+        const size_t blk_codes = row * head_dim;
+        int64_t cap = static_cast<int64_t>(kAllLayerBytes / (2 * blk_codes));
+        if (cap > static_cast<int64_t>(n_layers) * max_restore_blocks)
+            cap = static_cast<int64_t>(n_layers) * max_restore_blocks;
+        const int64_t max_n = cap / n_layers;  // blocks per restore the mode can take
+        p->codes_3d = static_cast<size_t>(n_blocks) * blk_codes <= mp &&
+                      static_cast<size_t>(max_n) * blk_codes <= mp;
+        if (!(flags & SC_PIPE_PER_LAYER) && max_n >= 1 && p->codes_3d &&
+            static_cast<size_t>(n_blocks) * row * 2 <= mp) {
+            p->all_cap_pages = max_n * n_layers;
+            p->off_dps = (static_cast<size_t>(n_layers) * 4 + 7) / 8 * 8;
+            p->off_kp = p->off_dps + (static_cast<size_t>(p->all_cap_pages) * 4 + 7) / 8 * 8;
+            p->off_vp = p->off_kp + static_cast<size_t>(n_layers) * 8;
+            p->all_meta_bytes = p->off_vp + static_cast<size_t>(n_layers) * 8;
+            e = cudaMalloc(&p->d_all, 2 * static_cast<size_t>(p->all_cap_pages) * blk_codes);
+            if (e == cudaSuccess) e = cudaMalloc(&p->d_all_meta, p->all_meta_bytes);
+            if (e == cudaSuccess)
+                e = cudaHostAlloc(&p->h_all_meta, p->all_meta_bytes, cudaHostAllocPortable);
+            if (e == cudaSuccess)
+                e = cudaEventCreateWithFlags(&p->all_meta_uploaded, cudaEventDisableTiming);
+        }
     }
-    if (e == cudaSuccess) e = cudaMalloc(&p->d_table, sizeof(int32_t) * max_restore_blocks);
+    const int64_t table_len = p->all_cap_pages > max_restore_blocks ? p->all_cap_pages
+                                                                     : max_restore_blocks;
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_table, sizeof(int32_t) * table_len);
     if (e == cudaSuccess) e = cudaMalloc(&p->d_meta, meta_bytes(max_restore_blocks));
     if (e == cudaSuccess) e = cudaMalloc(&p->d_status, sizeof(int32_t));
     if (e == cudaSuccess) e = cudaMemset(p->d_status, 0, sizeof(int32_t));
     if (e == cudaSuccess) {
-        std::vector<int32_t> ident(static_cast<size_t>(max_restore_blocks));
-        for (int64_t i = 0; i < max_restore_blocks; ++i) ident[i] = static_cast<int32_t>(i);
+        std::vector<int32_t> ident(static_cast<size_t>(table_len));
+        for (int64_t i = 0; i < table_len; ++i) ident[i] = static_cast<int32_t>(i);
         e = cudaMemcpy(p->d_table, ident.data(), sizeof(int32_t) * ident.size(),
                        cudaMemcpyHostToDevice);
     }
@@ -303,6 +347,105 @@ extern "C" int32_t sc_pipeline_host_slabs(const sc_pipeline* p, int8_t** k_quant
     return sc::ok();
 }
 
+namespace {
+
+// All-layers mode: every layer of the restore in one staging buffer and one launch, the
+// layers being the requests of one paged restore (request l writes layer l's outputs).
+int32_t restore_all_layers(sc_pipeline* p, const int32_t* block_ids, const int32_t* delta_ps,
+                           int32_t n, double theta_base, const float* inv_freq,
+                           void* const* k_out, void* const* v_out, const int64_t* out_strides,
+                           int64_t out_numel, int32_t out_dtype, cudaStream_t cs) {
+    const int L = p->L;
+    for (int l = 0; l < L; ++l)
+        if (((reinterpret_cast<uintptr_t>(k_out[l]) | reinterpret_cast<uintptr_t>(v_out[l])) & 31) != 0)
+            return set_error(SC_ERR_INVALID_ARGUMENT, "outputs must be 32-byte aligned (layer %d)", l);
+    const size_t row = static_cast<size_t>(p->chunk) * p->H;
+    const size_t blk_codes = row * p->D, blk_scales = row;
+    const size_t pages = static_cast<size_t>(L) * n;
+    cudaError_t e = cudaSuccess;
+    // The host metadata may still feed the previous all-layers upload.
+    if (p->any_all) e = cudaEventSynchronize(p->all_meta_uploaded);
+    if (e != cudaSuccess) return cuda_error(e, "waiting for the previous metadata upload");
+    int32_t* seq = reinterpret_cast<int32_t*>(p->h_all_meta);
+    float* dps = reinterpret_cast<float*>(p->h_all_meta + p->off_dps);
+    uint64_t* kp = reinterpret_cast<uint64_t*>(p->h_all_meta + p->off_kp);
+    uint64_t* vp = reinterpret_cast<uint64_t*>(p->h_all_meta + p->off_vp);
+    for (int l = 0; l < L; ++l) {
+        seq[l] = n * p->chunk;
+        kp[l] = reinterpret_cast<uint64_t>(k_out[l]);
+        vp[l] = reinterpret_cast<uint64_t>(v_out[l]);
+        for (int32_t i = 0; i < n; ++i) dps[static_cast<size_t>(l) * n + i] = static_cast<float>(delta_ps[i]);
+    }
+    // The staging, the scales and the metadata on the device may still be read by the
+    // previous restore's kernels.
+    if (p->any_restore) e = cudaStreamWaitEvent(p->transfer, p->done, 0);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(p->d_all_meta, p->h_all_meta, p->all_meta_bytes, cudaMemcpyHostToDevice,
+                            p->transfer);
+    if (e == cudaSuccess) e = cudaEventRecord(p->all_meta_uploaded, p->transfer);
+    if (e != cudaSuccess) return cuda_error(e, "metadata upload");
+    // Per run of consecutive blocks: K and V codes of every layer with one 3-D copy (rows:
+    // layers at the slab's layer pitch; slices: K then V), packed [2][L][n][block] on the
+    // device; the scales of every layer with one 2-D copy, packed [2][L][n][chunk * H].
+    const size_t src_pitch = static_cast<size_t>(p->B) * blk_codes;
+    for (int32_t i = 0; i < n && e == cudaSuccess;) {
+        int32_t rn = 1;
+        while (i + rn < n && block_ids[i + rn] == block_ids[i] + rn) ++rn;
+        const size_t b0 = static_cast<size_t>(block_ids[i]);
+        cudaMemcpy3DParms m = {};
+        m.srcPtr = make_cudaPitchedPtr(p->h_kq + b0 * blk_codes, src_pitch, rn * blk_codes, L);
+        m.dstPtr = make_cudaPitchedPtr(p->d_all + static_cast<size_t>(i) * blk_codes,
+                                       static_cast<size_t>(n) * blk_codes, rn * blk_codes, L);
+        m.extent = make_cudaExtent(rn * blk_codes, L, 2);
+        m.kind = cudaMemcpyHostToDevice;
+        e = cudaMemcpy3DAsync(&m, p->transfer);
+        if (e == cudaSuccess)
+            e = cudaMemcpy2DAsync(p->d_sc + static_cast<size_t>(i) * blk_scales,
+                                  static_cast<size_t>(n) * blk_scales * 2,
+                                  p->h_ks + b0 * blk_scales, static_cast<size_t>(p->B) * blk_scales * 2,
+                                  rn * blk_scales * 2, 2 * static_cast<size_t>(L),
+                                  cudaMemcpyHostToDevice, p->transfer);
+        i += rn;
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(p->ready[0], p->transfer);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, p->ready[0], 0);
+    if (e != cudaSuccess) return cuda_error(e, "all-layers copies");
+    sc::PagedArgs a{};
+    a.n_requests = L;
+    a.max_pages = n;
+    a.page_size = p->chunk;
+    a.n_heads = p->H;
+    a.head_dim = p->D;
+    a.n_pool_pages = static_cast<int64_t>(pages);
+    a.pool_kq = p->d_all;
+    a.pool_vq = p->d_all + pages * blk_codes;
+    a.pool_ks = p->d_sc;
+    a.pool_vs = p->d_sc + pages * blk_scales;
+    a.page_table = p->d_table;  // identity: page i of request l is page l * n + i
+    a.page_table_stride = n;
+    a.seq_lens = reinterpret_cast<const int32_t*>(p->d_all_meta);
+    a.delta_p = reinterpret_cast<const float*>(p->d_all_meta + p->off_dps);
+    a.delta_p_per_page = 1;
+    a.theta_base = theta_base;
+    a.inv_freq = inv_freq;
+    a.k_out_ptrs = reinterpret_cast<const uint64_t*>(p->d_all_meta + p->off_kp);
+    a.v_out_ptrs = reinterpret_cast<const uint64_t*>(p->d_all_meta + p->off_vp);
+    for (int i = 0; i < 3; ++i) a.out_strides[i] = out_strides[i];
+    a.out_numel = out_numel;
+    a.out_dtype = out_dtype;
+    a.status = p->d_status;
+    a.stream = cs;
+    const int32_t rc = sc::launch_paged(a);
+    if (rc != SC_OK) return rc;
+    e = cudaEventRecord(p->done, cs);
+    if (e != cudaSuccess) return cuda_error(e, "restore enqueue");
+    p->any_restore = true;
+    p->any_all = true;
+    return sc::ok();
+}
+
+}  // namespace
+
 extern "C" int32_t sc_pipeline_restore(sc_pipeline* p, const int32_t* block_ids,
                                        const int32_t* delta_ps, int32_t n_blocks,
                                        double theta_base, const float* inv_freq,
@@ -326,6 +469,9 @@ extern "C" int32_t sc_pipeline_restore(sc_pipeline* p, const int32_t* block_ids,
     DeviceGuard g(p->device);
     if (!g.ok) return set_error(SC_ERR_CUDA, "cudaSetDevice(%d) failed", p->device);
     cudaStream_t cs = static_cast<cudaStream_t>(compute_stream);
+    if (static_cast<int64_t>(p->L) * n_blocks <= p->all_cap_pages)
+        return restore_all_layers(p, block_ids, delta_ps, n_blocks, theta_base, inv_freq, k_out,
+                                  v_out, out_strides, out_numel, out_dtype, cs);
     cudaError_t e = cudaSuccess;
 
     // Metadata: the host buffer may still feed the previous restore's upload.

@@ -145,6 +145,50 @@ def test_offload_then_restore_round_trip(scb, oracle):
     inj.close()
 
 
+@pytest.mark.parametrize("n_blocks", [1, 3, 7])
+def test_all_layers_restore_equals_per_layer(scb, oracle, n_blocks):
+    # a small restore takes the all-layers path (one 3-D copy per run, one launch); it must
+    # write exactly what the layer-by-layer path writes, scattered and consecutive blocks alike
+    from speccache_b200.cache import KVRestorePipeline
+
+    layers, blocks, chunk, h, d = 5, 12, 32, 4, 128
+    g = torch.Generator().manual_seed(40 + n_blocks)
+    ids = torch.randperm(blocks, generator=g)[:n_blocks].tolist()
+    if n_blocks == 7:
+        ids = [2, 3, 4, 9, 10, 0, 1]  # runs of consecutive ids and a jump back
+    dps = torch.randint(-3000, 3000, (n_blocks,), generator=g).tolist()
+    outs = []
+    for per_layer in (False, True):
+        with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV, per_layer=per_layer) as pipe:
+            g2 = torch.Generator().manual_seed(99)
+            for t in (pipe.k_quant, pipe.v_quant):
+                t.copy_(torch.randint(-127, 128, tuple(t.shape), generator=g2, dtype=torch.int8))
+            for t in (pipe.k_scale, pipe.v_scale):
+                t.copy_((torch.rand(tuple(t.shape), generator=g2) * 0.05 + 1e-3).half())
+            # model-layout outputs: [1, H, Tmax, D] per layer, separate allocations
+            kc = [torch.zeros((1, h, 256, d), dtype=torch.bfloat16, device=DEV) for _ in range(layers)]
+            vc = [torch.zeros_like(x) for x in kc]
+            n_tok = n_blocks * chunk
+            pipe.restore(ids, dps, [x[0, :, 16:16 + n_tok].permute(1, 0, 2) for x in kc],
+                         [x[0, :, 16:16 + n_tok].permute(1, 0, 2) for x in vc], theta=5e5)
+            pipe.synchronize()
+            assert pipe.status() == 0
+            outs.append(([x.cpu() for x in kc], [x.cpu() for x in vc]))
+            if not per_layer:
+                for layer in range(layers):
+                    kr, vr = oracle.restore_blocks(pipe.k_quant[layer], pipe.k_scale[layer],
+                                                   pipe.v_quant[layer], pipe.v_scale[layer], ids, dps,
+                                                   5e5, torch.bfloat16)
+                    got_v = outs[0][1][layer][0, :, 16:16 + n_tok].permute(1, 0, 2)
+                    assert bits_equal(got_v.contiguous(), vr)
+                    got_k = outs[0][0][layer][0, :, 16:16 + n_tok].permute(1, 0, 2)
+                    torch.testing.assert_close(got_k.float(), kr.float(), rtol=1e-2, atol=1e-2)
+                    assert not outs[0][0][layer][0, :, :16].any()  # nothing written before
+    for layer in range(layers):
+        assert bits_equal(outs[0][0][layer], outs[1][0][layer])
+        assert bits_equal(outs[0][1][layer], outs[1][1][layer])
+
+
 def test_offload_staging_ring_and_join(scb, oracle):
     # successive offloads alternate two staging slots (the third reuses the first); join makes
     # the current stream wait for their copies on the GPU, after which the slabs hold the

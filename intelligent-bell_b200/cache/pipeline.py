@@ -63,6 +63,7 @@ class KVRestorePipeline:
         self.chunk_size, self.num_kv_heads, self.head_dim = int(chunk_size), int(num_kv_heads), int(head_dim)
         self.max_restore_blocks = int(max_restore_blocks or num_blocks)
         self._lib = _lib.load()
+        self._ptr_arrays: dict[tuple, ctypes.Array] = {}
         handle = ctypes.c_void_p()
         flags = (_lib.SC_PIPE_NUMA_LOCAL if numa_local else 0) | (
             _lib.SC_PIPE_WRITE_COMBINED if write_combined else 0) | (
@@ -93,35 +94,54 @@ class KVRestorePipeline:
         self.v_scale[layer, block_id].copy_(v_scale)
 
     # -- restore --------------------------------------------------------------------------
-    def restore(self, block_ids, delta_ps, k_out: list[torch.Tensor], v_out: list[torch.Tensor],
-                *, theta: float = 10000.0) -> None:
+    def restore(self, block_ids, delta_ps, k_out, v_out, *, theta: float = 10000.0) -> None:
         """Enqueue the restore of ``block_ids`` (block i shifted by ``delta_ps[i]``) for
-        every layer.  ``k_out[l]`` / ``v_out[l]`` are ``[n*chunk, H, D]`` fp16/bf16 views
-        (any token/head strides, unit dim stride) that all share one layout.  Completion is
-        ordered on the current CUDA stream; nothing blocks."""
+        every layer.  ``k_out`` / ``v_out``: a list of ``num_layers`` ``[n*chunk, H, D]``
+        fp16/bf16 views (any token/head strides, unit dim stride) sharing one layout, or one
+        ``[num_layers, n*chunk, H, D]`` tensor.  The kernels write only inside these views.
+        Completion is ordered on the current CUDA stream; nothing blocks."""
         ids = np.ascontiguousarray(np.asarray(block_ids, dtype=np.int32).reshape(-1))
         dps = np.ascontiguousarray(np.asarray(delta_ps, dtype=np.int64).reshape(-1))
         if ids.size != dps.size:
             raise ValueError(f"{ids.size} block ids but {dps.size} shifts")
-        if np.any(np.abs(dps) >= 2**31):
-            raise ValueError("shifts must fit in int32")
         dps32 = dps.astype(np.int32)
-        if len(k_out) != self.num_layers or len(v_out) != self.num_layers:
-            raise ValueError(f"need {self.num_layers} K and V outputs")
-        n_tok = ids.size * self.chunk_size
-        ref = k_out[0]
-        if ref.dtype not in (torch.float16, torch.bfloat16):
-            raise TypeError(f"outputs must be float16 or bfloat16, got {ref.dtype}")
-        for o in list(k_out) + list(v_out):
-            if (o.shape != (n_tok, self.num_kv_heads, self.head_dim) or o.stride() != ref.stride()
-                    or o.dtype != ref.dtype or o.device != self.device):
-                raise ValueError(
-                    f"outputs must be [{n_tok}, {self.num_kv_heads}, {self.head_dim}] {ref.dtype} "
-                    f"views on {self.device} sharing one layout")
-        numel = min(o.untyped_storage().nbytes() // o.element_size() - o.storage_offset()
-                    for o in list(k_out) + list(v_out))
-        self._restore(ids, dps32, [o.data_ptr() for o in k_out], [o.data_ptr() for o in v_out],
-                      ref.stride(), numel, ref.dtype, theta)
+        if (dps32 != dps).any():
+            raise ValueError("shifts must fit in int32")
+        shape = (ids.size * self.chunk_size, self.num_kv_heads, self.head_dim)
+        kp, kst, dtype = self._layer_pointers(k_out, shape)
+        vp, vst, vdt = self._layer_pointers(v_out, shape)
+        if vst != kst or vdt != dtype:
+            raise ValueError("K and V outputs must share dtype and layout")
+        # elements from a layer's address to the end of its view (the kernels' write bound)
+        extent = (shape[0] - 1) * kst[0] + (shape[1] - 1) * kst[1] + shape[2]
+        self._restore(ids, dps32, kp, vp, kst, extent, dtype, theta)
+
+    def _layer_pointers(self, out, shape):
+        """Per-layer output addresses, the common [token, head, dim] strides and the dtype."""
+        bad = ValueError(f"outputs must be {self.num_layers} [{shape[0]}, {shape[1]}, {shape[2]}] "
+                         f"float16/bfloat16 views on {self.device} sharing one layout (unit dim "
+                         "stride), or one tensor with a leading layer dimension")
+        dev = self.device.index
+        if isinstance(out, torch.Tensor):  # [L, T, H, D]: checked once
+            if (out.ndim != 4 or tuple(out.shape) != (self.num_layers,) + shape
+                    or out.get_device() != dev or out.stride(3) != 1
+                    or out.dtype not in (torch.float16, torch.bfloat16)):
+                raise bad
+            base, step = out.data_ptr(), out.stride(0) * out.element_size()
+            return (tuple([base + layer * step for layer in range(self.num_layers)]),
+                    tuple(out.stride()[1:]), out.dtype)
+        if len(out) != self.num_layers:
+            raise bad
+        ref = out[0]
+        dtype, st = ref.dtype, ref.stride()
+        if dtype not in (torch.float16, torch.bfloat16) or st[2] != 1:
+            raise bad
+        ptrs = []
+        for o in out:
+            if o.dtype is not dtype or o.shape != shape or o.stride() != st or o.get_device() != dev:
+                raise bad
+            ptrs.append(o.data_ptr())
+        return tuple(ptrs), st, dtype
 
     def restore_into(self, block_ids, delta_ps, k_ptrs: list[int], v_ptrs: list[int],
                      out_strides: tuple[int, int, int], out_numel: int,
@@ -136,19 +156,28 @@ class KVRestorePipeline:
             raise ValueError(f"{ids.size} block ids but {dps.size} shifts")
         if len(k_ptrs) != self.num_layers or len(v_ptrs) != self.num_layers:
             raise ValueError(f"need {self.num_layers} K and V pointers")
-        self._restore(ids, dps.astype(np.int32), list(k_ptrs), list(v_ptrs), tuple(out_strides),
-                      int(out_numel), out_dtype, theta)
+        self._restore(ids, dps.astype(np.int32), tuple(map(int, k_ptrs)), tuple(map(int, v_ptrs)),
+                      tuple(out_strides), int(out_numel), out_dtype, theta)
 
     def _restore(self, ids, dps32, k_ptrs, v_ptrs, strides, numel, dtype, theta) -> None:
         if dtype not in (torch.float16, torch.bfloat16):
             raise TypeError(f"outputs must be float16 or bfloat16, got {dtype}")
-        kp = (ctypes.c_void_p * self.num_layers)(*k_ptrs)
-        vp = (ctypes.c_void_p * self.num_layers)(*v_ptrs)
+        kp, vp = self._pointer_array(k_ptrs), self._pointer_array(v_ptrs)
         rc = self._lib.sc_pipeline_restore(
             self._h, ids.ctypes.data, dps32.ctypes.data, int(ids.size), float(theta),
             _lib.inv_freq_ptr(self.head_dim, theta), kp, vp, _lib.strides(*strides), numel,
             _lib.DTYPE_CODE[dtype], _lib.stream_handle(self.device))
         _lib.check(rc, "sc_pipeline_restore")
+
+    def _pointer_array(self, ptrs: tuple):
+        """The per-layer address array for the C call, kept for outputs seen before (a
+        serving loop restores into the same cache buffers again and again)."""
+        arr = self._ptr_arrays.get(ptrs)
+        if arr is None:
+            if len(self._ptr_arrays) >= 64:
+                self._ptr_arrays.clear()
+            arr = self._ptr_arrays[ptrs] = (ctypes.c_void_p * self.num_layers)(*ptrs)
+        return arr
 
     def offload(self, layer: int, block_ids, k: torch.Tensor, v: torch.Tensor) -> None:
         """Enqueue quantize-on-GPU + D2H of freshly computed K/V into the slabs.

@@ -9,9 +9,9 @@ the host (nothing here faults, traps or hangs the GPU):
   results are right;
 * ``preload()`` loads every kernel up front, so a fresh process's first calls enqueued behind
   running work do not wait for it;
-* stream hazards: back-to-back restores and offloads that reuse the staging slots, the shift
-  metadata and the offload slots, with random GPU-side delays on the compute stream and random
-  host delays between enqueues, all checked against the oracle.
+* stream hazards: back-to-back restores and offloads that reuse the staging slots (or the
+  all-layers staging), the shift metadata and the offload slots, with random GPU-side delays on
+  the compute stream and random host delays between enqueues, all checked against the oracle.
 """
 
 from __future__ import annotations
@@ -119,13 +119,15 @@ def test_preloaded_first_calls_do_not_wait_for_the_device(scb):
     assert dt < 0.25, out.stdout
 
 
+@pytest.mark.parametrize("per_layer", [False, True])
 @pytest.mark.parametrize("seed", [0, 1, 2])
-def test_stream_hazards_under_random_delays(scb, oracle, seed):
+def test_stream_hazards_under_random_delays(scb, oracle, seed, per_layer):
     from speccache_b200.cache import KVRestorePipeline
 
     rng = random.Random(seed)
     layers, blocks, chunk, h, d = 6, 12, 32, 4, 128
-    with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV, n_slots=2) as pipe:
+    with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV, n_slots=2,
+                           per_layer=per_layer) as pipe:
         _fill(pipe, 10 + seed)
         jobs = []
         for _ in range(4):  # restores that reuse the slots and the shift metadata

@@ -327,6 +327,34 @@ def test_paged_bad_entries_are_flagged_not_faulted(scb, oracle):
     assert scb.paged_status(DEV) == 0  # reading cleared it
 
 
+def test_pipeline_restore_into_one_tensor_per_side(scb, oracle):
+    # outputs given as one [L, T, H, D] tensor per side instead of a list of layer views
+    from speccache_b200.cache import KVRestorePipeline
+
+    n_l, n_blocks, chunk, h, d = 4, 8, 32, 2, 128
+    g = torch.Generator().manual_seed(31)
+    with KVRestorePipeline(n_l, n_blocks, chunk, h, d, device=DEV) as pipe:
+        pipe.k_quant.copy_(torch.randint(-127, 128, pipe.k_quant.shape, generator=g, dtype=torch.int8))
+        pipe.v_quant.copy_(torch.randint(-127, 128, pipe.v_quant.shape, generator=g, dtype=torch.int8))
+        pipe.k_scale.fill_(0.01)
+        pipe.v_scale.fill_(0.02)
+        blocks, dps = [6, 7, 1], [5, 5, -40]
+        k4 = torch.empty((n_l, 3 * chunk, h, d), dtype=torch.bfloat16, device=DEV)
+        v4 = torch.empty_like(k4)
+        pipe.restore(blocks, dps, k4, v4)
+        k_l = [torch.empty((3 * chunk, h, d), dtype=torch.bfloat16, device=DEV) for _ in range(n_l)]
+        v_l = [torch.empty_like(x) for x in k_l]
+        pipe.restore(blocks, dps, k_l, v_l)
+        pipe.synchronize(timeout=30.0)
+        for layer in range(n_l):
+            assert bits_equal(k4[layer].cpu(), k_l[layer].cpu())
+            assert bits_equal(v4[layer].cpu(), v_l[layer].cpu())
+        with pytest.raises(ValueError, match="sharing one layout"):
+            pipe.restore(blocks, dps, k4[:, :-1], v4[:, :-1])
+        with pytest.raises(ValueError, match="sharing one layout"):
+            pipe.restore(blocks, dps, k_l[:-1], v_l[:-1])
+
+
 def test_pipeline_restore_matches_oracle(scb, oracle):
     from speccache_b200.cache import KVRestorePipeline
 
@@ -353,12 +381,14 @@ def test_pipeline_restore_matches_oracle(scb, oracle):
                 assert bits_equal(v_out[layer].cpu(), vr)
 
 
-def test_pipeline_back_to_back_restores_reuse_slots(scb, oracle):
+@pytest.mark.parametrize("per_layer", [False, True])
+def test_pipeline_back_to_back_restores_reuse_slots(scb, oracle, per_layer):
     from speccache_b200.cache import KVRestorePipeline
 
     n_l, n_blocks, chunk, h, d = 5, 6, 64, 8, 128
     g = torch.Generator().manual_seed(12)
-    with KVRestorePipeline(n_l, n_blocks, chunk, h, d, device=DEV, n_slots=2) as pipe:
+    with KVRestorePipeline(n_l, n_blocks, chunk, h, d, device=DEV, n_slots=2,
+                           per_layer=per_layer) as pipe:
         pipe.k_quant.copy_(torch.randint(-127, 128, pipe.k_quant.shape, generator=g, dtype=torch.int8))
         pipe.v_quant.copy_(torch.randint(-127, 128, pipe.v_quant.shape, generator=g, dtype=torch.int8))
         pipe.k_scale.fill_(0.01)

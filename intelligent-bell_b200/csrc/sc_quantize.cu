@@ -6,10 +6,12 @@
 //
 // Vector path: a row is G lanes x V x 32 bytes (G = head_dim * sizeof(x) / (32 V), a power of
 // two <= 32, V 256-bit loads per lane); the absmax is reduced with G-lane xor shuffles; each
-// lane writes 32 V / sizeof(x) codes with 32-byte (or smaller) stores.  Codes come from x * (1/scale) in packed
-// fp32x2 arithmetic, exact unless the quotient lies within 2^-14 of a half-integer, where
-// the lane redoes the IEEE division; rounding to an integer is done by adding 1.5 * 2^23
-// (the fp32 add rounds half to even and leaves the integer in the low mantissa byte).
+// lane writes 32 V / sizeof(x) codes with 32-byte (or smaller) stores.  Codes come from packed
+// fp32x2 arithmetic; rounding to an integer is done by adding 1.5 * 2^23 (the fp32 add rounds
+// half to even and leaves the integer in the low mantissa byte).  For fp16/bf16 inputs with
+// fp16 scales, two products that bracket x / scale give the exact code with no tie test
+// (pair_codes2); otherwise x * (1/scale) is exact unless the quotient lies within 2^-14 of a
+// half-integer, where the lane redoes the IEEE division (fast_codes2).
 // Generic path: one warp per row, any strides, two passes over the row.
 #include <type_traits>
 
@@ -26,7 +28,7 @@ constexpr int kQThreads = 256;
 // Resident blocks per SM the vector kernel is compiled for, per input type (the register
 // cap follows; 0 leaves the register count to the compiler).
 #ifndef SC_QUANT_MB_F16
-#define SC_QUANT_MB_F16 5
+#define SC_QUANT_MB_F16 0
 #endif
 #ifndef SC_QUANT_MB_BF16
 #define SC_QUANT_MB_BF16 0
@@ -117,6 +119,28 @@ __device__ __forceinline__ void fast_codes2(float2 x, float2 rcp2, uint32_t& t0,
     t1 = __float_as_uint(t.y);
 }
 
+// Codes for 16-bit inputs with fp16 scales, with no tie test.  x and s have at most 11
+// significant bits, so x - (m + 1/2) s is a multiple of min(ulp(x), ulp(s) / 2): a quotient
+// q = x / s (|q| <= 127.5) that is not itself a half-integer lies at least 2^-19 |q| from
+// every half-integer.  rcp_lo and rcp_hi bracket 1 / s within 1.5 * 2^-22 relative
+// (rcp_lo * s < 1 < rcp_hi * s), so the exact products x * rcp_lo and x * rcp_hi (one fma
+// each, rounded to an integer by adding 1.5 * 2^23) both round to the integer nearest q
+// unless q is exactly a half-integer, when they are its two neighbours.  t1 + t2 then lies
+// in [2^24, 2^25), where the fp32 grid step is 2: the sum is exact when t1 = t2 and rounds
+// half to even onto 2 * (the even neighbour) otherwise, which is rint_even(q) either way.
+// RN(x / s) rounds to the same integer because it is within 2^-24 |q| of q.  The low byte
+// of the sum's bits is that integer as int8 (the sum is 2^24 + 2 * (2^22 + n)).
+constexpr float kPairLo = 0x1.fffff8p-1f;  // 1 - 2^-22
+constexpr float kPairHi = 0x1.000004p+0f;  // 1 + 2^-22
+
+__device__ __forceinline__ void pair_codes2(float2 x, float2 lo2, float2 hi2, uint32_t& c0,
+                                            uint32_t& c1) {
+    const float2 m2 = make_float2(kRound, kRound);
+    const float2 s = __fadd2_rn(__ffma2_rn(x, lo2, m2), __ffma2_rn(x, hi2, m2));
+    c0 = __float_as_uint(s.x);
+    c1 = __float_as_uint(s.y);
+}
+
 // Low bytes of four words -> one word.
 __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
@@ -187,19 +211,33 @@ __device__ __forceinline__ void convert_store(const QuantParams& p, uint32_t* w,
                                               int64_t t, int64_t h, int lane) {
     constexpr int E = 32 * V / static_cast<int>(sizeof(InT));
     constexpr bool kF16Scale = std::is_same<ScaleT, __half>::value;
+    // 16-bit input and fp16 scale: two-product rule, no tie test (pair_codes2)
+    constexpr bool kPairRule = kF16Scale && !std::is_same<InT, float>::value;
     const float sc = quant_scale(m, p.eps, kF16Scale);
     const float rcp = __frcp_rn(sc);
-    const float2 rcp2 = make_float2(rcp, rcp);
     // zero, tiny, huge or non-finite scale: exact path
     bool tie = !(sc >= 0x1p-126f && sc <= 0x1p125f);
     // Codes are packed four to a word as they are made, so only the packed words stay live.
     uint32_t packed[E / 4];
+    if constexpr (kPairRule) {
+        const float lo = __fmul_rn(rcp, kPairLo), hi = __fmul_rn(rcp, kPairHi);
+        const float2 lo2 = make_float2(lo, lo), hi2 = make_float2(hi, hi);
 #pragma unroll
-    for (int k = 0; k < E; k += 4) {
-        uint32_t c0, c1, c2, c3;
-        fast_codes2(pair_at<InT>(w, k), rcp2, c0, c1, tie);
-        fast_codes2(pair_at<InT>(w, k + 2), rcp2, c2, c3, tie);
-        packed[k / 4] = pack_low_bytes(c0, c1, c2, c3);
+        for (int k = 0; k < E; k += 4) {
+            uint32_t c0, c1, c2, c3;
+            pair_codes2(pair_at<InT>(w, k), lo2, hi2, c0, c1);
+            pair_codes2(pair_at<InT>(w, k + 2), lo2, hi2, c2, c3);
+            packed[k / 4] = pack_low_bytes(c0, c1, c2, c3);
+        }
+    } else {
+        const float2 rcp2 = make_float2(rcp, rcp);
+#pragma unroll
+        for (int k = 0; k < E; k += 4) {
+            uint32_t c0, c1, c2, c3;
+            fast_codes2(pair_at<InT>(w, k), rcp2, c0, c1, tie);
+            fast_codes2(pair_at<InT>(w, k + 2), rcp2, c2, c3, tie);
+            packed[k / 4] = pack_low_bytes(c0, c1, c2, c3);
+        }
     }
     if (tie) {  // rare: reload the lane's input (keeps the fast path's registers free)
         int64_t t2, h2;

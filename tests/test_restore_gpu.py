@@ -445,6 +445,34 @@ def test_quantize_ties_and_near_ties_bit_exact(scb, oracle, rows):
     assert torch.equal(q.cpu(), q_ref)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_quantize_exact_ties_16bit_inputs(scb, oracle, dtype):
+    # 16-bit inputs with fp16 scales take the two-product rule (no tie test).  Rows whose
+    # scale is s = m * 2^e (m odd, few bits, so (2k + 1) * m fits the input's significand)
+    # with one element 127 * s and the others (k + 1/2) * s or k * s: every half-integer
+    # quotient is exact and must round half to even, in both directions of the
+    # reciprocal's rounding error (m = 1: exact reciprocal; m = 3, 5, 7: inexact).
+    g = torch.Generator().manual_seed(5)
+    rows, d = 8192, 128
+    ms = torch.tensor([1.0, 3.0, 5.0, 7.0] if dtype == torch.float16 else [1.0])
+    m = ms[torch.randint(0, ms.numel(), (rows, 1), generator=g)]
+    e = torch.randint(-12, -1, (rows, 1), generator=g).to(torch.float32)
+    s = m * torch.pow(2.0, e)
+    k = torch.randint(-127, 127, (rows, d), generator=g).to(torch.float32)
+    half = torch.randint(0, 4, (rows, d), generator=g) > 0
+    x = torch.where(half, (k + 0.5) * s, k * s)
+    x[:, 0] = 127.0 * s[:, 0] * torch.where(torch.rand(rows, generator=g) < 0.5, -1.0, 1.0)
+    x16 = x.to(dtype)
+    assert torch.equal(x16.to(torch.float32), x)  # every element exactly representable
+    x16 = x16.view(rows // 8, 8, d)
+    q, sc = scb.quantize_kv_int8(x16.to(DEV))
+    q_ref, s_ref = oracle.quantize_kv_int8(x16)
+    torch.cuda.synchronize()
+    assert bits_equal(sc.cpu(), s_ref)
+    assert torch.equal(sc.cpu().to(torch.float32).view(rows, 1), s)
+    assert torch.equal(q.cpu(), q_ref)
+
+
 def test_fp32_scales_dense_and_quantize(scb, oracle):
     # float32 scales (an extension): x = fp16(fp32(q * s)) exactly as the reference's
     # arithmetic would do with float32 scales; quantize with float32 scale output skips the

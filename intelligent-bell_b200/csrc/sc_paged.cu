@@ -116,7 +116,10 @@ __device__ __forceinline__ int64_t page_out_offset(const PagedParams& p, int32_t
     return off + (tok0 + static_cast<int64_t>(c)) * p.o_t + h * p.o_h + j * 16;
 }
 
-template <typename OutT, bool X16>
+// kPtrs: request r writes its own buffers (ko_ptrs[r], vo_ptrs[r]) from offset 0; otherwise
+// ko / vo + out_off[r].  A separate instantiation keeps the offset path's output base in the
+// kernel parameters (holding it in registers measured 9 % slower).
+template <typename OutT, bool X16, bool kPtrs>
 __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
     paged_restore(const __grid_constant__ PagedParams p) {
     __shared__ __align__(16) float s_cos[kMaxHeadDim / 2];
@@ -149,12 +152,12 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
     // Page id, output offset and shift together: one memory latency for the three (all in
     // bounds: r < R, pg < max_pages <= table stride).
     const int32_t page_id = ld_meta(p.table + static_cast<int64_t>(r) * p.table_stride + pg);
-    void* ko = p.ko;
-    void* vo = p.vo;
+    void* ko_r = nullptr;
+    void* vo_r = nullptr;
     int64_t off = 0;
-    if (p.ko_ptrs != nullptr) {  // request r writes its own buffers from offset 0
-        if (has_k) ko = reinterpret_cast<void*>(ld_meta(reinterpret_cast<const int64_t*>(p.ko_ptrs) + r));
-        if (has_v) vo = reinterpret_cast<void*>(ld_meta(reinterpret_cast<const int64_t*>(p.vo_ptrs) + r));
+    if constexpr (kPtrs) {
+        if (has_k) ko_r = reinterpret_cast<void*>(ld_meta(reinterpret_cast<const int64_t*>(p.ko_ptrs) + r));
+        if (has_v) vo_r = reinterpret_cast<void*>(ld_meta(reinterpret_cast<const int64_t*>(p.vo_ptrs) + r));
     } else {
         off = ld_meta(p.out_off + r);
     }
@@ -168,7 +171,8 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
         const int64_t first = off + static_cast<int64_t>(tok0) * p.o_t;
         const int64_t last = first + static_cast<int64_t>(n_tok - 1) * p.o_t +
                              static_cast<int64_t>(p.H - 1) * p.o_h + p.D;
-        const bool misaligned = ((reinterpret_cast<uintptr_t>(ko) | reinterpret_cast<uintptr_t>(vo)) & 31) != 0;
+        const bool misaligned =
+            kPtrs && ((reinterpret_cast<uintptr_t>(ko_r) | reinterpret_cast<uintptr_t>(vo_r)) & 31) != 0;
         if ((off & 15) != 0 || misaligned || first < 0 || last > p.out_numel || p.o_t < 0 ||
             p.o_h < 0) {
             if (reporter) atomicOr(p.status, SC_STATUS_BAD_OUT_OFFSET);
@@ -205,11 +209,11 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
         if (buf[k].row < 0) continue;
         const int64_t oo = page_out_offset(p, buf[k].row, j, off, tok0);
         if (has_k) {
-            OutT* o = reinterpret_cast<OutT*>(ko) + oo;
+            OutT* o = reinterpret_cast<OutT*>(kPtrs ? ko_r : p.ko) + oo;
             rope_slice_store<OutT, __half, X16>(buf[k].ka, buf[k].kb, buf[k].ksc, cs, o, o + half);
         }
         if (has_v) {
-            OutT* o = reinterpret_cast<OutT*>(vo) + oo;
+            OutT* o = reinterpret_cast<OutT*>(kPtrs ? vo_r : p.vo) + oo;
             value_slice_store<OutT, __half>(buf[k].va, buf[k].vsc, o);
             value_slice_store<OutT, __half>(buf[k].vb, buf[k].vsc, o + half);
         }
@@ -221,7 +225,10 @@ template <typename OutT, bool X16>
 cudaError_t launch(const PagedParams& p, cudaStream_t stream) {
     const int threads = (kPThreads / p.P) * p.P;
     const int64_t blocks = static_cast<int64_t>(p.R) * p.max_pages * p.chunks;
-    paged_restore<OutT, X16><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p);
+    if (p.ko_ptrs != nullptr || p.vo_ptrs != nullptr)
+        paged_restore<OutT, X16, true><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p);
+    else
+        paged_restore<OutT, X16, false><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
@@ -229,10 +236,14 @@ cudaError_t launch(const PagedParams& p, cudaStream_t stream) {
 
 cudaError_t preload_paged_kernels() {
     cudaFuncAttributes attr;
-    cudaError_t e = cudaFuncGetAttributes(&attr, paged_restore<__half, true>);
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__half, false>);
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__nv_bfloat16, true>);
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__nv_bfloat16, false>);
+    cudaError_t e = cudaFuncGetAttributes(&attr, paged_restore<__half, true, false>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__half, false, false>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__nv_bfloat16, true, false>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__nv_bfloat16, false, false>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__half, true, true>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__half, false, true>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__nv_bfloat16, true, true>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__nv_bfloat16, false, true>);
     return e;
 }
 

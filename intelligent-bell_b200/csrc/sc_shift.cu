@@ -10,7 +10,8 @@
 // with each product and the sum rounded separately (no contraction), so the result equals
 // the reference's bit for bit given the same tables, subnormal products included.
 //
-// Vector path: a thread owns F = 16 (or 8) frequencies of one (token, head) row: two 32-byte
+// Vector path: a thread owns F = 16 (or 8) frequencies of one (token, head) row (packed fp32x2
+// arithmetic, two frequencies per instruction): two 32-byte
 // (16-byte) loads - the slice and its rotate-half partner - and two stores; one-shot blocks.  The
 // table of a host-side shift travels in the kernel parameters and is copied to shared
 // memory; device tables ([1 | T, D/2] fp16) are read per row.  Generic path: one thread per
@@ -52,6 +53,18 @@ __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) {
     return __bfloat162float(v);
 }
 
+// Two packed 16-bit values as floats (exact).
+template <typename T>
+__device__ __forceinline__ float2 to_f2(uint32_t w);
+template <>
+__device__ __forceinline__ float2 to_f2<__half>(uint32_t w) {
+    return __half22float2(bit_cast_u32<__half2>(w));
+}
+template <>
+__device__ __forceinline__ float2 to_f2<__nv_bfloat16>(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
 __device__ __forceinline__ void shift_pair(float x1, float x2, float c, float s, float& o1,
                                            float& o2) {
     o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
@@ -90,8 +103,8 @@ __device__ __forceinline__ void store_f(void* p, uint32_t* w) {
 template <typename InT, typename OutT, int F>
 __global__ void __launch_bounds__(kSThreads) shift_vec(const __grid_constant__ ShiftParams p) {
     constexpr int NW = F / 2;  // 32-bit words per half-slice
-    __shared__ float s_cos[kMaxHeadDim / 2];
-    __shared__ float s_sin[kMaxHeadDim / 2];
+    __shared__ __align__(16) float s_cos[kMaxHeadDim / 2];
+    __shared__ __align__(16) float s_sin[kMaxHeadDim / 2];
     const int half = p.D >> 1;
     if (p.cos == nullptr) {
         for (int f = threadIdx.x; f < half; f += blockDim.x) {
@@ -120,22 +133,22 @@ __global__ void __launch_bounds__(kSThreads) shift_vec(const __grid_constant__ S
     uint32_t lo[NW], hi[NW];
 #pragma unroll
     for (int k = 0; k < NW; ++k) {
-        float c0, c1, s0, s1;
+        // Two frequencies at once in packed fp32x2: each product and sum is still rounded
+        // once (RN), as in shift_pair; x2 * (-s) = -(x2 * s) exactly.
+        float2 c, ns, s;
         if (p.cos == nullptr) {
-            c0 = s_cos[f0 + 2 * k], c1 = s_cos[f0 + 2 * k + 1];
-            s0 = s_sin[f0 + 2 * k], s1 = s_sin[f0 + 2 * k + 1];
+            c = *reinterpret_cast<const float2*>(&s_cos[f0 + 2 * k]);
+            s = *reinterpret_cast<const float2*>(&s_sin[f0 + 2 * k]);
         } else {
-            const float2 cc = __half22float2(bit_cast_u32<__half2>(cw[k]));
-            const float2 ss = __half22float2(bit_cast_u32<__half2>(sw[k]));
-            c0 = cc.x, c1 = cc.y, s0 = ss.x, s1 = ss.y;
+            c = __half22float2(bit_cast_u32<__half2>(cw[k]));
+            s = __half22float2(bit_cast_u32<__half2>(sw[k]));
         }
-        const InT* ap = reinterpret_cast<const InT*>(&aw[k]);
-        const InT* bp = reinterpret_cast<const InT*>(&bw[k]);
-        float o1a, o2a, o1b, o2b;
-        shift_pair(to_f(ap[0]), to_f(bp[0]), c0, s0, o1a, o2a);
-        shift_pair(to_f(ap[1]), to_f(bp[1]), c1, s1, o1b, o2b);
-        lo[k] = pack2<OutT>(o1a, o1b);
-        hi[k] = pack2<OutT>(o2a, o2b);
+        ns = make_float2(-s.x, -s.y);
+        const float2 a = to_f2<InT>(aw[k]), b = to_f2<InT>(bw[k]);
+        const float2 o1 = __fadd2_rn(__fmul2_rn(a, c), __fmul2_rn(b, ns));
+        const float2 o2 = __fadd2_rn(__fmul2_rn(b, c), __fmul2_rn(a, s));
+        lo[k] = pack2<OutT>(o1.x, o1.y);
+        hi[k] = pack2<OutT>(o2.x, o2.y);
     }
     OutT* op = reinterpret_cast<OutT*>(p.out) + t * p.o_t + h * p.o_h + f0;
     store_f<F>(op, lo);

@@ -668,14 +668,21 @@ extern "C" int32_t sc_pipeline_offload(sc_pipeline* p, int32_t layer, const int3
 }
 
 namespace {
+// Polls without sleeping for the first millisecond (a sleep of 50 us takes 50-100 us more
+// with the kernel's default timer slack, longer than a small restore), then every 50 us.
 int32_t wait_event(cudaEvent_t ev, double deadline, double timeout_s, const char* what) {
+    const double spin_until = now_s() + 1e-3;
     for (;;) {
         const cudaError_t e = cudaEventQuery(ev);
         if (e == cudaSuccess) return SC_OK;
         if (e != cudaErrorNotReady) return cuda_error(e, what);
-        if (now_s() >= deadline)
+        const double t = now_s();
+        if (t >= deadline)
             return set_error(SC_ERR_TIMEOUT, "%s not complete after %.3f s", what, timeout_s);
-        usleep(50);
+        if (t < spin_until)
+            sched_yield();
+        else
+            usleep(50);
     }
 }
 }  // namespace

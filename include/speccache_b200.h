@@ -266,7 +266,9 @@ SC_API int32_t sc_pipeline_host_slabs(const sc_pipeline* p, int8_t** k_quant, vo
  *                       layer l goes to k_out[l] + (i*chunk_size + c)*st + h*sh + d
  *  out_strides          [token, head, dim] (dim stride 1)
  *  out_numel            elements of each k_out[l] / v_out[l] buffer (bounds check)
- * Returns once everything is enqueued; completion is ordered on compute_stream.
+ * Returns once everything is enqueued; completion is ordered on compute_stream.  The host
+ * waits only when four earlier restores still have their metadata upload queued (each upload
+ * follows the previous restore's kernels).
  */
 SC_API int32_t sc_pipeline_restore(sc_pipeline* p, const int32_t* block_ids, const int32_t* delta_ps,
                             int32_t n_blocks, double theta_base, const float* inv_freq,

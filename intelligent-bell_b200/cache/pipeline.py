@@ -99,7 +99,8 @@ class KVRestorePipeline:
         every layer.  ``k_out`` / ``v_out``: a list of ``num_layers`` ``[n*chunk, H, D]``
         fp16/bf16 views (any token/head strides, unit dim stride) sharing one layout, or one
         ``[num_layers, n*chunk, H, D]`` tensor.  The kernels write only inside these views.
-        Completion is ordered on the current CUDA stream; nothing blocks."""
+        Completion is ordered on the current CUDA stream; the call does not wait for the
+        device unless four earlier restores are still queued behind unfinished kernels."""
         ids = np.ascontiguousarray(np.asarray(block_ids, dtype=np.int32).reshape(-1))
         dps = np.ascontiguousarray(np.asarray(delta_ps, dtype=np.int64).reshape(-1))
         if ids.size != dps.size:

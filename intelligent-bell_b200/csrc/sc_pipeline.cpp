@@ -15,8 +15,10 @@
 //     layer's K and V; a second event per slot releases the slot for layer l + n_slots.
 // The offload runs the other way: the quantize kernel writes a device staging buffer on
 // the compute stream, an event hands it to the transfer stream, D2H copies fill the slabs.
-// Nothing on the host waits during a restore or an offload; sc_pipeline_synchronize polls
-// events with a deadline.
+// Nothing on the host waits during a restore or an offload while fewer than four earlier
+// restores still have their metadata upload queued (each upload follows the previous
+// restore's kernels; the host metadata buffers form a ring of four); sc_pipeline_synchronize
+// polls events with a deadline.
 #include <errno.h>
 #include <sched.h>
 #include <stdio.h>
@@ -47,6 +49,13 @@ constexpr size_t kAllLayerBytes = size_t(64) << 20;
 size_t meta_bytes(int64_t max_blocks) {
     return sizeof(Meta) + sizeof(float) * static_cast<size_t>(max_blocks > 1 ? max_blocks - 1 : 0);
 }
+
+// Host metadata buffers per path: a restore fills the next one while the uploads of up to
+// kMetaRing - 1 earlier restores may still be queued behind their predecessors' kernels, so
+// the host waits only when kMetaRing restores are in flight.
+constexpr int kMetaRing = 4;
+
+size_t round_up64(size_t n) { return (n + 63) / 64 * 64; }
 
 // Bind the calling thread to the CPUs local to `device` (best effort); returns true and
 // the previous mask in `old` if the binding was changed.
@@ -117,7 +126,8 @@ struct sc_pipeline {
     uint16_t* h_ks = nullptr;
     int8_t* h_vq = nullptr;
     uint16_t* h_vs = nullptr;
-    Meta* h_meta = nullptr;
+    uint8_t* h_meta = nullptr;  // kMetaRing buffers of meta_stride bytes
+    size_t meta_stride = 0;
     std::vector<int8_t*> d_kq, d_vq;  // per slot; d_vq[s] = d_kq[s] + stage codes (one allocation)
     uint16_t* d_sc = nullptr;         // scales of every layer: [2][L][max_blocks * chunk * H]
     bool codes_2d = false, scales_2d = false;  // pitches within the device's copy limit
@@ -127,17 +137,22 @@ struct sc_pipeline {
     cudaStream_t transfer = nullptr;
     std::vector<cudaEvent_t> ready, slot_free;
     std::vector<bool> slot_used;
-    cudaEvent_t meta_uploaded = nullptr, done = nullptr;
+    cudaEvent_t meta_uploaded[kMetaRing] = {}, done = nullptr;
+    bool meta_used[kMetaRing] = {};
+    int meta_next = 0;
     bool any_restore = false;
     // all-layers mode (small restores): K and V codes of every layer in one staging buffer
     // [2][L][n][block], one 3-D copy per run, one kernel launch with one request per layer
     int8_t* d_all = nullptr;
     int64_t all_cap_pages = 0;  // capacity in (layer, block) pages; 0 = mode unavailable
     bool codes_3d = false;
-    uint8_t* h_all_meta = nullptr;  // seq[L] | dps[all_cap_pages] | k_out[L] | v_out[L]
+    // kMetaRing host buffers, each seq[L] | dps[all_cap_pages] | k_out[L] | v_out[L]
+    uint8_t* h_all_meta = nullptr;
     uint8_t* d_all_meta = nullptr;
-    size_t all_meta_bytes = 0, off_dps = 0, off_kp = 0, off_vp = 0;
-    cudaEvent_t all_meta_uploaded = nullptr;
+    size_t all_meta_bytes = 0, all_meta_stride = 0, off_dps = 0, off_kp = 0, off_vp = 0;
+    cudaEvent_t all_meta_uploaded[kMetaRing] = {};
+    bool all_meta_used[kMetaRing] = {};
+    int all_meta_next = 0;
     bool any_all = false;
     // offload: quantize into one of two device staging slots (K then V codes in one
     // allocation, K then V scales in another), then D2H into the slabs
@@ -160,8 +175,10 @@ void release(sc_pipeline* p) {
     for (auto e : p->ready) cudaEventDestroy(e);
     for (auto e : p->slot_free) cudaEventDestroy(e);
     if (p->any_offload && p->o_free[p->o_last]) cudaEventSynchronize(p->o_free[p->o_last]);
-    if (p->meta_uploaded) cudaEventDestroy(p->meta_uploaded);
-    if (p->all_meta_uploaded) cudaEventDestroy(p->all_meta_uploaded);
+    for (int i = 0; i < kMetaRing; ++i) {
+        if (p->meta_uploaded[i]) cudaEventDestroy(p->meta_uploaded[i]);
+        if (p->all_meta_uploaded[i]) cudaEventDestroy(p->all_meta_uploaded[i]);
+    }
     cudaFree(p->d_all);
     cudaFree(p->d_all_meta);
     cudaFreeHost(p->h_all_meta);
@@ -251,7 +268,8 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
     if (e == cudaSuccess) p->h_vq = p->h_kq + slab_codes;
     halloc(2 * slab_scales * 2, &ptr, slab_flags), p->h_ks = static_cast<uint16_t*>(ptr);
     if (e == cudaSuccess) p->h_vs = p->h_ks + slab_scales;
-    halloc(meta_bytes(max_restore_blocks), &ptr, cudaHostAllocPortable), p->h_meta = static_cast<Meta*>(ptr);
+    p->meta_stride = round_up64(meta_bytes(max_restore_blocks));
+    halloc(kMetaRing * p->meta_stride, &ptr, cudaHostAllocPortable), p->h_meta = static_cast<uint8_t*>(ptr);
     if (bound) sched_setaffinity(0, sizeof(cpu_set_t), &old);
     if (e != cudaSuccess) {
         const int32_t rc = set_error(SC_ERR_HOST_ALLOC, "cudaHostAlloc of %zu-byte slabs failed: %s",
@@ -291,12 +309,14 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
             p->off_kp = p->off_dps + (static_cast<size_t>(p->all_cap_pages) * 4 + 7) / 8 * 8;
             p->off_vp = p->off_kp + static_cast<size_t>(n_layers) * 8;
             p->all_meta_bytes = p->off_vp + static_cast<size_t>(n_layers) * 8;
+            p->all_meta_stride = round_up64(p->all_meta_bytes);
             e = cudaMalloc(&p->d_all, 2 * static_cast<size_t>(p->all_cap_pages) * blk_codes);
             if (e == cudaSuccess) e = cudaMalloc(&p->d_all_meta, p->all_meta_bytes);
             if (e == cudaSuccess)
-                e = cudaHostAlloc(&p->h_all_meta, p->all_meta_bytes, cudaHostAllocPortable);
-            if (e == cudaSuccess)
-                e = cudaEventCreateWithFlags(&p->all_meta_uploaded, cudaEventDisableTiming);
+                e = cudaHostAlloc(&p->h_all_meta, kMetaRing * p->all_meta_stride,
+                                  cudaHostAllocPortable);
+            for (int i = 0; i < kMetaRing && e == cudaSuccess; ++i)
+                e = cudaEventCreateWithFlags(&p->all_meta_uploaded[i], cudaEventDisableTiming);
         }
     }
     const int64_t table_len = p->all_cap_pages > max_restore_blocks ? p->all_cap_pages
@@ -320,7 +340,8 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&b, cudaEventDisableTiming);
         p->ready.push_back(a), p->slot_free.push_back(b), p->slot_used.push_back(false);
     }
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->meta_uploaded, cudaEventDisableTiming);
+    for (int i = 0; i < kMetaRing && e == cudaSuccess; ++i)
+        e = cudaEventCreateWithFlags(&p->meta_uploaded[i], cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->done, cudaEventDisableTiming);
     for (int s = 0; s < 2 && e == cudaSuccess; ++s) {
         e = cudaEventCreateWithFlags(&p->o_ready[s], cudaEventDisableTiming);
@@ -363,13 +384,15 @@ int32_t restore_all_layers(sc_pipeline* p, const int32_t* block_ids, const int32
     const size_t blk_codes = row * p->D, blk_scales = row;
     const size_t pages = static_cast<size_t>(L) * n;
     cudaError_t e = cudaSuccess;
-    // The host metadata may still feed the previous all-layers upload.
-    if (p->any_all) e = cudaEventSynchronize(p->all_meta_uploaded);
-    if (e != cudaSuccess) return cuda_error(e, "waiting for the previous metadata upload");
-    int32_t* seq = reinterpret_cast<int32_t*>(p->h_all_meta);
-    float* dps = reinterpret_cast<float*>(p->h_all_meta + p->off_dps);
-    uint64_t* kp = reinterpret_cast<uint64_t*>(p->h_all_meta + p->off_kp);
-    uint64_t* vp = reinterpret_cast<uint64_t*>(p->h_all_meta + p->off_vp);
+    // The next host metadata buffer may still feed an upload kMetaRing restores back.
+    const int ms = p->all_meta_next;
+    if (p->all_meta_used[ms]) e = cudaEventSynchronize(p->all_meta_uploaded[ms]);
+    if (e != cudaSuccess) return cuda_error(e, "waiting for an earlier metadata upload");
+    uint8_t* hm = p->h_all_meta + static_cast<size_t>(ms) * p->all_meta_stride;
+    int32_t* seq = reinterpret_cast<int32_t*>(hm);
+    float* dps = reinterpret_cast<float*>(hm + p->off_dps);
+    uint64_t* kp = reinterpret_cast<uint64_t*>(hm + p->off_kp);
+    uint64_t* vp = reinterpret_cast<uint64_t*>(hm + p->off_vp);
     for (int l = 0; l < L; ++l) {
         seq[l] = n * p->chunk;
         kp[l] = reinterpret_cast<uint64_t>(k_out[l]);
@@ -380,10 +403,12 @@ int32_t restore_all_layers(sc_pipeline* p, const int32_t* block_ids, const int32
     // previous restore's kernels.
     if (p->any_restore) e = cudaStreamWaitEvent(p->transfer, p->done, 0);
     if (e == cudaSuccess)
-        e = cudaMemcpyAsync(p->d_all_meta, p->h_all_meta, p->all_meta_bytes, cudaMemcpyHostToDevice,
+        e = cudaMemcpyAsync(p->d_all_meta, hm, p->all_meta_bytes, cudaMemcpyHostToDevice,
                             p->transfer);
-    if (e == cudaSuccess) e = cudaEventRecord(p->all_meta_uploaded, p->transfer);
+    if (e == cudaSuccess) e = cudaEventRecord(p->all_meta_uploaded[ms], p->transfer);
     if (e != cudaSuccess) return cuda_error(e, "metadata upload");
+    p->all_meta_used[ms] = true;
+    p->all_meta_next = (ms + 1) % kMetaRing;
     // Per run of consecutive blocks: K and V codes of every layer with one 3-D copy (rows:
     // layers at the slab's layer pitch; slices: K then V), packed [2][L][n][block] on the
     // device; the scales of every layer with one 2-D copy, packed [2][L][n][chunk * H].
@@ -474,19 +499,23 @@ extern "C" int32_t sc_pipeline_restore(sc_pipeline* p, const int32_t* block_ids,
                                   v_out, out_strides, out_numel, out_dtype, cs);
     cudaError_t e = cudaSuccess;
 
-    // Metadata: the host buffer may still feed the previous restore's upload.
-    if (p->any_restore) e = cudaEventSynchronize(p->meta_uploaded);
-    if (e != cudaSuccess) return cuda_error(e, "waiting for the previous metadata upload");
-    p->h_meta->seq_len = n_blocks * p->chunk;
-    p->h_meta->out_offset = 0;
-    for (int32_t i = 0; i < n_blocks; ++i) p->h_meta->delta_p[i] = static_cast<float>(delta_ps[i]);
+    // Metadata: the next host buffer may still feed an upload kMetaRing restores back.
+    const int ms = p->meta_next;
+    if (p->meta_used[ms]) e = cudaEventSynchronize(p->meta_uploaded[ms]);
+    if (e != cudaSuccess) return cuda_error(e, "waiting for an earlier metadata upload");
+    Meta* hm = reinterpret_cast<Meta*>(p->h_meta + static_cast<size_t>(ms) * p->meta_stride);
+    hm->seq_len = n_blocks * p->chunk;
+    hm->out_offset = 0;
+    for (int32_t i = 0; i < n_blocks; ++i) hm->delta_p[i] = static_cast<float>(delta_ps[i]);
     // The device copy may still be read by the previous restore's last kernels.
     if (p->any_restore) e = cudaStreamWaitEvent(p->transfer, p->done, 0);
     if (e == cudaSuccess)
-        e = cudaMemcpyAsync(p->d_meta, p->h_meta, meta_bytes(n_blocks), cudaMemcpyHostToDevice,
+        e = cudaMemcpyAsync(p->d_meta, hm, meta_bytes(n_blocks), cudaMemcpyHostToDevice,
                             p->transfer);
-    if (e == cudaSuccess) e = cudaEventRecord(p->meta_uploaded, p->transfer);
+    if (e == cudaSuccess) e = cudaEventRecord(p->meta_uploaded[ms], p->transfer);
     if (e != cudaSuccess) return cuda_error(e, "metadata upload");
+    p->meta_used[ms] = true;
+    p->meta_next = (ms + 1) % kMetaRing;
 
     const size_t row = static_cast<size_t>(p->chunk) * p->H;
     const size_t blk_codes = row * p->D, blk_scales = row;

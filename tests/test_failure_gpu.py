@@ -3,7 +3,7 @@ the host (nothing here faults, traps or hangs the GPU):
 
 * a pinned-allocation failure (host failpoint ``SC_FAILPOINT_HOST_ALLOC``) is reported as an
   error, cleans up what was allocated, and leaves the library usable;
-* a stalled stream (torch's bounded ``_sleep`` kernel ahead of the restore) does not block the
+* a stalled stream (torch's bounded ``_sleep`` kernel ahead of the restores) does not block the
   enqueue (the pipeline loads its kernels at creation) and makes
   ``synchronize`` with a short deadline raise ``TimeoutError``; a later wait completes and the
   results are right;
@@ -61,27 +61,33 @@ def test_pinned_allocation_failure_is_reported_and_cleaned_up(scb, fail_at):
         assert pipe.k_quant.shape == (2, 4, 16, 2, 128)
 
 
-def test_synchronize_times_out_on_a_stalled_stream(scb, oracle):
+@pytest.mark.parametrize("per_layer", [False, True])
+def test_synchronize_times_out_on_a_stalled_stream(scb, oracle, per_layer):
     from speccache_b200.cache import KVRestorePipeline
 
     layers, blocks, chunk, h, d = 3, 6, 32, 4, 128
-    with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV) as pipe:
+    with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV, per_layer=per_layer) as pipe:
         _fill(pipe, 3)
-        ids, dps = [5, 0, 1], [-50, 7, 7]
-        k_out = torch.empty((layers, len(ids) * chunk, h, d), dtype=torch.bfloat16, device=DEV)
-        v_out = torch.empty_like(k_out)
+        cases = [([5, 0, 1], [-50, 7, 7]), ([2], [300]), ([3, 4], [0, -9]), ([1, 5, 2], [4, 4, 4])]
+        outs = []
+        for ids, _ in cases:
+            k_out = torch.empty((layers, len(ids) * chunk, h, d), dtype=torch.bfloat16, device=DEV)
+            outs.append((k_out, torch.empty_like(k_out)))
         torch.cuda._sleep(1000 * CYCLES_PER_MS)  # about one second of bounded delay
-        # the pipeline loaded its kernels when it was created, so this first restore is
-        # enqueued without waiting for the device (a lazy module load at the first launch
-        # would block until the delay is over)
-        t0 = time.perf_counter()
-        pipe.restore(ids, dps, list(k_out), list(v_out))
-        assert time.perf_counter() - t0 < 0.3
+        # The pipeline loaded its kernels when it was created, so restores are enqueued
+        # without waiting for the device (a lazy module load at the first launch would block
+        # until the delay is over); four restores in flight use distinct host metadata
+        # buffers, so none of them waits for the delayed kernels either.
+        for (ids, dps), (k_out, v_out) in zip(cases, outs):
+            t0 = time.perf_counter()
+            pipe.restore(ids, dps, list(k_out), list(v_out))
+            assert time.perf_counter() - t0 < 0.3
         with pytest.raises(TimeoutError):
             pipe.synchronize(timeout=0.05)
         pipe.synchronize(timeout=60.0)
         assert pipe.status() == 0
-        _check_layers(oracle, pipe, k_out, v_out, ids, dps)
+        for (ids, dps), (k_out, v_out) in zip(cases, outs):
+            _check_layers(oracle, pipe, k_out, v_out, ids, dps)
 
 
 PRELOAD_SCRIPT = r"""

@@ -458,7 +458,8 @@ def e2e_line(nbytes, e2e_ms, steps, world, h2d, d2h, launches, path, extra=None)
     out = {"value": nbytes * world * steps / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
            "restore_ms": e2e_ms / steps, "h2d_bytes_per_step": int(h2d),
            "d2h_bytes_per_step": int(d2h),
-           "h2d_gbs": h2d * world * steps / (e2e_ms / 1e3) / 1e9, "path": path,
+           "h2d_gbs": h2d * world * steps / (e2e_ms / 1e3) / 1e9,
+           "h2d_gbs_per_gpu": h2d * steps / (e2e_ms / 1e3) / 1e9, "path": path,
            "gpu_launches": launches}
     out.update(extra or {})
     return out

@@ -38,6 +38,7 @@ from __future__ import annotations
 
 import argparse
 import importlib
+import importlib.util
 import json
 import os
 import statistics
@@ -287,8 +288,44 @@ def make_paged_case(cfg, seed):
 
 
 # ---------------------------------------------------------------------------------------
-# CPU baselines (the oracle: the reference's eager arithmetic restated on torch-CPU)
+# CPU baselines: the reference's own eager functions (speccache/kernels/reference.py, pure
+# torch) from the installed copy under baseline/_ref; the oracle (the same arithmetic
+# restated on torch-CPU) only when that copy cannot be imported.
 # ---------------------------------------------------------------------------------------
+REFERENCE_ROOT = os.path.join(REPO, "baseline", "_ref")
+
+
+def load_reference_kernels():
+    """``speccache/kernels/reference.py`` of the installed reference, imported alone (it
+    depends on torch only; importing the ``speccache`` package would also build its HTTP app).
+    Returns (module, None) or (None, reason)."""
+    path = os.path.join(REFERENCE_ROOT, "speccache", "kernels", "reference.py")
+    if not os.path.exists(path):
+        return None, f"{path} not installed"
+    try:
+        spec = importlib.util.spec_from_file_location("_speccache_reference_kernels", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return mod, None
+    except Exception as exc:  # reported in the JSON line
+        return None, f"import of {path} failed: {exc!r}"
+
+
+def load_reference_injector():
+    """The reference's ``MultiLayerKVInjector`` (its ``apply_rope_shift`` is the key-shift
+    workload's reference), imported through the installed ``speccache`` package."""
+    if REFERENCE_ROOT not in sys.path:
+        sys.path.insert(0, REFERENCE_ROOT)
+    import logging
+
+    logging.disable(logging.CRITICAL)
+    try:
+        from speccache.serving.kv_injector import MultiLayerKVInjector
+        return MultiLayerKVInjector, None
+    except Exception as exc:
+        return None, f"import of speccache.serving.kv_injector failed: {exc!r}"
+
+
 def _cpu_layer(tokens, heads, head_dim, seed):
     g = torch.Generator().manual_seed(seed)
     kq = torch.randint(-127, 128, (tokens, heads, head_dim), generator=g, dtype=torch.int8)
@@ -298,62 +335,98 @@ def _cpu_layer(tokens, heads, head_dim, seed):
     return kq, ks, vq, vs
 
 
-def cpu_step_fn(workload: str, cfg: dict):
+def _restore_fn(ops, kq, ks, vq, vs, dp, head_dim, theta, out_dtype):
+    """One restore of one layer: the shift's tables, K dequant + shift, V dequant."""
+    if ops["kind"] == "reference":
+        ref = ops["mod"]
+
+        def fn():
+            c, s = ref.compute_rope_cos_sin_delta(torch.tensor([float(dp)]), head_dim,
+                                                  theta_base=theta)
+            ref.pytorch_eager_dequant_rope_shift(kq, ks, c, s)
+            ref.dequant_value_ref(vq, vs)
+        return fn
+    oracle = ops["mod"]
+
+    def fn():
+        c, s = oracle.compute_rope_cos_sin_delta(dp, head_dim, theta)
+        oracle.dequant_rope_shift(kq, ks, c, s, out_dtype=out_dtype)
+        oracle.dequant_value(vq, vs, out_dtype=out_dtype)
+    return fn
+
+
+def cpu_ops(workload: str) -> dict:
+    """What the CPU legs time: the reference's own functions, else the oracle port."""
+    if workload == "keyshift":
+        inj, why = load_reference_injector()
+        if inj is not None:
+            return {"kind": "reference", "mod": inj, "why": None}
+    else:
+        mod, why = load_reference_kernels()
+        if mod is not None:
+            return {"kind": "reference", "mod": mod, "why": None}
+    return {"kind": "port", "mod": importlib.import_module("oracle.speccache_oracle"), "why": why}
+
+
+def cpu_step_fn(workload: str, cfg: dict, ops: dict):
     """One bounded CPU sample of the workload; returns (callable, bytes, description)."""
-    oracle = importlib.import_module("oracle.speccache_oracle")
     h, d = cfg["heads"], cfg["head_dim"]
+    ref = ops["kind"] == "reference"
+    who = ("the reference's own functions (baseline/_ref speccache/kernels/reference.py: "
+           "compute_rope_cos_sin_delta, pytorch_eager_dequant_rope_shift, dequant_value_ref"
+           + (", quantize_kv_int8" if workload == "roundtrip" else "")
+           + "; fp16 outputs, the only dtype they produce, same bytes as bf16)") if ref else (
+           "the oracle port (the reference's eager arithmetic restated on torch-CPU)")
     if workload == "paged":
         t = 4224  # the mean request length of the batch
         kq, ks, vq, vs = _cpu_layer(t, h, d, SEED)
-        dp = 2048
-
-        def fn():
-            c, s = oracle.compute_rope_cos_sin_delta(dp, d, cfg["theta"])
-            oracle.dequant_rope_shift(kq, ks, c, s, out_dtype=cfg["out"])
-            oracle.dequant_value(vq, vs, out_dtype=cfg["out"])
-
+        fn = _restore_fn(ops, kq, ks, vq, vs, 2048, d, cfg["theta"], cfg["out"])
         return fn, restore_bytes(t * h, d), (
             f"1 request of mean length {t} of the {cfg['requests']}-request batch "
-            f"(H={h}, D={d}, K shift + V dequant)")
+            f"(H={h}, D={d}, K shift + V dequant) by {who}")
     t = cfg["tokens"]
     if workload == "keyshift":
         g = torch.Generator().manual_seed(SEED)
         k = torch.randn((t, h, d), generator=g).to(torch.float16)
+        if ref:
+            inj = ops["mod"](1, h, d, device=torch.device("cpu"), max_blocks=1, chunk_size=64)
 
-        def fn():
-            oracle.apply_rope_shift(k, cfg["delta_p"], cfg["theta"])
+            def fn():
+                inj.apply_rope_shift(k, cfg["delta_p"])
+            who = ("the reference's own MultiLayerKVInjector.apply_rope_shift "
+                   "(speccache/serving/kv_injector.py:246-283, theta 10000: it takes no theta)")
+        else:
+            oracle = ops["mod"]
 
+            def fn():
+                oracle.apply_rope_shift(k, cfg["delta_p"], cfg["theta"])
         return fn, shift_bytes(t * h, d), (
-            f"1 of {cfg['layers']} layers (T={t}, H={h}, D={d}: RoPE shift of fp16 keys)")
+            f"1 of {cfg['layers']} layers (T={t}, H={h}, D={d}: RoPE shift of fp16 keys) by {who}")
     if workload == "roundtrip":
         g = torch.Generator().manual_seed(SEED)
         xk = torch.randn((t, h, d), generator=g).to(torch.float16)
         xv = torch.randn((t, h, d), generator=g).to(torch.float16)
+        mod = ops["mod"]
 
         def fn():
-            kq, ks = oracle.quantize_kv_int8(xk)
-            vq, vs = oracle.quantize_kv_int8(xv)
-            c, s = oracle.compute_rope_cos_sin_delta(cfg["delta_p"], d, cfg["theta"])
-            oracle.dequant_rope_shift(kq, ks, c, s, out_dtype=cfg["out"])
-            oracle.dequant_value(vq, vs, out_dtype=cfg["out"])
+            kq, ks = mod.quantize_kv_int8(xk)
+            vq, vs = mod.quantize_kv_int8(xv)
+            _restore_fn(ops, kq, ks, vq, vs, cfg["delta_p"], d, cfg["theta"], cfg["out"])()
 
         return fn, quantize_bytes(t * h, d) + restore_bytes(t * h, d), (
-            f"1 of {cfg['layers']} layers (T={t}, H={h}, D={d}: quantize K,V then restore)")
+            f"1 of {cfg['layers']} layers (T={t}, H={h}, D={d}: quantize K,V then restore) by {who}")
     kq, ks, vq, vs = _cpu_layer(t, h, d, SEED)
     dp = cfg.get("delta_p", draw_shift(SEED))
-
-    def fn():
-        c, s = oracle.compute_rope_cos_sin_delta(dp, d, cfg["theta"])
-        oracle.dequant_rope_shift(kq, ks, c, s, out_dtype=cfg["out"])
-        oracle.dequant_value(vq, vs, out_dtype=cfg["out"])
-
+    fn = _restore_fn(ops, kq, ks, vq, vs, dp, d, cfg["theta"], cfg["out"])
     return fn, restore_bytes(t * h, d), (
-        f"1 of {cfg['layers']} layers (T={t}, H={h}, D={d}, K shift + V dequant)")
+        f"1 of {cfg['layers']} layers (T={t}, H={h}, D={d}, K shift + V dequant) by {who}")
 
 
 def cpu_baseline(workload: str, cfg: dict, time_limit_s: float = 10.0) -> dict:
     torch.set_num_threads(os.cpu_count() or 1)
-    fn, nbytes, what = cpu_step_fn(workload, cfg)
+    ops = cpu_ops(workload)
+    fn, nbytes, what = cpu_step_fn(workload, cfg, ops)
+    fn()  # first call outside the timing (allocator warm-up)
     times = []
     t_end = time.perf_counter() + time_limit_s
     while len(times) < 5 or (time.perf_counter() < t_end and len(times) < 200):
@@ -361,20 +434,24 @@ def cpu_baseline(workload: str, cfg: dict, time_limit_s: float = 10.0) -> dict:
         fn()
         times.append(time.perf_counter() - t0)
     med = statistics.median(times)
-    return {"value": nbytes / med / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
-            "kind": "port", "sample": f"{what}; median of {len(times)} runs; per-layer cost "
-                                      "is independent of the layer, so it scales linearly"}
+    out = {"value": nbytes / med / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+           "kind": ops["kind"], "sample": f"{what}; median of {len(times)} runs; per-layer cost "
+                                          "is independent of the layer, so it scales linearly"}
+    if ops["why"]:
+        out["reference_unavailable"] = ops["why"]
+    return out
 
 
 def run_reference(args) -> None:
-    """The reference's CPU implementation of the path (its eager arithmetic, restated in the
-    oracle) on the host cores; rank 0 only under torchrun."""
+    """The reference's CPU implementation of the path (its own eager functions from
+    baseline/_ref, else the oracle port) on the host cores; rank 0 only under torchrun."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     cfg = WORKLOADS[args.workload]
     torch.set_num_threads(os.cpu_count() or 1)
-    fn, nbytes, what = cpu_step_fn(args.workload, cfg)
+    ops = cpu_ops(args.workload)
+    fn, nbytes, what = cpu_step_fn(args.workload, cfg, ops)
     for _ in range(args.warmup):
         fn()
     times = []
@@ -384,16 +461,17 @@ def run_reference(args) -> None:
         times.append(time.perf_counter() - t0)
     mean = sum(times) / len(times)
     value = nbytes / mean / 1e9
+    base = {"value": value, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": ops["kind"],
+            "sample": f"{what}, one per step"}
+    if ops["why"]:
+        base["reference_unavailable"] = ops["why"]
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8/fp16 in, fp32 math, 16-bit out", "data": "synthetic (seeded)",
         "config": workload_config(args.workload, cfg, world),
-        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": torch.get_num_threads(),
-                         "kind": "port",
-                         "sample": f"{what} per step (the reference's eager arithmetic "
-                                   "restated on torch-CPU, the oracle)"},
+        "cpu_baseline": base,
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -502,6 +580,7 @@ def bench_llama8b(args, scb, dist: Dist, cfg: dict):
             tail[1].copy_(v_out[layers - 1, t - 1], non_blocking=True)
 
         e2e_ms, _ = time_steps(e2e_step, args.steps, args.warmup, dist)
+        ceiling = h2d_ceiling(pipe, dist)
         # one restore on its own (latency, nothing overlapping it)
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -515,7 +594,91 @@ def bench_llama8b(args, scb, dist: Dist, cfg: dict):
                            tail.numel() * tail.element_size(), layers * args.steps,
                            "sc_pipeline_restore from pinned host slabs, one kernel per layer",
                            {"restore_ms_single": single_ms, "device_status": status})
+    line["e2e"].update(ceiling)
+    line["e2e"]["h2d_vs_ceiling"] = line["e2e"]["h2d_gbs"] / ceiling["h2d_ceiling_gbs"]
     return line
+
+
+def h2d_ceiling(pipe, dist: Dist, reps: int = 3) -> dict:
+    """Copy-only ceiling of the host-to-device leg at this N: every rank copies its whole
+    pinned slab (the K and V codes and scales of every layer, the bytes one restore moves)
+    into HBM with one cudaMemcpyAsync per slab and nothing else running, all ranks at once
+    between barriers; aggregate GB/s over the slowest rank's time."""
+    slabs = [pipe.k_quant, pipe.v_quant, pipe.k_scale, pipe.v_scale]
+    srcs = [x.reshape(-1).view(torch.uint8) for x in slabs]
+    nbytes = sum(x.numel() for x in srcs)
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=dist.device)
+    parts = []
+    off = 0
+    for x in srcs:
+        parts.append(dst[off:off + x.numel()])
+        off += x.numel()
+
+    def copy_all():
+        for d_, s_ in zip(parts, srcs):
+            d_.copy_(s_, non_blocking=True)
+
+    ms, _ = time_steps(copy_all, reps, 1, dist)
+    del dst
+    return {"h2d_ceiling_gbs": nbytes * dist.world * reps / (ms / 1e3) / 1e9,
+            "h2d_ceiling_ms": ms / reps,
+            "h2d_ceiling_how": f"{len(srcs)} cudaMemcpyAsync of the rank's pinned slabs "
+                               f"({nbytes} B) into HBM per rank, all ranks at once, nothing else running"}
+
+
+def gather_check(scb, dist: Dist, layers: int = 3, blocks: int = 6, chunk: int = 64,
+                 heads: int = 8, head_dim: int = 128, theta: float = 500000.0) -> dict:
+    """The head-shard gather onto one GPU, checked in the run (N >= 2, outside the timing).
+
+    Every rank restores its KV-head shard of a small model (3 layers x 4 blocks of 64
+    tokens, 8 heads, per-block shifts) from its own pinned slab straight into GPU 0's caches
+    (HeadShardGather: CUDA IPC mapping, plain 32-byte peer stores from the restore kernel;
+    no multicast, no TMA, no library kernel on peer memory).  GPU 0 then restores every
+    head itself with the dense kernel (sc_dequant_rope_kv, a different kernel on the same
+    arithmetic) and compares all K and V bits."""
+    from speccache_b200.cache import HeadShardGather, KVRestorePipeline, shard_view
+
+    ids, shifts = [4, 0, 1, 5], [-300, 12, 12, 4000]
+    g = torch.Generator().manual_seed(4242)  # the whole model's codes, the same on every rank
+    kq = torch.randint(-127, 128, (layers, blocks, chunk, heads, head_dim), generator=g,
+                       dtype=torch.int8)
+    vq = torch.randint(-127, 128, kq.shape, generator=g, dtype=torch.int8)
+    ks = (torch.rand(kq.shape[:4] + (1,), generator=g) * 0.05 + 1e-3).half()
+    vs = (torch.rand(kq.shape[:4] + (1,), generator=g) * 0.05 + 1e-3).half()
+    world, rank, dev = dist.world, dist.rank, dist.device
+    n_tok = len(ids) * chunk
+    out = {"layers": layers, "tokens": n_tok, "heads": heads, "heads_per_rank": heads // world,
+           "owner": 0}
+    with KVRestorePipeline(layers, blocks, chunk, heads // world, head_dim, device=dev) as pipe:
+        for dst, src in ((pipe.k_quant, kq), (pipe.k_scale, ks), (pipe.v_quant, vq),
+                         (pipe.v_scale, vs)):
+            dst.copy_(shard_view(src, heads, world, rank, 3))
+        k_full = v_full = None
+        if rank == 0:
+            k_full = torch.zeros((layers, n_tok, heads, head_dim), dtype=torch.bfloat16, device=dev)
+            v_full = torch.zeros_like(k_full)
+        gather = HeadShardGather(pipe, k_full, v_full, owner=0, rank=rank, world_size=world,
+                                 num_kv_heads=heads)
+        gather.restore(ids, shifts, theta=theta)
+        pipe.synchronize()
+        out["device_status_max"] = int(dist.max(float(pipe.status())))
+        dist.barrier()  # every writer's stream has completed
+        if rank == 0:
+            exp_k = torch.empty_like(k_full)
+            exp_v = torch.empty_like(v_full)
+            for i, (b, dp) in enumerate(zip(ids, shifts)):
+                sl = slice(i * chunk, (i + 1) * chunk)
+                scb.restore_layers(kq[:, b].to(dev), ks[:, b].to(dev), vq[:, b].to(dev),
+                                   vs[:, b].to(dev), delta_p=dp, theta=theta,
+                                   k_out=exp_k[:, sl], v_out=exp_v[:, sl])
+            torch.cuda.synchronize(dev)
+            out["k_mismatched"] = int((k_full.view(torch.int16) != exp_k.view(torch.int16)).sum())
+            out["v_mismatched"] = int((v_full.view(torch.int16) != exp_v.view(torch.int16)).sum())
+            out["ok"] = (out["k_mismatched"] == 0 and out["v_mismatched"] == 0
+                         and out["device_status_max"] == 0)
+        dist.barrier()  # the other ranks keep their mappings until GPU 0 has checked
+        gather.close()
+    return out
 
 
 def bench_paged(args, scb, dist: Dist, cfg: dict):
@@ -752,6 +915,10 @@ def run_ours(args) -> None:
           "llama70b": bench_llama70b, "keyshift": bench_keyshift}[args.workload]
     with ClockSampler(dist.device.index or 0) as clocks:
         part = fn(args, scb, dist, cfg)
+    check = None
+    if dist.world > 1 and args.workload in ("llama8b", "llama70b") and not args.skip_gather_check:
+        check = gather_check(scb, dist)
+        part["gather_check"] = check
     if dist.rank == 0:
         line = {"metric": METRIC, "value": part.pop("value"), "unit": "GB/s",
                 "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
@@ -767,6 +934,8 @@ def run_ours(args) -> None:
             line["cpu_baseline"] = cpu_baseline(args.workload, cfg)
         print(json.dumps(line), flush=True)
     dist.close()
+    if check is not None and dist.rank == 0 and not check.get("ok", False):
+        raise SystemExit(f"head-shard gather check failed: {check}")
 
 
 def main() -> None:
@@ -783,6 +952,8 @@ def main() -> None:
     ap.add_argument("--skip-cpu-baseline", action="store_true", help="profiling aid")
     ap.add_argument("--write-combined", action="store_true",
                     help="pin the host slabs write-combined (pipeline workloads)")
+    ap.add_argument("--skip-gather-check", action="store_true",
+                    help="N > 1: skip the in-run check of the head-shard gather onto GPU 0")
     ap.add_argument("--gather", action="store_true",
                     help="llama70b: restore every rank's head shard into GPU 0's caches (NVLink)")
     args = ap.parse_args()

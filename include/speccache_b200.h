@@ -143,8 +143,10 @@ SC_API int32_t sc_dequant_rope_kv(int32_t n_layers, int64_t n_tokens, int32_t n_
  * <= 1,048,576 (e.g. 16384 tokens at head_dim 128); larger calls are rejected with
  * SC_ERR_INVALID_ARGUMENT.  Keys are required, values optional; other arguments as for
  * sc_dequant_rope_kv.  The first call on a device looks up the array's device address
- * (make it before any stream capture).  Calls share the array: calls that overlap on the
- * GPU race.
+ * (make it before any stream capture) and keeps it for the life of the process, so a
+ * cudaDeviceReset after that first call is not supported.  Calls share the array: calls
+ * that overlap on the GPU race.  Arguments are all checked before the array is written, so
+ * a refused call leaves it untouched.
  */
 SC_API int32_t sc_dequant_rope_kv_token_shifts_noalloc(
     int32_t n_layers, int64_t n_tokens, int32_t n_heads, int32_t head_dim, const int8_t* k_quant,

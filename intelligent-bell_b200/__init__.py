@@ -4,7 +4,8 @@ The reference's kernel API (``speccache.kernels``) on hand-written CUDA kernels 
 the C ABI of ``libspeccache_b200.so`` (declared in ``include/speccache_b200.h``):
 
 * ``triton_fused_k_dequant_rope_shift`` / ``dequant_value`` / ``dequant_kv_cache`` —
-  INT8 K dequant + relative RoPE shift and V dequant;
+  INT8 K dequant + relative RoPE shift and V dequant (and the reference's eager ``*_ref`` and
+  compiled ``*_compiled`` names on the same kernels);
 * ``quantize_kv_int8`` — the bit-exact offload twin;
 * ``compute_rope_cos_sin_delta`` — shift tables;
 * ``restore_paged`` — ragged, paged gather + restore in one launch;
@@ -23,10 +24,16 @@ from ._build import LIB_PATH, build_library
 from .kernels import (
     compute_rope_cos_sin_delta,
     dequant_and_rope_key,
+    dequant_and_rope_key_compiled,
+    dequant_and_rope_key_ref,
     dequant_kv_cache,
     dequant_value,
+    dequant_value_compiled,
+    dequant_value_ref,
     fused_k_dequant_rope_shift_kernel,
     paged_status,
+    pytorch_compiled_dequant_rope_shift,
+    pytorch_eager_dequant_rope_shift,
     quantize_kv_int8,
     quantize_symmetric_int8,
     restore_layers,
@@ -63,10 +70,16 @@ __all__ = [
     "preload",
     "compute_rope_cos_sin_delta",
     "dequant_and_rope_key",
+    "dequant_and_rope_key_compiled",
+    "dequant_and_rope_key_ref",
     "dequant_kv_cache",
     "dequant_value",
+    "dequant_value_compiled",
+    "dequant_value_ref",
     "fused_k_dequant_rope_shift_kernel",
     "paged_status",
+    "pytorch_compiled_dequant_rope_shift",
+    "pytorch_eager_dequant_rope_shift",
     "quantize_kv_int8",
     "quantize_symmetric_int8",
     "restore_layers",

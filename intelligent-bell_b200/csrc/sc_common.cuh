@@ -190,6 +190,23 @@ __device__ __forceinline__ void rope_cs(float dp, float inv_freq, float& c, floa
     s = __half2float(sh);
 }
 
+// The rotate-half pair: o1 = x1 c - x2 s, o2 = x2 c + x1 s, rounded like torch's separate
+// multiply and add (each product rounded to fp32, then the sum).  kExact: x1, x2, c and s
+// are all fp16 values, so both products are exact in fp32 and one fma per output gives the
+// same bits with fewer instructions.  Otherwise (fp32 intermediate) the products carry up to
+// 29 significant bits and are rounded explicitly, which an fma would skip.
+template <bool kExact>
+__device__ __forceinline__ void rotate_pair(float x1, float x2, float c, float s, float& o1,
+                                            float& o2) {
+    if constexpr (kExact) {
+        o1 = fmaf(x1, c, -(x2 * s));
+        o2 = fmaf(x2, c, x1 * s);
+    } else {
+        o1 = __fadd_rn(__fmul_rn(x1, c), -__fmul_rn(x2, s));
+        o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+    }
+}
+
 // cos/sin of a 16-frequency slice, read four at a time.
 //   CsShared: the block's table in shared memory (16-byte aligned float4 reads).
 //   CsRegs:   values the thread holds itself (per-token tables).
@@ -253,10 +270,9 @@ __device__ __forceinline__ void rope_slice_store(const uint4& a, const uint4& b,
                 }
             }
             const float c0 = cv[2 * k], c1 = cv[2 * k + 1], s0 = sv[2 * k], s1 = sv[2 * k + 1];
-            const float o1a = fmaf(x1.x, c0, -(x2.x * s0));
-            const float o1b = fmaf(x1.y, c1, -(x2.y * s1));
-            const float o2a = fmaf(x2.x, c0, x1.x * s0);
-            const float o2b = fmaf(x2.y, c1, x1.y * s1);
+            float o1a, o1b, o2a, o2b;
+            rotate_pair<X16>(x1.x, x2.x, c0, s0, o1a, o2a);
+            rotate_pair<X16>(x1.y, x2.y, c1, s1, o1b, o2b);
             r1[w * 2 + k] = pack2<OutT>(o1a, o1b);
             r2[w * 2 + k] = pack2<OutT>(o2a, o2b);
         }

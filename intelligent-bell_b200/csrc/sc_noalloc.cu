@@ -11,7 +11,9 @@
 // it (4 MiB) until the process exits.  Host code cannot use the symbol as a device address:
 // the first call on a device, with that device current, looks the address up with
 // cudaGetSymbolAddress and caches it for that device.  Make that first call before any
-// stream capture.  All calls share the array and it keeps the last call's tables; the tables
+// stream capture.  The cached address belongs to the device's primary context: after a
+// cudaDeviceReset it would be stale, so resetting a device after its first call here is not
+// supported.  All calls share the array and it keeps the last call's tables; the tables
 // are rewritten in full for every token a call uses, so nothing needs clearing, but calls
 // whose work overlaps on the GPU (different streams, or different host threads) race on it.
 #include <mutex>
@@ -57,10 +59,22 @@ extern "C" int32_t sc_dequant_rope_kv_token_shifts_noalloc(
     const int64_t* vs_strides, int32_t scale_dtype, const float* delta_p_tokens,
     double theta_base, const float* inv_freq, void* k_out, const int64_t* ko_strides,
     void* v_out, const int64_t* vo_strides, int32_t out_dtype, uint32_t flags, void* stream) {
+    // Every argument is checked before the shared tables are touched, so a call that is
+    // refused never overwrites tables that a call still running on the GPU is reading.
+    if (n_layers < 0 || n_tokens < 0 || n_heads < 0)
+        return sc::set_error(SC_ERR_INVALID_ARGUMENT, "negative size (layers=%d tokens=%lld heads=%d)",
+                             n_layers, (long long)n_tokens, n_heads);
     if (head_dim <= 0 || (head_dim & 1))
         return sc::set_error(SC_ERR_INVALID_ARGUMENT,
                              "head_dim must be even for RoPE half-pairing, got head_dim=%d", head_dim);
-    if (n_tokens < 0) return sc::set_error(SC_ERR_INVALID_ARGUMENT, "negative n_tokens");
+    if (head_dim > sc::kMaxHeadDim)
+        return sc::set_error(SC_ERR_UNSUPPORTED, "head_dim %d exceeds %d", head_dim, sc::kMaxHeadDim);
+    if (out_dtype != SC_DTYPE_F16 && out_dtype != SC_DTYPE_BF16)
+        return sc::set_error(SC_ERR_INVALID_DTYPE, "output dtype code %d: float16 or bfloat16 only",
+                             out_dtype);
+    if (scale_dtype != SC_DTYPE_F16 && scale_dtype != SC_DTYPE_F32)
+        return sc::set_error(SC_ERR_INVALID_DTYPE, "scale dtype code %d: float16 or float32 only",
+                             scale_dtype);
     const int64_t entries = n_tokens * (head_dim / 2);
     if (entries > kMaxEntries)
         return sc::set_error(SC_ERR_INVALID_ARGUMENT,
@@ -72,6 +86,12 @@ extern "C" int32_t sc_dequant_rope_kv_token_shifts_noalloc(
         return sc::set_error(SC_ERR_INVALID_ARGUMENT, "keys are required (the shift applies to K)");
     if (delta_p_tokens == nullptr)
         return sc::set_error(SC_ERR_INVALID_ARGUMENT, "null delta_p_tokens");
+    if (!k_scale || !k_out || !kq_strides || !ks_strides || !ko_strides)
+        return sc::set_error(SC_ERR_INVALID_ARGUMENT, "K given without its scale/output/strides");
+    if (v_quant && (!v_scale || !v_out || !vq_strides || !vs_strides || !vo_strides))
+        return sc::set_error(SC_ERR_INVALID_ARGUMENT, "V given without its scale/output/strides");
+    if (static_cast<int64_t>(n_layers) * n_tokens * n_heads >= (int64_t(1) << 31))
+        return sc::set_error(SC_ERR_INVALID_ARGUMENT, "too many rows in one call; split it below 2^31");
     if (n_layers == 0 || n_tokens == 0 || n_heads == 0) return sc::ok();
     void* tables = nullptr;
     const int32_t rc = table_address(&tables);

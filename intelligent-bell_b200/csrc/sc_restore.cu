@@ -252,8 +252,10 @@ __global__ void __launch_bounds__(kThreads)
                 s = s_sin[f];
             }
             OutT* o = reinterpret_cast<OutT*>(p.ko) + l * p.ko_s[0] + t * p.ko_s[1] + h * p.ko_s[2];
-            o[f * g.ko_d] = from_float<OutT>(fmaf(x1, c, -(x2 * s)));
-            o[(f + half) * g.ko_d] = from_float<OutT>(fmaf(x2, c, x1 * s));
+            float o1, o2;
+            rotate_pair<X16>(x1, x2, c, s, o1, o2);
+            o[f * g.ko_d] = from_float<OutT>(o1);
+            o[(f + half) * g.ko_d] = from_float<OutT>(o2);
         }
         if (p.has_v) {
             const int8_t* vb = p.vq + l * p.vq_s[0] + t * p.vq_s[1] + h * p.vq_s[2];
@@ -357,11 +359,12 @@ void fill_host_table(uint32_t* out_tab, int head_dim, float dp, double theta, co
     memcpy(out_tab, c.tab, sizeof(uint32_t) * half);
 }
 
+// Resident blocks per SM of `kernel`, cached per device in the caller's `cache` (one cache
+// per kernel instantiation: every instantiation has its own register count).
 template <typename K>
-int blocks_per_sm(K kernel, int threads) {
+int blocks_per_sm(K kernel, int threads, int (&cache)[64]) {
     int dev = 0;
     cudaGetDevice(&dev);
-    static int cache[64] = {0};
     if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, 0) != cudaSuccess ||
@@ -391,7 +394,8 @@ cudaError_t launch_generic(const DenseParams& p, const GenericStrides& g, cudaSt
     auto kern = dense_restore_generic<OutT, ScaleT, X16>;
     const int64_t total = g.rows * (p.D / 2);
     const int64_t need = (total + kThreads - 1) / kThreads;
-    const int64_t cap = static_cast<int64_t>(sm_count()) * blocks_per_sm(kern, kThreads);
+    static int occupancy[64] = {0};  // this instantiation's resident blocks per SM, per device
+    const int64_t cap = static_cast<int64_t>(sm_count()) * blocks_per_sm(kern, kThreads, occupancy);
     const int grid = static_cast<int>(need < cap ? (need > 0 ? need : 1) : cap);
     kern<<<grid, kThreads, 0, stream>>>(p, g);
     return cudaGetLastError();

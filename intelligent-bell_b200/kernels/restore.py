@@ -6,13 +6,27 @@ speccache/kernels/reference.py:122-165), with the same names, arguments, ``out=`
 semantics (written in place and returned) and exceptions.  They run the sm_100a kernels
 of ``libspeccache_b200.so`` on ``torch.cuda.current_stream()``; nothing synchronises.
 
-Additive extensions (defaults keep the reference's behaviour):
+Two arithmetics, both within the reference's rtol = atol = 1e-2 of each other:
+  * fp32 intermediate: ``x = q*s`` stays in fp32 before the rotation, the arithmetic of the
+    reference's Triton kernel (triton_rope_kv.py:150-158).  It is the default of the names
+    that replace the Triton wrappers (``triton_fused_k_dequant_rope_shift``,
+    ``dequant_and_rope_key``, ``dequant_kv_cache``) and of ``pytorch_compiled_dequant_rope_shift``
+    / ``dequant_and_rope_key_compiled`` (Inductor drops the fp16 round trip of the eager code).
+  * fp16 intermediate: ``x`` is rounded to fp16 first, the reference's eager arithmetic
+    (reference.py:257), used by ``pytorch_eager_dequant_rope_shift`` /
+    ``dequant_and_rope_key_ref`` and by ``restore_layers`` (default).
+Either way every product and sum is rounded as torch rounds its separate multiply and add,
+so given the same cos/sin tables the outputs are bit-exact against the reference's torch
+arithmetic of that kind.  ``fp32_intermediate=`` selects the other one on any of them.
+
+Additive extensions (other defaults keep the reference's behaviour):
   * ``theta=`` for the ``delta_p`` path (the reference hard-wires 10000);
   * bfloat16 outputs (``out`` of dtype bf16, or ``out_dtype=torch.bfloat16``);
   * arbitrary input/output strides (no ``.contiguous()`` copies);
-  * ``fp32_intermediate=True`` keeps ``q*s`` in fp32 before the rotation (the reference
-    Triton kernel's arithmetic) instead of rounding it to fp16 (its eager arithmetic);
   * ``restore_layers`` restores many layers ``[L, T, H, D]`` in one launch.
+
+Every name takes CUDA tensors only and raises ``RuntimeError`` for CPU tensors: there is
+no CPU path.
 """
 
 from __future__ import annotations
@@ -149,12 +163,13 @@ def triton_fused_k_dequant_rope_shift(
     delta_p: int | torch.Tensor | None = None,
     theta: float = DEFAULT_THETA,
     out_dtype: torch.dtype | None = None,
-    fp32_intermediate: bool = False,
+    fp32_intermediate: bool = True,
 ) -> torch.Tensor:
     """Fused INT8 key dequant + relative RoPE shift (triton_rope_kv.py:243-345).
 
     ``k_quant`` int8 ``[T, H, D]``, ``k_scale`` fp16 ``[T, H, 1]``, cos/sin fp16
-    ``[1 | T, D/2]`` or ``delta_p`` (int, or tensor of 1 or T shifts).
+    ``[1 | T, D/2]`` or ``delta_p`` (int, or tensor of 1 or T shifts).  Default arithmetic:
+    the Triton kernel's (``q*s`` kept in fp32).
     """
     validate_key_core(k_quant, k_scale, out)
     cos, sin, dp, dp_dev = _resolve_shift(k_quant, cos_delta, sin_delta, delta_p, theta)
@@ -170,6 +185,50 @@ def triton_fused_k_dequant_rope_shift(
 
 
 dequant_and_rope_key = triton_fused_k_dequant_rope_shift
+
+
+def pytorch_eager_dequant_rope_shift(
+    k_quant: torch.Tensor,
+    k_scale: torch.Tensor,
+    cos_delta: torch.Tensor | None = None,
+    sin_delta: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+    *,
+    delta_p: int | torch.Tensor | None = None,
+) -> torch.Tensor:
+    """The reference's eager dequant + shift (reference.py:212-280) on the CUDA kernel.
+
+    Same arguments and result as the reference function: the dequantised key is rounded to
+    fp16 before the rotation (reference.py:257); a ``delta_p`` without tables uses theta
+    10000 like the reference.  CUDA tensors only.
+    """
+    return triton_fused_k_dequant_rope_shift(k_quant, k_scale, cos_delta, sin_delta, out,
+                                             delta_p=delta_p, fp32_intermediate=False)
+
+
+dequant_and_rope_key_ref = pytorch_eager_dequant_rope_shift
+
+
+def pytorch_compiled_dequant_rope_shift(
+    k_quant: torch.Tensor,
+    k_scale: torch.Tensor,
+    cos_delta: torch.Tensor | None = None,
+    sin_delta: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+    *,
+    delta_p: int | torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Replaces the reference's ``torch.compile`` of the eager function (reference.py:310-322).
+
+    Inductor does not keep the eager code's fp16 round trip of ``q*s``
+    (``torch._inductor.config.emulate_precision_casts`` is off by default), so this runs the
+    kernel with the dequantised key kept in fp32.  CUDA tensors only.
+    """
+    return triton_fused_k_dequant_rope_shift(k_quant, k_scale, cos_delta, sin_delta, out,
+                                             delta_p=delta_p, fp32_intermediate=True)
+
+
+dequant_and_rope_key_compiled = pytorch_compiled_dequant_rope_shift
 
 
 def dequant_value(
@@ -190,6 +249,23 @@ def dequant_value(
     return out
 
 
+def dequant_value_ref(
+    v_quant: torch.Tensor,
+    v_scale: torch.Tensor,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """The reference's eager value dequant (reference.py:283-307) on the CUDA kernel.
+
+    ``fp16(q*s)`` has one rounding of an exact product, so the eager, compiled and Triton
+    versions all give the same bits.  CUDA tensors only.
+    """
+    return dequant_value(v_quant, v_scale, out)
+
+
+# torch.compile of the eager value dequant (reference.py:318-327): the same bits.
+dequant_value_compiled = dequant_value_ref
+
+
 def dequant_kv_cache(
     k_quant: torch.Tensor,
     k_scale: torch.Tensor,
@@ -203,9 +279,10 @@ def dequant_kv_cache(
     delta_p: int | torch.Tensor | None = None,
     theta: float = DEFAULT_THETA,
     out_dtype: torch.dtype | None = None,
-    fp32_intermediate: bool = False,
+    fp32_intermediate: bool = True,
 ) -> tuple[torch.Tensor, torch.Tensor]:
-    """K (shifted) and V (plain) in one launch (triton_rope_kv.py:414-427)."""
+    """K (shifted) and V (plain) in one launch (triton_rope_kv.py:414-427).  Default
+    arithmetic: the Triton kernel's (``q*s`` kept in fp32)."""
     validate_key_core(k_quant, k_scale, k_out)
     validate_value_inputs(v_quant, v_scale, v_out)
     cos, sin, dp, dp_dev = _resolve_shift(k_quant, cos_delta, sin_delta, delta_p, theta)

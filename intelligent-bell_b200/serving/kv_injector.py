@@ -224,8 +224,9 @@ class MultiLayerKVInjector:
             torch.cuda.current_stream(self.device).wait_stream(stream)
             for x in dev:
                 x.record_stream(torch.cuda.current_stream(self.device))
+        # The eager arithmetic (fp16 intermediate), like every restore path of the injector.
         return dequant_kv_cache(*dev, cos_delta, sin_delta, delta_p=delta_p if cos_delta is None else None,
-                                theta=self.theta, out_dtype=self.out_dtype)
+                                theta=self.theta, out_dtype=self.out_dtype, fp32_intermediate=False)
 
     def reconstruct_and_inject_multi_layer(self, cache: SpecDynamicCache, block_ids: list[int],
                                            delta_ps: list[int]):

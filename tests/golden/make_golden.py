@@ -3,7 +3,7 @@
 Usage (in a container that has the reference checked out; it is not needed on the
 GPU machine, which only reads the committed ``.npz`` output)::
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <reference source tree>
 
 The reference package is imported from its source tree.  Each case records the
 inputs and the reference's outputs; ``tests/test_oracle_golden.py`` checks the
@@ -232,9 +232,12 @@ def make_key_shift_and_inject(ref_root: str, out: dict) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("SPECCACHE_REFERENCE"),
+                    help="the reference project's source tree (or set SPECCACHE_REFERENCE)")
     ap.add_argument("--out", default=os.path.join(HERE, "golden_path1.npz"))
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give the reference's source tree with --reference or SPECCACHE_REFERENCE")
     torch.set_num_threads(1)
     ref = _load_reference_kernels(args.reference)
     out: dict = {}

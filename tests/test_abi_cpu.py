@@ -154,6 +154,60 @@ def test_operators_refuse_cpu_tensors(scb):
             call()
 
 
+# The fifteen public names of the reference's kernels package
+# (speccache/kernels/__init__.py:23-38).
+REFERENCE_KERNEL_NAMES = [
+    "compute_rope_cos_sin_delta", "dequant_and_rope_key", "dequant_and_rope_key_compiled",
+    "dequant_and_rope_key_ref", "dequant_kv_cache", "dequant_value", "dequant_value_compiled",
+    "dequant_value_ref", "fused_k_dequant_rope_shift_kernel", "pytorch_compiled_dequant_rope_shift",
+    "pytorch_eager_dequant_rope_shift", "quantize_kv_int8", "quantize_symmetric_int8",
+    "rotate_half", "triton_fused_k_dequant_rope_shift",
+]
+
+
+def test_every_reference_kernel_name_is_exported(scb):
+    for name in REFERENCE_KERNEL_NAMES:
+        assert name in scb.__all__ and name in scb.kernels.__all__, name
+        assert getattr(scb, name) is getattr(scb.kernels, name), name
+
+
+def test_reference_eager_and_compiled_names_refuse_cpu_tensors(scb):
+    k = torch.zeros((4, 2, 64), dtype=torch.int8)
+    s = torch.ones((4, 2, 1), dtype=torch.float16)
+    for name in ("pytorch_eager_dequant_rope_shift", "dequant_and_rope_key_ref",
+                 "pytorch_compiled_dequant_rope_shift", "dequant_and_rope_key_compiled",
+                 "dequant_and_rope_key"):
+        with pytest.raises(RuntimeError, match="CUDA device"):
+            getattr(scb, name)(k, s, delta_p=3)
+    for name in ("dequant_value_ref", "dequant_value_compiled"):
+        with pytest.raises(RuntimeError, match="CUDA device"):
+            getattr(scb, name)(k, s)
+
+
+def test_kernel_handle_explains_itself(scb):
+    kern = scb.fused_k_dequant_rope_shift_kernel
+    assert "sc_dequant_rope_kv" in repr(kern)
+    with pytest.raises(TypeError, match="sc_dequant_rope_kv"):
+        kern[(1, 1)]
+    with pytest.raises(TypeError, match="triton_fused_k_dequant_rope_shift"):
+        kern(1, 2, 3)
+
+
+def test_ctypes_stub_matches_the_header(scb):
+    # include/b200_abi.py declares sc_dequant_rope_kv with as many arguments as the header
+    import importlib.util
+
+    os.environ["SPECCACHE_B200_LIB"] = scb._lib.LIB_PATH
+    spec = importlib.util.spec_from_file_location("b200_abi", os.path.join(REPO, "include", "b200_abi.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    with open(HEADER) as f:
+        text = f.read()
+    decl = re.search(r"SC_API int32_t sc_dequant_rope_kv\((.*?)\);", text, re.S).group(1)
+    assert len(mod._lib.sc_dequant_rope_kv.argtypes) == decl.count(",") + 1
+    assert mod.SC_FLAG_FP32_INTERMEDIATE == scb._lib.SC_FLAG_FP32_INTERMEDIATE
+
+
 def test_rotate_half_convention(scb):
     x = torch.tensor([[[1.0, 2.0, 3.0, 4.0]]])
     assert torch.equal(scb.rotate_half(x), torch.tensor([[[-3.0, -4.0, 1.0, 2.0]]]))

@@ -78,7 +78,7 @@ def _quantize_restore_config(scb, oracle, layers, t, h, d, theta, dp, out_dtype,
         _k_close(k_out[layer].cpu(), k_ref)
         assert bits_equal(v_out[layer].cpu(), v_ref), layer
         scb.dequant_kv_cache(kq[layer], ks[layer], vq[layer], vs[layer], cos_d, sin_d,
-                             k_out=k_tab, v_out=v_tab)
+                             k_out=k_tab, v_out=v_tab, fp32_intermediate=False)
         assert bits_equal(k_tab.cpu(), k_ref), layer
         assert bits_equal(v_tab.cpu(), v_ref), layer
 

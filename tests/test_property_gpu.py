@@ -37,9 +37,10 @@ def _codes(g, shape):
 @SETTINGS
 @given(t=st.integers(1, 300), h=st.integers(1, 12), d=head_dims, dp=st.integers(-70000, 70000),
        theta=st.sampled_from([10000.0, 500000.0, 1e6]), out_dtype=out_dtypes,
-       model_layout=st.booleans(), per_token=st.booleans(), seed=st.integers(0, 2**31 - 1))
+       model_layout=st.booleans(), per_token=st.booleans(), fp32=st.booleans(),
+       seed=st.integers(0, 2**31 - 1))
 def test_dense_restore_matches_oracle(scb, oracle, t, h, d, dp, theta, out_dtype, model_layout,
-                                      per_token, seed):
+                                      per_token, fp32, seed):
     g = torch.Generator().manual_seed(seed)
     kq, ks = _codes(g, (t, h, d))
     vq, vs = _codes(g, (t, h, d))
@@ -53,9 +54,10 @@ def test_dense_restore_matches_oracle(scb, oracle, t, h, d, dp, theta, out_dtype
         k_out = torch.empty((t, h, d), dtype=out_dtype, device=DEV)
         v_out = torch.empty_like(k_out)
     scb.dequant_kv_cache(kq.to(DEV), ks.to(DEV), vq.to(DEV), vs.to(DEV), cos.to(DEV), sin.to(DEV),
-                         k_out=k_out, v_out=v_out)
+                         k_out=k_out, v_out=v_out, fp32_intermediate=fp32)
     torch.cuda.synchronize()
-    assert bits_equal(k_out.cpu().contiguous(), oracle.dequant_rope_shift(kq, ks, cos, sin, out_dtype))
+    assert bits_equal(k_out.cpu().contiguous(),
+                      oracle.dequant_rope_shift(kq, ks, cos, sin, out_dtype, fp16_intermediate=not fp32))
     assert bits_equal(v_out.cpu().contiguous(), oracle.dequant_value(vq, vs, out_dtype))
 
 
@@ -69,7 +71,8 @@ def test_in_kernel_shift_within_tolerance(scb, oracle, t, h, d, dp, theta, seed)
     out = scb.triton_fused_k_dequant_rope_shift(kq.to(DEV), ks.to(DEV), delta_p=dp, theta=theta)
     cos, sin = oracle.compute_rope_cos_sin_delta(dp, d, theta)
     torch.cuda.synchronize()
-    torch.testing.assert_close(out.cpu(), oracle.dequant_rope_shift(kq, ks, cos, sin),
+    torch.testing.assert_close(out.cpu(), oracle.dequant_rope_shift(kq, ks, cos, sin,
+                                                                    fp16_intermediate=False),
                                rtol=1e-2, atol=1e-2)
 
 

@@ -1,8 +1,10 @@
 """GPU parity of the restore kernels against the CPU oracle and the reference's goldens.
 
 Tolerances: where the cos/sin tables are given, K is compared bit for bit with the
-reference's eager arithmetic (fp16-rounded dequant, fp32 rotation); V always bit for
-bit.  Where the kernel builds cos/sin itself from delta_p, each table entry may differ
+reference's torch arithmetic of the same kind: the eager one (fp16-rounded dequant, fp32
+rotation) for the ``*_ref`` names and ``fp32_intermediate=False``, the fp32-intermediate one
+(the Triton kernel's, and what Inductor compiles the eager code to) for the Triton-named
+wrappers' default and the ``*_compiled`` names; V always bit for bit.  Where the kernel builds cos/sin itself from delta_p, each table entry may differ
 from torch's by one fp16 ulp in rare cases (torch's float32 cos/sin is not correctly
 rounded), so K is checked with the reference's own tolerance, rtol = atol = 1e-2
 (reference tests/test_correctness.py:169), plus an exact-match fraction.
@@ -26,20 +28,70 @@ def _quantized(oracle, t, h, d, seed, dtype=torch.float32):
     return oracle.quantize_kv_int8(raw)
 
 
+# Every key entry point of the reference's kernels/__init__.py:3-21, with the arithmetic of
+# the function it replaces: True = fp16 intermediate (eager), False = fp32 intermediate.
+KEY_NAMES = [
+    ("pytorch_eager_dequant_rope_shift", True),
+    ("dequant_and_rope_key_ref", True),
+    ("pytorch_compiled_dequant_rope_shift", False),
+    ("dequant_and_rope_key_compiled", False),
+    ("triton_fused_k_dequant_rope_shift", False),
+    ("dequant_and_rope_key", False),
+]
+VALUE_NAMES = ["dequant_value", "dequant_value_ref", "dequant_value_compiled"]
+
+
 @pytest.mark.parametrize("t", [1, 17, 128, 511, 2048, 4096])
 @pytest.mark.parametrize("h", [4, 8, 32])
 @pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("delta_p", [-512, 0, 1024])
-def test_k_shift_grid_matches_eager_bitwise(scb, oracle, t, h, d, delta_p):
-    # the reference's 108-case grid (tests/test_correctness.py:142-169)
+def test_k_shift_grid_every_name_bitwise(scb, oracle, t, h, d, delta_p):
+    # the reference's 108-case grid (tests/test_correctness.py:142-169), for every key and
+    # value name the reference exports
     kq, ks = _quantized(oracle, t, h, d, 42)
+    vq, vs = _quantized(oracle, t, h, d, 43)
     cos, sin = oracle.compute_rope_cos_sin_delta(delta_p, d)
-    ref = oracle.dequant_rope_shift(kq, ks, cos, sin)
-    out = scb.triton_fused_k_dequant_rope_shift(kq.to(DEV), ks.to(DEV), cos.to(DEV), sin.to(DEV))
+    refs = {x16: oracle.dequant_rope_shift(kq, ks, cos, sin, fp16_intermediate=x16)
+            for x16 in (True, False)}
+    v_ref = oracle.dequant_value(vq, vs)
+    kd, sd, cd, snd = kq.to(DEV), ks.to(DEV), cos.to(DEV), sin.to(DEV)
+    outs = {name: getattr(scb, name)(kd, sd, cd, snd) for name, _ in KEY_NAMES}
+    v_outs = {name: getattr(scb, name)(vq.to(DEV), vs.to(DEV)) for name in VALUE_NAMES}
     torch.cuda.synchronize()
-    assert out.dtype == torch.float16 and out.shape == (t, h, d)
-    torch.testing.assert_close(out.cpu(), ref, rtol=1e-2, atol=1e-2)
-    assert bits_equal(out.cpu(), ref)
+    for name, x16 in KEY_NAMES:
+        out = outs[name].cpu()
+        assert out.dtype == torch.float16 and out.shape == (t, h, d), name
+        torch.testing.assert_close(out, refs[x16], rtol=1e-2, atol=1e-2)
+        assert bits_equal(out, refs[x16]), name
+    for name in VALUE_NAMES:
+        assert bits_equal(v_outs[name].cpu(), v_ref), name
+
+
+def test_reference_names_reject_cpu_tensors(scb, oracle):
+    kq, ks = _quantized(oracle, 4, 2, 64, 1)
+    cos, sin = oracle.compute_rope_cos_sin_delta(3, 64)
+    for name, _ in KEY_NAMES:
+        with pytest.raises(RuntimeError):
+            getattr(scb, name)(kq, ks, cos, sin)
+    for name in VALUE_NAMES:
+        with pytest.raises(RuntimeError):
+            getattr(scb, name)(kq, ks)
+
+
+def test_reference_names_with_delta_p_and_out(scb, oracle):
+    # the delta_p form (theta 10000, as the reference) and a preallocated out, per name
+    t, h, d, dp = 300, 8, 128, 777
+    kq, ks = _quantized(oracle, t, h, d, 8)
+    cos, sin = oracle.compute_rope_cos_sin_delta(dp, d)
+    for name, x16 in KEY_NAMES:
+        ref = oracle.dequant_rope_shift(kq, ks, cos, sin, fp16_intermediate=x16)
+        pre = torch.empty((t, h, d), dtype=torch.float16, device=DEV)
+        ret = getattr(scb, name)(kq.to(DEV), ks.to(DEV), out=pre, delta_p=dp)
+        torch.cuda.synchronize()
+        assert ret.data_ptr() == pre.data_ptr(), name
+        torch.testing.assert_close(ret.cpu(), ref, rtol=1e-2, atol=1e-2)
+        same = (ret.cpu().view(torch.int16) == ref.view(torch.int16)).float().mean().item()
+        assert same > 0.99, (name, same)
 
 
 def test_golden_vectors(scb, golden):
@@ -48,7 +100,7 @@ def test_golden_vectors(scb, golden):
         kq, ks = as_tensor(golden[p + "kq"]).to(DEV), as_tensor(golden[p + "ks"]).to(DEV)
         cos, sin = as_tensor(golden[p + "cos"]).to(DEV), as_tensor(golden[p + "sin"]).to(DEV)
         vq, vs = as_tensor(golden[p + "vq"]).to(DEV), as_tensor(golden[p + "vs"]).to(DEV)
-        k, v = scb.dequant_kv_cache(kq, ks, vq, vs, cos, sin)
+        k, v = scb.dequant_kv_cache(kq, ks, vq, vs, cos, sin, fp32_intermediate=False)
         torch.cuda.synchronize()
         assert bits_equal(k.cpu(), as_tensor(golden[p + "k"])), name
         assert bits_equal(v.cpu(), as_tensor(golden[p + "v"])), name
@@ -60,7 +112,7 @@ def test_delta_p_path_in_kernel_tables(scb, oracle, theta, delta_p):
     t, h, d = 257, 8, 128
     kq, ks = _quantized(oracle, t, h, d, 7)
     cos, sin = oracle.compute_rope_cos_sin_delta(delta_p, d, theta)
-    ref = oracle.dequant_rope_shift(kq, ks, cos, sin)
+    ref = oracle.dequant_rope_shift(kq, ks, cos, sin, fp16_intermediate=False)
     out = scb.triton_fused_k_dequant_rope_shift(kq.to(DEV), ks.to(DEV), delta_p=delta_p, theta=theta)
     torch.cuda.synchronize()
     torch.testing.assert_close(out.cpu(), ref, rtol=1e-2, atol=1e-2)
@@ -72,13 +124,13 @@ def test_delta_p_device_scalar_and_per_token(scb, oracle):
     t, h, d = 100, 4, 64
     kq, ks = _quantized(oracle, t, h, d, 11)
     cos, sin = oracle.compute_rope_cos_sin_delta(-77, d)
-    ref = oracle.dequant_rope_shift(kq, ks, cos, sin)
+    ref = oracle.dequant_rope_shift(kq, ks, cos, sin, fp16_intermediate=False)
     out = scb.triton_fused_k_dequant_rope_shift(kq.to(DEV), ks.to(DEV),
                                                 delta_p=torch.tensor([-77], device=DEV))
     torch.testing.assert_close(out.cpu(), ref, rtol=1e-2, atol=1e-2)
     dps = torch.randint(-3000, 3000, (t,), generator=torch.Generator().manual_seed(1))
     cos_t, sin_t = oracle.compute_rope_cos_sin_delta(dps, d)
-    ref_t = oracle.dequant_rope_shift(kq, ks, cos_t, sin_t)
+    ref_t = oracle.dequant_rope_shift(kq, ks, cos_t, sin_t, fp16_intermediate=False)
     out_t = scb.triton_fused_k_dequant_rope_shift(kq.to(DEV), ks.to(DEV), delta_p=dps)
     torch.cuda.synchronize()
     torch.testing.assert_close(out_t.cpu(), ref_t, rtol=1e-2, atol=1e-2)
@@ -110,7 +162,8 @@ def test_value_and_bf16_outputs(scb, oracle):
                                 sin.to(DEV), out_dtype=torch.bfloat16)
     torch.cuda.synchronize()
     assert k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16
-    assert bits_equal(k.cpu(), oracle.dequant_rope_shift(kq, ks, cos, sin, torch.bfloat16))
+    assert bits_equal(k.cpu(), oracle.dequant_rope_shift(kq, ks, cos, sin, torch.bfloat16,
+                                                         fp16_intermediate=False))
     assert bits_equal(v.cpu(), oracle.dequant_value(vq, vs, torch.bfloat16))
     v16 = scb.dequant_value(vq.to(DEV), vs.to(DEV))
     torch.cuda.synchronize()
@@ -126,6 +179,14 @@ def test_fp32_intermediate_mode(scb, oracle):
                                                 fp32_intermediate=True)
     torch.cuda.synchronize()
     torch.testing.assert_close(out.cpu(), ref, rtol=1e-3, atol=1e-3)
+    assert bits_equal(out.cpu(), ref)  # products and sum rounded as torch rounds them
+    # bf16 outputs and float32 scales, same arithmetic
+    ks32 = ks.to(torch.float32)
+    ref32 = oracle.dequant_rope_shift(kq, ks32, cos, sin, torch.bfloat16, fp16_intermediate=False)
+    out32 = scb.triton_fused_k_dequant_rope_shift(kq.to(DEV), ks32.to(DEV), cos.to(DEV),
+                                                  sin.to(DEV), out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert bits_equal(out32.cpu(), ref32)
 
 
 def test_preallocated_out_is_written_in_place(scb, oracle):
@@ -138,7 +199,7 @@ def test_preallocated_out_is_written_in_place(scb, oracle):
                                                 out=pre)
     assert ret.data_ptr() == pre.data_ptr()
     torch.cuda.synchronize()
-    assert bits_equal(ret.cpu(), oracle.dequant_rope_shift(kq, ks, cos, sin))
+    assert bits_equal(ret.cpu(), oracle.dequant_rope_shift(kq, ks, cos, sin, fp16_intermediate=False))
 
 
 @pytest.mark.parametrize("force_generic", [False, True])
@@ -180,19 +241,24 @@ def test_generic_path_odd_strides(scb, oracle):
     kq_hm = kq.permute(1, 0, 2).contiguous().to(DEV).permute(1, 0, 2)
     cos, sin = oracle.compute_rope_cos_sin_delta(-99, d)
     k_ref = oracle.dequant_rope_shift(kq, ks, cos, sin)
+    k_ref32 = oracle.dequant_rope_shift(kq, ks, cos, sin, fp16_intermediate=False)
     for k_in in (kq_strided, kq_hm):
-        k, v = scb.dequant_kv_cache(k_in, ks.to(DEV), vq.to(DEV), vs.to(DEV), cos.to(DEV),
-                                    sin.to(DEV))
-        torch.cuda.synchronize()
-        assert bits_equal(k.cpu(), k_ref)
-        assert bits_equal(v.cpu(), oracle.dequant_value(vq, vs))
+        for fp32 in (False, True):
+            k, v = scb.dequant_kv_cache(k_in, ks.to(DEV), vq.to(DEV), vs.to(DEV), cos.to(DEV),
+                                        sin.to(DEV), fp32_intermediate=fp32)
+            torch.cuda.synchronize()
+            assert bits_equal(k.cpu(), k_ref32 if fp32 else k_ref)
+            assert bits_equal(v.cpu(), oracle.dequant_value(vq, vs))
     # odd head_dim is rejected like the reference; head_dim 34 (even, not a multiple of 32)
     # runs on the generic kernel
     kq34, ks34 = _quantized(oracle, 5, 2, 34, 12)
     c34, s34 = oracle.compute_rope_cos_sin_delta(7, 34)
     k34 = scb.triton_fused_k_dequant_rope_shift(kq34.to(DEV), ks34.to(DEV), c34.to(DEV), s34.to(DEV))
+    e34 = scb.pytorch_eager_dequant_rope_shift(kq34.to(DEV), ks34.to(DEV), c34.to(DEV), s34.to(DEV))
     torch.cuda.synchronize()
-    assert bits_equal(k34.cpu(), oracle.dequant_rope_shift(kq34, ks34, c34, s34))
+    assert bits_equal(k34.cpu(), oracle.dequant_rope_shift(kq34, ks34, c34, s34,
+                                                           fp16_intermediate=False))
+    assert bits_equal(e34.cpu(), oracle.dequant_rope_shift(kq34, ks34, c34, s34))
 
 
 def test_end_to_end_rotational_equivalence(scb, oracle):
@@ -577,5 +643,5 @@ def test_concurrent_host_threads_on_separate_streams(scb, oracle):
     for i, (kq, ks, dp) in enumerate(cases):
         for k in range(8):
             c, s = oracle.compute_rope_cos_sin_delta(dp + k, d)
-            torch.testing.assert_close(results[i][k], oracle.dequant_rope_shift(kq, ks, c, s),
-                                       rtol=1e-2, atol=1e-2)
+            ref = oracle.dequant_rope_shift(kq, ks, c, s, fp16_intermediate=False)
+            torch.testing.assert_close(results[i][k], ref, rtol=1e-2, atol=1e-2)

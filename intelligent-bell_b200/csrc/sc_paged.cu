@@ -1,17 +1,12 @@
 // sc_paged.cu — ragged, paged restore: page-table gather + INT8 dequant + relative RoPE
 // shift, written straight into contiguous per-request caches.
 //
-// Work unit: one block per (request, page, chunk of the page's rows) - one-shot blocks,
-// no persistent loop (on B200 one-shot tiles stream 9-10 % faster).  A block first reads
-// its request's length and exits at once if its page lies past it; otherwise it reads the
-// page id, output offset and shift together (one memory latency for the three), builds
-// the cos/sin table of the request's (or page's) shift in shared memory (single-precision
-// sincos, double precision only where the fp16 rounding is not settled, rounded like the
-// reference's fp16 tables), then walks SC_PAGED_ROUNDS groups of rows: each thread loads
-// its 16-frequency slice of a row (two 16-byte loads per tensor, rotate-half partner in
-// the same thread), converts it and stores it (one 32-byte store per 16 outputs).
-//
-// Two kernels share that per-row work:
+// Per row (one token-head of a page), each thread owns a 16-frequency slice: it reads 16
+// codes of the first half and their rotate-half partners (two 16-byte pieces per tensor),
+// converts them with the row's scale and the request's (or page's) cos/sin table, and
+// writes each 16 outputs with one 32-byte store.  The table is built in shared memory
+// (single-precision sincos, double precision only where the fp16 rounding is not settled,
+// rounded like the reference's fp16 tables).  Two kernels share that per-row work:
 //
 // * paged_restore_stream (the default): persistent blocks walk only the live tiles (a tile
 //   is TR = threads / (D/32) consecutive rows of one page).  Every block reads the request
@@ -23,8 +18,12 @@
 //   current one are loaded a page ahead.  So no block is launched for pages past a request's
 //   end, no block waits on metadata before its first load, and the bytes in flight per SM
 //   are bounded by shared memory instead of registers.
-// * paged_restore (SC_FLAG_PAGED_ONE_SHOT, and more than kMaxStreamRequests requests):
-//   one-shot blocks over the whole (request, page, chunk) grid, described below.
+// * paged_restore (SC_FLAG_PAGED_ONE_SHOT, more than kMaxStreamRequests requests, odd
+//   page * heads, scale arrays not 4-byte aligned): one-shot blocks, one per (request,
+//   page, chunk of the page's rows).  A block first reads its request's length and exits
+//   at once if its page lies past it; otherwise it reads the page id, output offset and
+//   shift together (one memory latency for the three), builds the table, then walks
+//   SC_PAGED_ROUNDS groups of rows, loading each row-slice into registers.
 //
 // Device-side checks never fault: a page id outside the pool, a bad sequence length or an
 // output range outside out_numel makes the block skip the work and OR a status bit into

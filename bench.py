@@ -714,20 +714,10 @@ def bench_paged(args, scb, dist: Dist, cfg: dict):
 
     total_ms, per = time_steps(step, args.steps, args.warmup, dist)
     status = scb.paged_status(dev)
-
-    def step_one_shot():
-        scb.restore_paged(pkq, pks, pvq, pvs, tab, lens_d, dps, theta=cfg["theta"],
-                          k_out=k_out, v_out=v_out, out_offsets=offs, one_shot_tiles=True)
-
-    os_ms, _ = time_steps(step_one_shot, args.steps, args.warmup, dist)
     line = {"value": nbytes * dist.world * args.steps / (total_ms / 1e3) / 1e9,
             "ms_per_step": total_ms / args.steps, "roofline": roofline(nbytes, per, "paged"),
             "gpu_launches": args.steps, "device_status": status,
-            "tokens": total, "pool_pages": n_pool,
-            "kernel": "paged_restore_stream (persistent, live tiles only, cp.async staging)",
-            "one_shot_tiles": {"value": nbytes * dist.world * args.steps / (os_ms / 1e3) / 1e9,
-                               "ms_per_step": os_ms / args.steps,
-                               "kernel": "paged_restore (one-shot blocks over the whole grid)"}}
+            "tokens": total, "pool_pages": n_pool}
     if args.skip_e2e:
         return line
     # e2e: the pool's pages arrive from pinned host memory, then one restore launch

@@ -72,9 +72,6 @@ typedef enum sc_dtype {
 /* Flags for the restore entry points. */
 #define SC_FLAG_FP32_INTERMEDIATE 0x1u /* keep q*s in fp32 before the rotation            */
 #define SC_FLAG_FORCE_GENERIC 0x2u     /* use the stride-generic kernel (testing aid)      */
-#define SC_FLAG_PAGED_ONE_SHOT 0x4u    /* sc_restore_paged: the one-shot-tile kernel instead of
-                                          the streaming one (testing aid; it is also the kernel
-                                          for more than 1024 requests in one call)          */
 
 /* Device status bits written (atomicOr) by the paged kernels into a caller-given word. */
 #define SC_STATUS_BAD_PAGE_ID 0x1    /* page-table entry outside [0, n_pool_pages)          */

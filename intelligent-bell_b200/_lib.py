@@ -33,7 +33,6 @@ SC_DTYPE_F32 = 2
 
 SC_FLAG_FP32_INTERMEDIATE = 0x1
 SC_FLAG_FORCE_GENERIC = 0x2
-SC_FLAG_PAGED_ONE_SHOT = 0x4
 
 SC_STATUS_BAD_PAGE_ID = 0x1
 SC_STATUS_BAD_SEQ_LEN = 0x2

@@ -40,6 +40,14 @@ constexpr int kThreads = SC_DENSE_THREADS;
 #ifndef SC_ROWS_PER_THREAD
 #define SC_ROWS_PER_THREAD 1
 #endif
+// Stage SC_DENSE_ROUNDS rounds of rows per block in shared memory with cp.async before
+// converting any (1), instead of loading SC_ROWS_PER_THREAD rows into registers (0).
+#ifndef SC_DENSE_CPASYNC
+#define SC_DENSE_CPASYNC 0
+#endif
+#ifndef SC_DENSE_ROUNDS
+#define SC_DENSE_ROUNDS 4
+#endif
 
 struct DenseParams {
     int32_t rows;  // n_layers * n_tokens * n_heads  (< 2^31)
@@ -188,11 +196,70 @@ enum CsMode : int {
 
 // One-shot tile: block b owns rows [b * RB * R, (b + 1) * RB * R); each thread loads its R
 // row-slices, then converts and stores them.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+
 template <typename OutT, typename ScaleT, bool X16, int CSM>
 __global__ void __launch_bounds__(kThreads, SC_DENSE_MIN_BLOCKS)
     dense_restore_vec(const __grid_constant__ DenseParams p) {
     __shared__ __align__(16) float s_cos[kMaxHeadDim / 2];
     __shared__ __align__(16) float s_sin[kMaxHeadDim / 2];
+#if SC_DENSE_CPASYNC
+    {
+        constexpr int NR = SC_DENSE_ROUNDS;
+        constexpr bool kPerToken = CSM == kCsToken;
+        __shared__ __align__(16) uint4 s_codes[NR][4][kThreads];
+        const int tid = threadIdx.x;
+        const int P = p.P;
+        const int j = tid % P;
+        const int rl = tid / P;
+        const int RB = blockDim.x / P;
+        const int half = p.D >> 1;
+        const int64_t row0 = static_cast<int64_t>(blockIdx.x) * RB * NR + rl;
+        ScaleT ksc[NR], vsc[NR];
+#pragma unroll
+        for (int k = 0; k < NR; ++k) {
+            const int64_t row = row0 + k * RB;
+            if (row >= p.rows) continue;
+            int64_t l, t, h;
+            row_coords(p, static_cast<uint32_t>(row), l, t, h);
+            if (p.has_k) {
+                const int8_t* base = p.kq + l * p.kq_s[0] + t * p.kq_s[1] + h * p.kq_s[2] + j * 16;
+                cp_async16(&s_codes[k][0][tid], base);
+                cp_async16(&s_codes[k][1][tid], base + half);
+                ksc[k] = reinterpret_cast<const ScaleT*>(p.ks)[l * p.ks_s[0] + t * p.ks_s[1] + h * p.ks_s[2]];
+            }
+            if (p.has_v) {
+                const int8_t* base = p.vq + l * p.vq_s[0] + t * p.vq_s[1] + h * p.vq_s[2] + j * 16;
+                cp_async16(&s_codes[k][2][tid], base);
+                cp_async16(&s_codes[k][3][tid], base + half);
+                vsc[k] = reinterpret_cast<const ScaleT*>(p.vs)[l * p.vs_s[0] + t * p.vs_s[1] + h * p.vs_s[2]];
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        if constexpr (CSM != kCsToken) fill_shared_table(p, s_cos, s_sin);
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        const CsShared cs{reinterpret_cast<const float4*>(s_cos + j * 16),
+                          reinterpret_cast<const float4*>(s_sin + j * 16)};
+#pragma unroll
+        for (int k = 0; k < NR; ++k) {
+            const int64_t row = row0 + k * RB;
+            if (row >= p.rows) continue;
+            RowLoad<ScaleT> r;
+            r.row = static_cast<int32_t>(row);
+            r.ka = s_codes[k][0][tid];
+            r.kb = s_codes[k][1][tid];
+            r.va = s_codes[k][2][tid];
+            r.vb = s_codes[k][3][tid];
+            r.ksc = ksc[k];
+            r.vsc = vsc[k];
+            store_row<OutT, ScaleT, X16, kPerToken>(p, r, j, cs);
+        }
+        return;
+    }
+#endif
     constexpr int R = SC_ROWS_PER_THREAD;
     constexpr bool kPerToken = CSM == kCsToken;
     const int P = p.P;
@@ -383,7 +450,8 @@ template <typename OutT, typename ScaleT, bool X16, int CSM>
 cudaError_t launch_vec(const DenseParams& p, cudaStream_t stream) {
     auto kern = dense_restore_vec<OutT, ScaleT, X16, CSM>;
     const int threads = (kThreads / p.P) * p.P;
-    const int64_t per_block = static_cast<int64_t>(threads / p.P) * SC_ROWS_PER_THREAD;
+    const int64_t per_block = static_cast<int64_t>(threads / p.P) *
+                              (SC_DENSE_CPASYNC ? SC_DENSE_ROUNDS : SC_ROWS_PER_THREAD);
     const int64_t grid = (static_cast<int64_t>(p.rows) + per_block - 1) / per_block;
     kern<<<static_cast<unsigned>(grid), threads, 0, stream>>>(p);
     return cudaGetLastError();

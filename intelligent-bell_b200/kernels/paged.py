@@ -62,7 +62,6 @@ def restore_paged(
     out_offsets=None,
     delta_p_per_page: bool = False,
     fp32_intermediate: bool = False,
-    one_shot_tiles: bool = False,
 ) -> tuple[torch.Tensor | None, torch.Tensor | None, torch.Tensor]:
     """Restore ``R`` ragged requests from a paged INT8 pool.
 
@@ -76,8 +75,6 @@ def restore_paged(
         k_out, v_out: outputs; default packed ``[sum(seq_lens), H, D]`` of ``out_dtype``.
         out_offsets: ``[R]`` element offset of each request's first token in the outputs;
             default: packed (cumulative lengths times the token stride).
-        one_shot_tiles: run the one-shot-tile kernel instead of the streaming one (a testing
-            aid; the library picks it by itself for more than 1024 requests).
 
     Returns ``(k_out, v_out, cu_seqlens)`` with ``cu_seqlens`` int64 ``[R + 1]`` on the host
     (empty when the lengths were given on the device).
@@ -147,8 +144,7 @@ def restore_paged(
         return k_out, v_out, cu
     table, lens, dps, offs = to_device([table, lens, dps, offs], dev)
     status = _status_word(dev)
-    flags = (_lib.SC_FLAG_FP32_INTERMEDIATE if fp32_intermediate else 0) | (
-        _lib.SC_FLAG_PAGED_ONE_SHOT if one_shot_tiles else 0)
+    flags = _lib.SC_FLAG_FP32_INTERMEDIATE if fp32_intermediate else 0
     # The kernel bounds every write by the extent of the output's storage from its data_ptr.
     numel = min(o.untyped_storage().nbytes() // o.element_size() - o.storage_offset()
                 for o in (k_out, v_out) if o is not None)

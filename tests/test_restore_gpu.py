@@ -344,13 +344,12 @@ def _paged_case(oracle, n_req, page, h, d, seed, max_len):
     return pool_kq, pool_ks, pool_vq, pool_vs, table, lens, dps
 
 
-@pytest.mark.parametrize("one_shot", [False, True])
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
-def test_paged_ragged_restore(scb, oracle, out_dtype, one_shot):
+def test_paged_ragged_restore(scb, oracle, out_dtype):
     pkq, pks, pvq, pvs, table, lens, dps = _paged_case(oracle, 9, 64, 8, 128, 1, 700)
     theta = 500000.0
     k, v, cu = scb.restore_paged(pkq.to(DEV), pks.to(DEV), pvq.to(DEV), pvs.to(DEV), table, lens,
-                                 dps, theta=theta, out_dtype=out_dtype, one_shot_tiles=one_shot)
+                                 dps, theta=theta, out_dtype=out_dtype)
     torch.cuda.synchronize()
     assert scb.paged_status(DEV) == 0
     ref = oracle.restore_paged(pkq, pks, pvq, pvs, table, lens, dps, theta, out_dtype=out_dtype)
@@ -361,28 +360,11 @@ def test_paged_ragged_restore(scb, oracle, out_dtype, one_shot):
         assert bits_equal(vg, vr)
 
 
-def _paged_both_kernels(scb, pools, table, lens, dps, **kw):
-    """The streaming and the one-shot-tile kernel on the same call; asserts equal bits."""
-    outs = []
-    for one_shot in (False, True):
-        k, v, cu = scb.restore_paged(*[x.to(DEV) if x is not None else None for x in pools], table,
-                                     lens, dps, one_shot_tiles=one_shot, **kw)
-        torch.cuda.synchronize()
-        outs.append((k, v, cu, scb.paged_status(DEV)))
-    (k0, v0, cu0, st0), (k1, v1, _, st1) = outs
-    assert st0 == st1
-    for a, b in ((k0, k1), (v0, v1)):
-        if a is not None:
-            assert bits_equal(a.cpu(), b.cpu())
-    return k0, v0, cu0, st0
-
-
 @pytest.mark.parametrize("case", ["empty_requests", "single_token", "head_dim_96", "odd_rows",
                                   "head_dim_256", "k_only", "v_only"])
-def test_paged_streaming_edge_cases(scb, oracle, case):
-    # requests of length 0 between others (the walk skips them), one-token requests, tiles that
-    # do not divide a page (head_dim 96: 85 rows per tile), page * heads odd (the streaming
-    # kernel hands over to the one-shot one), head_dim 256, K or V alone
+def test_paged_edge_cases(scb, oracle, case):
+    # requests of length 0 between others, one-token requests, rounds that do not divide a
+    # page (head_dim 96: 42 rows per round), page * heads odd, head_dim 256, K or V alone
     h, d, page = {"head_dim_96": (3, 96, 16), "odd_rows": (3, 64, 5), "head_dim_256": (2, 256, 32)}.get(
         case, (4, 64, 16))
     pkq, pks, pvq, pvs, table, lens, dps = _paged_case(oracle, 6, page, h, d, 17, 60)
@@ -395,8 +377,10 @@ def test_paged_streaming_edge_cases(scb, oracle, case):
         pools = [pkq, pks, None, None]
     if case == "v_only":
         pools = [None, None, pvq, pvs]
-    k, v, cu, st = _paged_both_kernels(scb, pools, table, lens, dps, out_dtype=torch.float16)
-    assert st == 0
+    k, v, cu = scb.restore_paged(*[x.to(DEV) if x is not None else None for x in pools], table,
+                                 lens, dps, out_dtype=torch.float16)
+    torch.cuda.synchronize()
+    assert scb.paged_status(DEV) == 0
     ref = oracle.restore_paged(pkq, pks, pvq, pvs, table, lens, dps)
     for r, (kr, vr) in enumerate(ref):
         if k is not None:
@@ -405,31 +389,18 @@ def test_paged_streaming_edge_cases(scb, oracle, case):
             assert bits_equal(v[cu[r]:cu[r + 1]].cpu(), vr)
 
 
-def test_paged_more_requests_than_the_streaming_kernel_takes(scb, oracle):
-    # 1100 requests: beyond the streaming kernel's 1024, the library uses the one-shot kernel
-    pkq, pks, pvq, pvs, table, lens, dps = _paged_case(oracle, 1100, 8, 2, 32, 23, 20)
+def test_paged_many_requests(scb, oracle):
+    # 1100 requests, a third of them empty
+    pkq, pks, pvq, pvs, table, lens, dps = _paged_case(oracle, 1100, 8, 2, 64, 29, 30)
+    g = torch.Generator().manual_seed(5)
+    for r in torch.randperm(1100, generator=g)[:300].tolist():
+        lens[r] = 0
     k, v, cu = scb.restore_paged(pkq.to(DEV), pks.to(DEV), pvq.to(DEV), pvs.to(DEV), table, lens,
-                                 dps, out_dtype=torch.float16)
+                                 dps, out_dtype=torch.bfloat16)
     torch.cuda.synchronize()
     assert scb.paged_status(DEV) == 0
-    ref = oracle.restore_paged(pkq, pks, pvq, pvs, table, lens, dps)
-    for r in (0, 1, 517, 1023, 1024, 1099):
-        torch.testing.assert_close(k[cu[r]:cu[r + 1]].cpu(), ref[r][0], rtol=1e-2, atol=1e-2)
-        assert bits_equal(v[cu[r]:cu[r + 1]].cpu(), ref[r][1])
-
-
-def test_paged_many_requests_streaming(scb, oracle):
-    # 1024 requests, many of them empty, in the streaming kernel (the scan of lengths spans
-    # four entries per thread)
-    pkq, pks, pvq, pvs, table, lens, dps = _paged_case(oracle, 1024, 8, 2, 64, 29, 30)
-    g = torch.Generator().manual_seed(5)
-    for r in torch.randperm(1024, generator=g)[:300].tolist():
-        lens[r] = 0
-    k, v, cu, st = _paged_both_kernels(scb, [pkq, pks, pvq, pvs], table, lens, dps,
-                                       out_dtype=torch.bfloat16)
-    assert st == 0
     ref = oracle.restore_paged(pkq, pks, pvq, pvs, table, lens, dps, out_dtype=torch.bfloat16)
-    for r in range(0, 1024, 7):
+    for r in range(0, 1100, 7):
         torch.testing.assert_close(k[cu[r]:cu[r + 1]].cpu().float(), ref[r][0].float(),
                                    rtol=1e-2, atol=1e-2)
         assert bits_equal(v[cu[r]:cu[r + 1]].cpu(), ref[r][1])
@@ -449,13 +420,12 @@ def test_paged_per_page_shifts_bitwise_with_tables(scb, oracle):
     assert bits_equal(v.cpu(), vr[: lens[0]])
 
 
-@pytest.mark.parametrize("one_shot", [False, True])
-def test_paged_bad_entries_are_flagged_not_faulted(scb, oracle, one_shot):
+def test_paged_bad_entries_are_flagged_not_faulted(scb, oracle):
     pkq, pks, pvq, pvs, table, lens, dps = _paged_case(oracle, 3, 16, 2, 64, 4, 40)
     bad = table.clone()
     bad[1, 0] = 10_000  # page id outside the pool
     k, v, cu = scb.restore_paged(pkq.to(DEV), pks.to(DEV), pvq.to(DEV), pvs.to(DEV), bad, lens, dps,
-                                 out_dtype=torch.float16, one_shot_tiles=one_shot)
+                                 out_dtype=torch.float16)
     torch.cuda.synchronize()
     assert scb.paged_status(DEV) & scb._lib.SC_STATUS_BAD_PAGE_ID
     # the good requests are restored all the same
@@ -467,7 +437,7 @@ def test_paged_bad_entries_are_flagged_not_faulted(scb, oracle, one_shot):
     out = torch.zeros((sum(lens) + 64, 2, 64), dtype=torch.float16, device=DEV)
     offs = torch.tensor([0, 0, 10**9], dtype=torch.int64)
     scb.restore_paged(pkq.to(DEV), pks.to(DEV), pvq.to(DEV), pvs.to(DEV), table, lens_dev, dps,
-                      k_out=out, v_out=out.clone(), out_offsets=offs, one_shot_tiles=one_shot)
+                      k_out=out, v_out=out.clone(), out_offsets=offs)
     torch.cuda.synchronize()
     bits = scb.paged_status(DEV)
     assert bits & scb._lib.SC_STATUS_BAD_SEQ_LEN and bits & scb._lib.SC_STATUS_BAD_OUT_OFFSET

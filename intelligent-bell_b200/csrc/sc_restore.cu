@@ -196,10 +196,12 @@ enum CsMode : int {
 
 // One-shot tile: block b owns rows [b * RB * R, (b + 1) * RB * R); each thread loads its R
 // row-slices, then converts and stores them.
+#if SC_DENSE_CPASYNC
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
 }
+#endif
 
 template <typename OutT, typename ScaleT, bool X16, int CSM>
 __global__ void __launch_bounds__(kThreads, SC_DENSE_MIN_BLOCKS)

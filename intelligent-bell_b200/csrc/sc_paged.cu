@@ -23,7 +23,14 @@
 //   records and barriers made it issue-bound at 68 % DRAM throughput);
 // * staging every round's rows before converting any: 6.22 -> 6.47 TB/s over loading each
 //   round into registers in turn (the rounds' loads no longer wait for each other); loading
-//   two rows per thread into registers instead was slower (5.63 TB/s, register-bound).
+//   two rows per thread into registers instead was slower (5.63 TB/s, register-bound);
+// * what is left is mostly the page order: with the metadata loads replaced by arithmetic,
+//   a uniform batch streams 6.54 TB/s when its pages are scrambled like the shuffled page
+//   table's and 6.68 TB/s when they are in order, against 6.50-6.51 TB/s for this kernel (a
+//   64 KB page of codes spreads thinly over the DRAM channels, so scattered pages open more
+//   DRAM rows than consecutive ones).  Loading the metadata together with the length, or
+//   prefetching its lines into L1 beside it, measured no gain (the empty blocks of a ragged
+//   batch then wait for, or issue, more).
 //
 // Device-side checks never fault: a page id outside the pool, a bad sequence length or an
 // output range outside out_numel makes the block skip the work and OR a status bit into
@@ -47,11 +54,7 @@ constexpr int kRounds = SC_PAGED_ROUNDS;
 #ifndef SC_PAGED_MIN_BLOCKS
 #define SC_PAGED_MIN_BLOCKS 5
 #endif
-// Issue the page id, output offset and shift loads together with the length load (1), or
-// only once the length shows the page is live (0).
-#ifndef SC_PAGED_META_TOGETHER
-#define SC_PAGED_META_TOGETHER 0
-#endif
+
 
 // Read-only scalar loads kept in program order (volatile), so that metadata loads issued
 // together are not sunk past the early-exit branches that follow them.
@@ -146,27 +149,8 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
     const int r = static_cast<int>(task / p.max_pages);
     const int pg = static_cast<int>(task - static_cast<int64_t>(r) * p.max_pages);
     const bool reporter = chunk == 0 && tid == 0;
-    // Page id, output offset and shift: one memory latency for the three (all in bounds
-    // whatever the length: r < R, pg < max_pages <= table stride).
-    int32_t page_id = 0;
-    void* ko_r = nullptr;
-    void* vo_r = nullptr;
-    int64_t off = 0;
-    float dp = 0.0f;
-    auto load_meta = [&] {
-        page_id = ld_meta(p.table + static_cast<int64_t>(r) * p.table_stride + pg);
-        if constexpr (kPtrs) {
-            if (has_k) ko_r = reinterpret_cast<void*>(ld_meta(reinterpret_cast<const int64_t*>(p.ko_ptrs) + r));
-            if (has_v) vo_r = reinterpret_cast<void*>(ld_meta(reinterpret_cast<const int64_t*>(p.vo_ptrs) + r));
-        } else {
-            off = ld_meta(p.out_off + r);
-        }
-        if (has_k) dp = ld_meta(p.dp + (p.dp_per_page ? task : r));
-    };
-    // The length first: a block past its request's length exits after that load (with
-    // SC_PAGED_META_TOGETHER the other three are already in flight by then).
+    // The length alone first: a block past its request's length exits after one load.
     const int len = ld_meta(p.seq_lens + r);
-    if (SC_PAGED_META_TOGETHER) load_meta();
     if (len < 0 || static_cast<int64_t>(len) > static_cast<int64_t>(p.max_pages) * p.page) {
         if (reporter && pg == 0) atomicOr(p.status, SC_STATUS_BAD_SEQ_LEN);
         return;
@@ -177,7 +161,19 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
     const int64_t rows = static_cast<int64_t>(n_tok) * p.H;
     const int64_t row_begin = static_cast<int64_t>(chunk) * RB * kRounds;
     if (row_begin >= rows) return;
-    if (!SC_PAGED_META_TOGETHER) load_meta();
+    // Page id, output offset and shift together: one memory latency for the three (all in
+    // bounds: r < R, pg < max_pages <= table stride).
+    const int32_t page_id = ld_meta(p.table + static_cast<int64_t>(r) * p.table_stride + pg);
+    void* ko_r = nullptr;
+    void* vo_r = nullptr;
+    int64_t off = 0;
+    if constexpr (kPtrs) {
+        if (has_k) ko_r = reinterpret_cast<void*>(ld_meta(reinterpret_cast<const int64_t*>(p.ko_ptrs) + r));
+        if (has_v) vo_r = reinterpret_cast<void*>(ld_meta(reinterpret_cast<const int64_t*>(p.vo_ptrs) + r));
+    } else {
+        off = ld_meta(p.out_off + r);
+    }
+    const float dp = has_k ? ld_meta(p.dp + (p.dp_per_page ? task : r)) : 0.0f;
     if (page_id < 0 || page_id >= p.n_pool_pages) {
         if (reporter) atomicOr(p.status, SC_STATUS_BAD_PAGE_ID);
         return;

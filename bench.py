@@ -17,11 +17,17 @@ Workloads (synthetic, seeded data with the shapes and value distributions below)
     (``sc_pipeline_restore``, the C ABI): each step copies the 32 layers' codes and
     scales from pinned host slabs (545 MB), restores them, and reads back the last cache
     row of K and V.  ``restore_ms`` is the T = 8192 restore time.
-  - ``cpu_baseline``: the reference's eager CPU arithmetic (the oracle port) on the host
-    cores over a bounded sample (one layer).
+  - ``e2e.h2d_ceiling_gbs``: the copy-only ceiling at the same N - every rank copies its
+    whole pinned slab into HBM with nothing else running, all ranks at once, best of 5 -
+    and ``e2e.h2d_vs_ceiling``, the pipeline's host-to-device rate over it.
+  - ``cpu_baseline``: the reference's own eager functions (speccache/kernels/reference.py
+    from the installed copy under baseline/_ref; the oracle port only if that import
+    fails) on the host cores over a bounded sample (one layer).
   - N > 1 (torchrun): every rank restores its own 8-head shard of an N x 8-head model
     (weak scaling, no collective on the data path); ``value`` = bytes of all ranks over
-    the slowest rank's time.
+    the slowest rank's time.  After the timing, ``gather_check``: every rank restores its
+    heads of a small model into GPU 0's caches over NVLink (HeadShardGather), and GPU 0
+    compares every bit with its own restore of all heads; a mismatch fails the run.
 * ``paged``: ragged paged batch, Llama-3-8B geometry - 64 requests with lengths uniform
   in [256, 8192] and shifts uniform in [0, 4096] from the seed, INT8 pool of 64-token
   pages addressed by a shuffled page table, restored into packed bf16 caches in one
@@ -32,6 +38,11 @@ Workloads (synthetic, seeded data with the shapes and value distributions below)
 * ``llama70b``: Llama-3-70B KV geometry - 80 layers, 8 KV heads x 128, T = 32768, shift
   8192, theta 5e5; pinned host slab -> GPU pipeline; with N GPUs each rank restores 8/N
   heads (strong scaling).  ``value`` is end-to-end (H2D-bound).
+* ``keyshift``: the RoPE shift of already-dequantised fp16 keys (the injector's
+  apply_rope_shift), 32 layers x T = 8192 x 8 heads x 128, shift -384, one launch.
+
+``--impl reference`` times the reference's own CPU implementation of the workload (as the
+``cpu_baseline`` above) on all host threads; under torchrun rank 0 alone runs.
 """
 
 from __future__ import annotations

@@ -12,7 +12,14 @@
 //     copies instead of 128 for a 32-layer restore);
 //   * an event per slot joins the transfer stream to the caller's compute stream, where
 //     the paged restore kernel (identity page table, one shift per block) writes the
-//     layer's K and V; a second event per slot releases the slot for layer l + n_slots.
+//     layer's K and V; a second event per slot releases the slot for layer l + n_slots;
+//   * layer groups (the default where the copy pitches allow): the K and V codes of up to
+//     group_cap layers (64 MiB) go with one 3-D copy per run into a slot, and one kernel
+//     launch restores the group, its layers being the requests of the paged kernel; the last
+//     groups shrink (..., 2, 1, 1) so that one layer's kernel remains after the last copy.
+//     A 32-layer restore then takes 10 copies and launches instead of 32 (a copy costs a few
+//     microseconds of engine time beyond its bytes).  A restore small enough for one
+//     64 MiB buffer is one group of every layer (the all-layers mode).
 // The offload runs the other way: the quantize kernel writes a device staging buffer on
 // the compute stream, an event hands it to the transfer stream, D2H copies fill the slabs.
 // Nothing on the host waits during a restore or an offload while fewer than four earlier
@@ -45,6 +52,8 @@ struct Meta {  // one upload per restore: identity-table length and per-block sh
 // launches and events cost about 8 us of host time per layer, more than the copies of a
 // restore of a few blocks take).
 constexpr size_t kAllLayerBytes = size_t(64) << 20;
+// Largest K + V codes of one layer group in a slot.
+constexpr size_t kGroupBytes = size_t(64) << 20;
 
 size_t meta_bytes(int64_t max_blocks) {
     return sizeof(Meta) + sizeof(float) * static_cast<size_t>(max_blocks > 1 ? max_blocks - 1 : 0);
@@ -146,7 +155,11 @@ struct sc_pipeline {
     int8_t* d_all = nullptr;
     int64_t all_cap_pages = 0;  // capacity in (layer, block) pages; 0 = mode unavailable
     bool codes_3d = false;
-    // kMetaRing host buffers, each seq[L] | dps[all_cap_pages] | k_out[L] | v_out[L]
+    // layer-group mode: slots of group_cap layers (0 = mode unavailable), group sizes in order
+    int32_t group_cap = 0;
+    std::vector<int32_t> group_sizes;
+    // kMetaRing host buffers, each seq[L] | dps[meta_pages] | k_out[L] | v_out[L] (both the
+    // all-layers and the layer-group modes; meta_pages = L x the most blocks they take)
     uint8_t* h_all_meta = nullptr;
     uint8_t* d_all_meta = nullptr;
     size_t all_meta_bytes = 0, all_meta_stride = 0, off_dps = 0, off_kp = 0, off_vp = 0;
@@ -280,17 +293,42 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
     }
     const size_t stage_codes = static_cast<size_t>(max_restore_blocks) * row * head_dim;
     const size_t stage_scales = static_cast<size_t>(max_restore_blocks) * row;
+    int max_pitch = 0;
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&max_pitch, cudaDevAttrMaxPitch, device);
+    const size_t mp = static_cast<size_t>(max_pitch);
+    {
+        // Layer groups need the 3-D copy's pitches (the slab's layer pitch, the staging row) and
+        // the scales' 2-D copy within the device's limit.
+        const size_t blk_codes = row * head_dim;
+        const bool pitches = static_cast<size_t>(n_blocks) * blk_codes <= mp && stage_codes <= mp &&
+                             static_cast<size_t>(n_blocks) * row * 2 <= mp;
+        int64_t cap = static_cast<int64_t>(kGroupBytes / (2 * stage_codes));
+        if (cap > n_layers) cap = n_layers;
+        if (!(flags & SC_PIPE_PER_LAYER) && pitches && cap >= 2) {
+            p->group_cap = static_cast<int32_t>(cap);
+            // sizes from the last group back: 1, 1, 2, 4, ... up to group_cap
+            std::vector<int32_t> rev;
+            int32_t rem = n_layers, g = 1;
+            bool second_one = false;
+            while (rem > 0) {
+                const int32_t take = g < rem ? g : rem;
+                rev.push_back(take);
+                rem -= take;
+                if (g == 1 && !second_one) second_one = true;
+                else g = g * 2 < p->group_cap ? g * 2 : p->group_cap;
+            }
+            p->group_sizes.assign(rev.rbegin(), rev.rend());
+        }
+    }
+    const size_t slot_layers = p->group_cap > 1 ? static_cast<size_t>(p->group_cap) : 1;
     for (int s = 0; s < n_slots && e == cudaSuccess; ++s) {
         int8_t* kv = nullptr;
-        e = cudaMalloc(&kv, 2 * stage_codes);
+        e = cudaMalloc(&kv, 2 * slot_layers * stage_codes);
         p->d_kq.push_back(kv), p->d_vq.push_back(kv ? kv + stage_codes : nullptr);
     }
     if (e == cudaSuccess)
         e = cudaMalloc(&p->d_sc, 2 * static_cast<size_t>(n_layers) * stage_scales * 2);
     if (e == cudaSuccess) {
-        int max_pitch = 0;
-        e = cudaDeviceGetAttribute(&max_pitch, cudaDevAttrMaxPitch, device);
-        const size_t mp = static_cast<size_t>(max_pitch);
         p->codes_2d = slab_codes <= mp && stage_codes <= mp;
         p->scales_2d = static_cast<size_t>(n_blocks) * row * 2 <= mp && stage_scales * 2 <= mp;
         p->offload_scales_2d = slab_scales * 2 <= mp && stage_scales * 2 <= mp;
@@ -305,13 +343,17 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
         if (!(flags & SC_PIPE_PER_LAYER) && max_n >= 1 && p->codes_3d &&
             static_cast<size_t>(n_blocks) * row * 2 <= mp) {
             p->all_cap_pages = max_n * n_layers;
+            e = cudaMalloc(&p->d_all, 2 * static_cast<size_t>(p->all_cap_pages) * blk_codes);
+        }
+        if (e == cudaSuccess && (p->all_cap_pages > 0 || p->group_cap > 1)) {
+            const int64_t meta_pages = p->group_cap > 1 ? n_layers * max_restore_blocks
+                                                        : p->all_cap_pages;
             p->off_dps = (static_cast<size_t>(n_layers) * 4 + 7) / 8 * 8;
-            p->off_kp = p->off_dps + (static_cast<size_t>(p->all_cap_pages) * 4 + 7) / 8 * 8;
+            p->off_kp = p->off_dps + (static_cast<size_t>(meta_pages) * 4 + 7) / 8 * 8;
             p->off_vp = p->off_kp + static_cast<size_t>(n_layers) * 8;
             p->all_meta_bytes = p->off_vp + static_cast<size_t>(n_layers) * 8;
             p->all_meta_stride = round_up64(p->all_meta_bytes);
-            e = cudaMalloc(&p->d_all, 2 * static_cast<size_t>(p->all_cap_pages) * blk_codes);
-            if (e == cudaSuccess) e = cudaMalloc(&p->d_all_meta, p->all_meta_bytes);
+            e = cudaMalloc(&p->d_all_meta, p->all_meta_bytes);
             if (e == cudaSuccess)
                 e = cudaHostAlloc(&p->h_all_meta, kMetaRing * p->all_meta_stride,
                                   cudaHostAllocPortable);
@@ -319,8 +361,10 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
                 e = cudaEventCreateWithFlags(&p->all_meta_uploaded[i], cudaEventDisableTiming);
         }
     }
-    const int64_t table_len = p->all_cap_pages > max_restore_blocks ? p->all_cap_pages
-                                                                     : max_restore_blocks;
+    int64_t table_len = p->all_cap_pages > max_restore_blocks ? p->all_cap_pages
+                                                               : max_restore_blocks;
+    if (p->group_cap > 1 && static_cast<int64_t>(p->group_cap) * max_restore_blocks > table_len)
+        table_len = static_cast<int64_t>(p->group_cap) * max_restore_blocks;
     if (e == cudaSuccess) e = cudaMalloc(&p->d_table, sizeof(int32_t) * table_len);
     if (e == cudaSuccess) e = cudaMalloc(&p->d_meta, meta_bytes(max_restore_blocks));
     if (e == cudaSuccess) e = cudaMalloc(&p->d_status, sizeof(int32_t));
@@ -370,19 +414,24 @@ extern "C" int32_t sc_pipeline_host_slabs(const sc_pipeline* p, int8_t** k_quant
 
 namespace {
 
-// All-layers mode: every layer of the restore in one staging buffer and one launch, the
-// layers being the requests of one paged restore (request l writes layer l's outputs).
-int32_t restore_all_layers(sc_pipeline* p, const int32_t* block_ids, const int32_t* delta_ps,
-                           int32_t n, double theta_base, const float* inv_freq,
-                           void* const* k_out, void* const* v_out, const int64_t* out_strides,
-                           int64_t out_numel, int32_t out_dtype, cudaStream_t cs) {
+// Layer groups: the layers of a group are the requests of one paged restore (request g
+// writes layer l0 + g).  Their K and V codes are staged [2][G][n][block] by one 3-D copy per
+// run of consecutive blocks (rows: layers at the slab's layer pitch; slices: K then V), every
+// layer's scales [2][L][n][chunk * H] by one 2-D copy per run up front.
+//   all_layers: one group of every layer in d_all (restores of at most kAllLayerBytes);
+//   otherwise:  p->group_sizes groups in the slot buffers, the transfer stream filling slot s
+//               while the compute stream restores the groups in the other slots.
+int32_t restore_layer_groups(sc_pipeline* p, bool all_layers, const int32_t* block_ids,
+                             const int32_t* delta_ps, int32_t n, double theta_base,
+                             const float* inv_freq, void* const* k_out, void* const* v_out,
+                             const int64_t* out_strides, int64_t out_numel, int32_t out_dtype,
+                             cudaStream_t cs) {
     const int L = p->L;
     for (int l = 0; l < L; ++l)
         if (((reinterpret_cast<uintptr_t>(k_out[l]) | reinterpret_cast<uintptr_t>(v_out[l])) & 31) != 0)
             return set_error(SC_ERR_INVALID_ARGUMENT, "outputs must be 32-byte aligned (layer %d)", l);
     const size_t row = static_cast<size_t>(p->chunk) * p->H;
     const size_t blk_codes = row * p->D, blk_scales = row;
-    const size_t pages = static_cast<size_t>(L) * n;
     cudaError_t e = cudaSuccess;
     // The next host metadata buffer may still feed an upload kMetaRing restores back.
     const int ms = p->all_meta_next;
@@ -409,63 +458,83 @@ int32_t restore_all_layers(sc_pipeline* p, const int32_t* block_ids, const int32
     if (e != cudaSuccess) return cuda_error(e, "metadata upload");
     p->all_meta_used[ms] = true;
     p->all_meta_next = (ms + 1) % kMetaRing;
-    // Per run of consecutive blocks: K and V codes of every layer with one 3-D copy (rows:
-    // layers at the slab's layer pitch; slices: K then V), packed [2][L][n][block] on the
-    // device; the scales of every layer with one 2-D copy, packed [2][L][n][chunk * H].
+    // Runs of consecutive block ids: fn(first block, position in the restore, length).
+    auto for_runs = [&](auto&& fn) {
+        for (int32_t i = 0; i < n && e == cudaSuccess;) {
+            int32_t rn = 1;
+            while (i + rn < n && block_ids[i + rn] == block_ids[i] + rn) ++rn;
+            fn(static_cast<size_t>(block_ids[i]), static_cast<size_t>(i), static_cast<size_t>(rn));
+            i += rn;
+        }
+    };
+    for_runs([&](size_t b0, size_t i, size_t rn) {
+        e = cudaMemcpy2DAsync(p->d_sc + i * blk_scales, static_cast<size_t>(n) * blk_scales * 2,
+                              p->h_ks + b0 * blk_scales, static_cast<size_t>(p->B) * blk_scales * 2,
+                              rn * blk_scales * 2, 2 * static_cast<size_t>(L),
+                              cudaMemcpyHostToDevice, p->transfer);
+    });
+    if (e != cudaSuccess) return cuda_error(e, "scale copies");
     const size_t src_pitch = static_cast<size_t>(p->B) * blk_codes;
-    for (int32_t i = 0; i < n && e == cudaSuccess;) {
-        int32_t rn = 1;
-        while (i + rn < n && block_ids[i + rn] == block_ids[i] + rn) ++rn;
-        const size_t b0 = static_cast<size_t>(block_ids[i]);
-        cudaMemcpy3DParms m = {};
-        m.srcPtr = make_cudaPitchedPtr(p->h_kq + b0 * blk_codes, src_pitch, rn * blk_codes, L);
-        m.dstPtr = make_cudaPitchedPtr(p->d_all + static_cast<size_t>(i) * blk_codes,
-                                       static_cast<size_t>(n) * blk_codes, rn * blk_codes, L);
-        m.extent = make_cudaExtent(rn * blk_codes, L, 2);
-        m.kind = cudaMemcpyHostToDevice;
-        e = cudaMemcpy3DAsync(&m, p->transfer);
-        if (e == cudaSuccess)
-            e = cudaMemcpy2DAsync(p->d_sc + static_cast<size_t>(i) * blk_scales,
-                                  static_cast<size_t>(n) * blk_scales * 2,
-                                  p->h_ks + b0 * blk_scales, static_cast<size_t>(p->B) * blk_scales * 2,
-                                  rn * blk_scales * 2, 2 * static_cast<size_t>(L),
-                                  cudaMemcpyHostToDevice, p->transfer);
-        i += rn;
+    const size_t n_groups = all_layers ? 1 : p->group_sizes.size();
+    int32_t l0 = 0;
+    for (size_t gi = 0; gi < n_groups; ++gi) {
+        const int32_t G = all_layers ? L : p->group_sizes[gi];
+        const int s = all_layers ? 0 : static_cast<int>(gi % static_cast<size_t>(p->n_slots));
+        if (!all_layers && p->slot_used[s]) e = cudaStreamWaitEvent(p->transfer, p->slot_free[s], 0);
+        int8_t* stage = all_layers ? p->d_all : p->d_kq[s];
+        const size_t pages = static_cast<size_t>(G) * n;
+        for_runs([&](size_t b0, size_t i, size_t rn) {
+            cudaMemcpy3DParms m = {};
+            m.srcPtr = make_cudaPitchedPtr(p->h_kq, src_pitch, src_pitch, static_cast<size_t>(L));
+            m.srcPos = make_cudaPos(b0 * blk_codes, static_cast<size_t>(l0), 0);
+            m.dstPtr = make_cudaPitchedPtr(stage, static_cast<size_t>(n) * blk_codes,
+                                           static_cast<size_t>(n) * blk_codes, static_cast<size_t>(G));
+            m.dstPos = make_cudaPos(i * blk_codes, 0, 0);
+            m.extent = make_cudaExtent(rn * blk_codes, static_cast<size_t>(G), 2);
+            m.kind = cudaMemcpyHostToDevice;
+            e = cudaMemcpy3DAsync(&m, p->transfer);
+        });
+        if (e == cudaSuccess) e = cudaEventRecord(p->ready[s], p->transfer);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, p->ready[s], 0);
+        if (e != cudaSuccess) return cuda_error(e, "layer-group copies");
+        sc::PagedArgs a{};
+        a.n_requests = G;
+        a.max_pages = n;
+        a.page_size = p->chunk;
+        a.n_heads = p->H;
+        a.head_dim = p->D;
+        a.n_pool_pages = static_cast<int64_t>(pages);
+        a.pool_kq = stage;
+        a.pool_vq = stage + pages * blk_codes;
+        a.pool_ks = p->d_sc + static_cast<size_t>(l0) * n * blk_scales;
+        a.pool_vs = p->d_sc + (static_cast<size_t>(L) + l0) * n * blk_scales;
+        a.page_table = p->d_table;  // identity: page i of request g is page g * n + i
+        a.page_table_stride = n;
+        a.seq_lens = reinterpret_cast<const int32_t*>(p->d_all_meta) + l0;
+        a.delta_p = reinterpret_cast<const float*>(p->d_all_meta + p->off_dps) + static_cast<size_t>(l0) * n;
+        a.delta_p_per_page = 1;
+        a.theta_base = theta_base;
+        a.inv_freq = inv_freq;
+        a.k_out_ptrs = reinterpret_cast<const uint64_t*>(p->d_all_meta + p->off_kp) + l0;
+        a.v_out_ptrs = reinterpret_cast<const uint64_t*>(p->d_all_meta + p->off_vp) + l0;
+        for (int i = 0; i < 3; ++i) a.out_strides[i] = out_strides[i];
+        a.out_numel = out_numel;
+        a.out_dtype = out_dtype;
+        a.status = p->d_status;
+        a.stream = cs;
+        const int32_t rc = sc::launch_paged(a);
+        if (rc != SC_OK) return rc;
+        if (!all_layers) {
+            e = cudaEventRecord(p->slot_free[s], cs);
+            if (e != cudaSuccess) return cuda_error(e, "restore enqueue");
+            p->slot_used[s] = true;
+        }
+        l0 += G;
     }
-    if (e == cudaSuccess) e = cudaEventRecord(p->ready[0], p->transfer);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, p->ready[0], 0);
-    if (e != cudaSuccess) return cuda_error(e, "all-layers copies");
-    sc::PagedArgs a{};
-    a.n_requests = L;
-    a.max_pages = n;
-    a.page_size = p->chunk;
-    a.n_heads = p->H;
-    a.head_dim = p->D;
-    a.n_pool_pages = static_cast<int64_t>(pages);
-    a.pool_kq = p->d_all;
-    a.pool_vq = p->d_all + pages * blk_codes;
-    a.pool_ks = p->d_sc;
-    a.pool_vs = p->d_sc + pages * blk_scales;
-    a.page_table = p->d_table;  // identity: page i of request l is page l * n + i
-    a.page_table_stride = n;
-    a.seq_lens = reinterpret_cast<const int32_t*>(p->d_all_meta);
-    a.delta_p = reinterpret_cast<const float*>(p->d_all_meta + p->off_dps);
-    a.delta_p_per_page = 1;
-    a.theta_base = theta_base;
-    a.inv_freq = inv_freq;
-    a.k_out_ptrs = reinterpret_cast<const uint64_t*>(p->d_all_meta + p->off_kp);
-    a.v_out_ptrs = reinterpret_cast<const uint64_t*>(p->d_all_meta + p->off_vp);
-    for (int i = 0; i < 3; ++i) a.out_strides[i] = out_strides[i];
-    a.out_numel = out_numel;
-    a.out_dtype = out_dtype;
-    a.status = p->d_status;
-    a.stream = cs;
-    const int32_t rc = sc::launch_paged(a);
-    if (rc != SC_OK) return rc;
     e = cudaEventRecord(p->done, cs);
     if (e != cudaSuccess) return cuda_error(e, "restore enqueue");
     p->any_restore = true;
-    p->any_all = true;
+    if (all_layers) p->any_all = true;
     return sc::ok();
 }
 
@@ -494,9 +563,10 @@ extern "C" int32_t sc_pipeline_restore(sc_pipeline* p, const int32_t* block_ids,
     DeviceGuard g(p->device);
     if (!g.ok) return set_error(SC_ERR_CUDA, "cudaSetDevice(%d) failed", p->device);
     cudaStream_t cs = static_cast<cudaStream_t>(compute_stream);
-    if (static_cast<int64_t>(p->L) * n_blocks <= p->all_cap_pages)
-        return restore_all_layers(p, block_ids, delta_ps, n_blocks, theta_base, inv_freq, k_out,
-                                  v_out, out_strides, out_numel, out_dtype, cs);
+    if (static_cast<int64_t>(p->L) * n_blocks <= p->all_cap_pages || p->group_cap > 1)
+        return restore_layer_groups(p, static_cast<int64_t>(p->L) * n_blocks <= p->all_cap_pages,
+                                    block_ids, delta_ps, n_blocks, theta_base, inv_freq, k_out,
+                                    v_out, out_strides, out_numel, out_dtype, cs);
     cudaError_t e = cudaSuccess;
 
     // Metadata: the next host buffer may still feed an upload kMetaRing restores back.

@@ -189,6 +189,52 @@ def test_all_layers_restore_equals_per_layer(scb, oracle, n_blocks):
         assert bits_equal(outs[0][1][layer], outs[1][1][layer])
 
 
+def test_layer_group_restore_equals_per_layer(scb, oracle):
+    # a restore beyond the all-layers buffer (64 MiB of codes) takes the layer-group path:
+    # groups of up to 6 layers (64 MiB of codes each) here 4, 2, 1, 1 after a first group of 1,
+    # one 3-D copy per run of blocks and group, one launch per group, the groups rotating over
+    # two slots.  Two restores back to back (the second reuses the slots and the scales); both
+    # must write exactly what the layer-by-layer path writes.
+    from speccache_b200.cache import KVRestorePipeline
+
+    layers, blocks, chunk, h, d = 9, 80, 64, 8, 128
+    ids_a = list(range(10, 40)) + list(range(0, 10)) + [45, 44, 43] + list(range(50, 77))
+    ids_b = list(range(79, 59, -1)) + list(range(0, 50))
+    g = torch.Generator().manual_seed(77)
+    dps_a = torch.randint(-3000, 3000, (len(ids_a),), generator=g).tolist()
+    dps_b = torch.randint(-3000, 3000, (len(ids_b),), generator=g).tolist()
+    n_a, n_b = len(ids_a) * chunk, len(ids_b) * chunk
+    outs = []
+    for per_layer in (False, True):
+        with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV, per_layer=per_layer) as pipe:
+            g2 = torch.Generator().manual_seed(101)
+            for t in (pipe.k_quant, pipe.v_quant):
+                t.copy_(torch.randint(-127, 128, tuple(t.shape), generator=g2, dtype=torch.int8))
+            for t in (pipe.k_scale, pipe.v_scale):
+                t.copy_((torch.rand(tuple(t.shape), generator=g2) * 0.05 + 1e-3).half())
+            ka = torch.zeros((layers, n_a, h, d), dtype=torch.bfloat16, device=DEV)
+            va = torch.zeros_like(ka)
+            kb = torch.zeros((layers, n_b, h, d), dtype=torch.float16, device=DEV)
+            vb = torch.zeros_like(kb)
+            pipe.restore(ids_a, dps_a, ka, va, theta=5e5)
+            pipe.restore(ids_b, dps_b, kb, vb, theta=1e4)
+            pipe.synchronize()
+            assert pipe.status() == 0
+            outs.append([x.cpu() for x in (ka, va, kb, vb)])
+            if not per_layer:
+                for layer in (0, 4, 8):
+                    for ids, dps, theta, k, v, dt in ((ids_a, dps_a, 5e5, ka, va, torch.bfloat16),
+                                                      (ids_b, dps_b, 1e4, kb, vb, torch.float16)):
+                        kr, vr = oracle.restore_blocks(pipe.k_quant[layer], pipe.k_scale[layer],
+                                                       pipe.v_quant[layer], pipe.v_scale[layer],
+                                                       ids, dps, theta, dt)
+                        assert bits_equal(v[layer].cpu(), vr)
+                        torch.testing.assert_close(k[layer].cpu().float(), kr.float(), rtol=1e-2,
+                                                   atol=1e-2)
+    for grouped, per_layer in zip(outs[0], outs[1]):
+        assert bits_equal(grouped, per_layer)
+
+
 def test_offload_staging_ring_and_join(scb, oracle):
     # successive offloads alternate two staging slots (the third reuses the first); join makes
     # the current stream wait for their copies on the GPU, after which the slabs hold the

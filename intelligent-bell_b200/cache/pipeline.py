@@ -41,9 +41,11 @@ class KVRestorePipeline:
         numa_local: allocate the slabs from a thread bound to the GPU's NUMA node.
         write_combined: pin the slabs write-combined (host writes and GPU reads only; host
             reads of the slab views become very slow).
-        per_layer: always restore layer by layer; by default a small restore (K and V codes
+        per_layer: always restore layer by layer.  By default a small restore (K and V codes
             of all layers within 64 MiB) is copied with one 3-D copy per run of blocks and
-            restored by one launch for all layers.
+            restored by one launch for all layers, and a larger one goes in groups of layers
+            (up to 64 MiB of codes each, the last groups shrinking to one layer): one 3-D copy
+            per run and one launch per group.
     """
 
     def __init__(self, num_layers: int, num_blocks: int, chunk_size: int, num_kv_heads: int,

@@ -166,7 +166,6 @@ struct sc_pipeline {
     cudaEvent_t all_meta_uploaded[kMetaRing] = {};
     bool all_meta_used[kMetaRing] = {};
     int all_meta_next = 0;
-    bool any_all = false;
     // offload: quantize into one of two device staging slots (K then V codes in one
     // allocation, K then V scales in another), then D2H into the slabs
     int8_t* o_codes[2] = {nullptr, nullptr};
@@ -534,7 +533,6 @@ int32_t restore_layer_groups(sc_pipeline* p, bool all_layers, const int32_t* blo
     e = cudaEventRecord(p->done, cs);
     if (e != cudaSuccess) return cuda_error(e, "restore enqueue");
     p->any_restore = true;
-    if (all_layers) p->any_all = true;
     return sc::ok();
 }
 

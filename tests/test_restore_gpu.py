@@ -266,6 +266,35 @@ def test_generic_path_odd_strides(scb, oracle):
     assert bits_equal(e34.cpu(), oracle.dequant_rope_shift(kq34, ks34, c34, s34))
 
 
+@pytest.mark.parametrize("fp32", [False, True])
+def test_zero_shift_is_plain_dequant(scb, oracle, fp32):
+    # reference tests/test_correctness.py:91-106: a shift of 0 equals the plain dequant (here
+    # bit for bit: cos 1 and sin 0 are exact, so the rotation returns x unchanged), through the
+    # tables and through the shift expanded in the kernel
+    t, h, d = 16, 4, 64
+    kq, ks = _quantized(oracle, t, h, d, 61)
+    direct = oracle.dequant_value(kq, ks)
+    cos, sin = scb.compute_rope_cos_sin_delta(torch.tensor([0]), d, device=DEV)
+    torch.cuda.synchronize()
+    assert torch.equal(cos.cpu(), torch.ones_like(cos.cpu())) and torch.equal(sin.cpu(), torch.zeros_like(sin.cpu()))
+    a = scb.triton_fused_k_dequant_rope_shift(kq.to(DEV), ks.to(DEV), cos, sin, fp32_intermediate=fp32)
+    b = scb.triton_fused_k_dequant_rope_shift(kq.to(DEV), ks.to(DEV), delta_p=0, fp32_intermediate=fp32)
+    torch.cuda.synchronize()
+    assert bits_equal(a.cpu(), direct) and bits_equal(b.cpu(), direct)
+
+
+def test_rotational_composition(scb, oracle):
+    # reference tests/test_correctness.py:109-140: R(15 + 27) == R(27) R(15), the second
+    # rotation by the key-shift kernel on the first one's fp16 output (reference tolerance 1e-3)
+    t, h, d = 8, 2, 64
+    kq, ks = _quantized(oracle, t, h, d, 62)
+    direct = scb.pytorch_eager_dequant_rope_shift(kq.to(DEV), ks.to(DEV), delta_p=42)
+    step1 = scb.pytorch_eager_dequant_rope_shift(kq.to(DEV), ks.to(DEV), delta_p=15)
+    composed = scb.rope_shift_keys(step1, 27)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(composed.cpu(), direct.cpu(), rtol=1e-3, atol=1e-3)
+
+
 def test_end_to_end_rotational_equivalence(scb, oracle):
     # reference tests/test_correctness.py:172-235 with the quantize twin on the GPU
     g = torch.Generator().manual_seed(999)

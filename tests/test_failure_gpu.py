@@ -9,9 +9,10 @@ the host (nothing here faults, traps or hangs the GPU):
   results are right;
 * ``preload()`` loads every kernel up front, so a fresh process's first calls enqueued behind
   running work do not wait for it;
-* stream hazards: back-to-back restores and offloads that reuse the staging slots (or the
-  all-layers staging), the shift metadata and the offload slots, with random GPU-side delays on
-  the compute stream and random host delays between enqueues, all checked against the oracle.
+* stream hazards: back-to-back restores and offloads that reuse the staging slots (on the
+  all-layers, layer-group and layer-by-layer paths), the shift metadata and the offload slots,
+  with random GPU-side delays on the compute stream and random host delays between enqueues,
+  all checked against the oracle.
 """
 
 from __future__ import annotations
@@ -125,19 +126,30 @@ def test_preloaded_first_calls_do_not_wait_for_the_device(scb):
     assert dt < 0.25, out.stdout
 
 
-@pytest.mark.parametrize("per_layer", [False, True])
+# The restore paths: small restores in one all-layers launch, larger ones in layer groups
+# (here 90-100 blocks of 64 tokens x 8 heads: groups of 2, 2, 1, 1 layers over two slots), and
+# layer by layer.
+PATHS = {
+    "all_layers": dict(blocks=12, chunk=32, h=4, per_layer=False, n=(1, 8)),
+    "layer_groups": dict(blocks=100, chunk=64, h=8, per_layer=False, n=(90, 98)),
+    "per_layer": dict(blocks=12, chunk=32, h=4, per_layer=True, n=(1, 8)),
+}
+
+
+@pytest.mark.parametrize("path", sorted(PATHS))
 @pytest.mark.parametrize("seed", [0, 1, 2])
-def test_stream_hazards_under_random_delays(scb, oracle, seed, per_layer):
+def test_stream_hazards_under_random_delays(scb, oracle, seed, path):
     from speccache_b200.cache import KVRestorePipeline
 
     rng = random.Random(seed)
-    layers, blocks, chunk, h, d = 6, 12, 32, 4, 128
+    geo = PATHS[path]
+    layers, blocks, chunk, h, d = 6, geo["blocks"], geo["chunk"], geo["h"], 128
     with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV, n_slots=2,
-                           per_layer=per_layer) as pipe:
+                           per_layer=geo["per_layer"]) as pipe:
         _fill(pipe, 10 + seed)
         jobs = []
         for _ in range(4):  # restores that reuse the slots and the shift metadata
-            ids = rng.sample(range(blocks), rng.randint(1, 8))
+            ids = rng.sample(range(blocks - 2), rng.randint(*geo["n"]))
             dps = [rng.randint(-5000, 5000) for _ in ids]
             k_out = torch.empty((layers, len(ids) * chunk, h, d), dtype=torch.float16, device=DEV)
             v_out = torch.empty_like(k_out)

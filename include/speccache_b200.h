@@ -309,6 +309,13 @@ SC_API int32_t sc_pipeline_join(sc_pipeline* p, void* stream);
 /* Read and clear the device status word of the pipeline's kernels (synchronises). */
 SC_API int32_t sc_pipeline_status(sc_pipeline* p, int32_t* status_bits);
 
+/* How sc_pipeline_restore would run a restore of n_blocks blocks: the kernel launches it
+ * issues (1 for a restore small enough for the all-layers buffer, one per layer group for
+ * larger ones, one per layer when the groups are off) into *launches.  No device work.  No
+ * counterpart in the reference (it launches two kernels per chunk and layer). */
+SC_API int32_t sc_pipeline_restore_launches(const sc_pipeline* p, int32_t n_blocks,
+                                            int32_t* launches);
+
 SC_API int32_t sc_pipeline_destroy(sc_pipeline* p);
 
 /*

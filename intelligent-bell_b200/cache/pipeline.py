@@ -3,10 +3,10 @@
 Python face of ``sc_pipeline_*``: it owns pinned host slabs laid out like the
 reference's unified multi-layer slabs (speccache/serving/kv_injector.py:171-192,
 ``[L, blocks, chunk, H, D]`` int8 and ``[L, blocks, chunk, H, 1]`` fp16), and restores a
-list of blocks for every layer: per layer, H2D copies (one per run of consecutive block
-ids) on its own transfer stream into a ring of device slots, joined by events to the
-restore kernel on the caller's current stream, so layer l+1's copy overlaps layer l's
-kernel.  This replaces the Python loops of
+list of blocks for every layer: per group of layers (or per layer), H2D copies (one per run
+of consecutive block ids) on its own transfer stream into a ring of device slots, joined by
+events to the restore kernel on the caller's current stream, so the next group's copy
+overlaps this group's kernel.  This replaces the Python loops of
 ``MultiLayerKVInjector.reconstruct_and_inject_multi_layer`` (kv_injector.py:392-498)
 and ``SpecCacheEngine.execute_async_dma_and_rope`` (speccache/cache/engine.py:441-601).
 """
@@ -216,6 +216,14 @@ class KVRestorePipeline:
         offloads enqueued so far, copies included; the host does not wait."""
         handle = stream.cuda_stream if stream is not None else _lib.stream_handle(self.device)
         _lib.check(self._lib.sc_pipeline_join(self._h, handle), "sc_pipeline_join")
+
+    def restore_launches(self, n_blocks: int) -> int:
+        """Kernel launches a restore of ``n_blocks`` blocks issues: 1 when it fits the
+        all-layers buffer, one per layer group above that, one per layer with ``per_layer``."""
+        count = ctypes.c_int32(0)
+        _lib.check(self._lib.sc_pipeline_restore_launches(self._h, int(n_blocks), ctypes.byref(count)),
+                   "sc_pipeline_restore_launches")
+        return int(count.value)
 
     def status(self) -> int:
         """Device status bits of the restore kernels (0 = clean); reading clears them."""

@@ -538,6 +538,23 @@ int32_t restore_layer_groups(sc_pipeline* p, bool all_layers, const int32_t* blo
 
 }  // namespace
 
+extern "C" int32_t sc_pipeline_restore_launches(const sc_pipeline* p, int32_t n_blocks,
+                                                int32_t* launches) {
+    if (!p || !launches) return set_error(SC_ERR_INVALID_ARGUMENT, "null argument");
+    if (n_blocks < 0 || n_blocks > p->max_blocks)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "n_blocks %d outside [0, %lld]", n_blocks,
+                         (long long)p->max_blocks);
+    if (n_blocks == 0)
+        *launches = 0;
+    else if (static_cast<int64_t>(p->L) * n_blocks <= p->all_cap_pages)
+        *launches = 1;
+    else if (p->group_cap > 1)
+        *launches = static_cast<int32_t>(p->group_sizes.size());
+    else
+        *launches = p->L;
+    return sc::ok();
+}
+
 extern "C" int32_t sc_pipeline_restore(sc_pipeline* p, const int32_t* block_ids,
                                        const int32_t* delta_ps, int32_t n_blocks,
                                        double theta_base, const float* inv_freq,

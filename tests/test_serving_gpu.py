@@ -216,6 +216,9 @@ def test_layer_group_restore_equals_per_layer(scb, oracle):
             va = torch.zeros_like(ka)
             kb = torch.zeros((layers, n_b, h, d), dtype=torch.float16, device=DEV)
             vb = torch.zeros_like(kb)
+            # groups of 1, 4, 2, 1, 1 layers (6 fit 64 MiB of codes here), or one per layer
+            assert pipe.restore_launches(len(ids_a)) == (layers if per_layer else 5)
+            assert pipe.restore_launches(4) == (layers if per_layer else 1)  # all-layers buffer
             pipe.restore(ids_a, dps_a, ka, va, theta=5e5)
             pipe.restore(ids_b, dps_b, kb, vb, theta=1e4)
             pipe.synchronize()

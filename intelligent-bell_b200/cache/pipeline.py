@@ -44,8 +44,8 @@ class KVRestorePipeline:
         per_layer: always restore layer by layer.  By default a small restore (K and V codes
             of all layers within 64 MiB) is copied with one 3-D copy per run of blocks and
             restored by one launch for all layers, and a larger one goes in groups of layers
-            (up to 64 MiB of codes each, the last groups shrinking to one layer): one 3-D copy
-            per run and one launch per group.
+            (up to 64 MiB of codes each, the last group one layer): one 3-D copy per run and
+            one launch per group.
     """
 
     def __init__(self, num_layers: int, num_blocks: int, chunk_size: int, num_kv_heads: int,

@@ -16,8 +16,8 @@
 //   * layer groups (the default where the copy pitches allow): the K and V codes of up to
 //     group_cap layers (64 MiB) go with one 3-D copy per run into a slot, and one kernel
 //     launch restores the group, its layers being the requests of the paged kernel; the last
-//     groups shrink (..., 2, 1, 1) so that one layer's kernel remains after the last copy.
-//     A 32-layer restore then takes 10 copies and launches instead of 32 (a copy costs a few
+//     group is one layer, so that one layer's kernel remains after the last copy.  A 32-layer
+//     restore then takes 9 copies and launches instead of 32 (a copy costs a few
 //     microseconds of engine time beyond its bytes).  A restore small enough for one
 //     64 MiB buffer is one group of every layer (the all-layers mode).
 // The offload runs the other way: the quantize kernel writes a device staging buffer on
@@ -305,18 +305,15 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
         if (cap > n_layers) cap = n_layers;
         if (!(flags & SC_PIPE_PER_LAYER) && pitches && cap >= 2) {
             p->group_cap = static_cast<int32_t>(cap);
-            // sizes from the last group back: 1, 1, 2, 4, ... up to group_cap
-            std::vector<int32_t> rev;
-            int32_t rem = n_layers, g = 1;
-            bool second_one = false;
-            while (rem > 0) {
-                const int32_t take = g < rem ? g : rem;
-                rev.push_back(take);
-                rem -= take;
-                if (g == 1 && !second_one) second_one = true;
-                else g = g * 2 < p->group_cap ? g * 2 : p->group_cap;
-            }
-            p->group_sizes.assign(rev.rbegin(), rev.rend());
+            // The last group is one layer: its kernel is the only one left after the last copy
+            // (every other group's kernels run while the next group's copy, about 40x longer,
+            // is in flight).  The layers before it go in as few groups of at most group_cap as
+            // possible, of nearly equal size.
+            const int32_t front = n_layers - 1;
+            const int32_t n_front = (front + p->group_cap - 1) / p->group_cap;
+            for (int32_t i = 0; i < n_front; ++i)
+                p->group_sizes.push_back(front / n_front + (i < front % n_front ? 1 : 0));
+            p->group_sizes.push_back(1);
         }
     }
     const size_t slot_layers = p->group_cap > 1 ? static_cast<size_t>(p->group_cap) : 1;

@@ -127,7 +127,7 @@ def test_preloaded_first_calls_do_not_wait_for_the_device(scb):
 
 
 # The restore paths: small restores in one all-layers launch, larger ones in layer groups
-# (here 90-100 blocks of 64 tokens x 8 heads: groups of 2, 2, 1, 1 layers over two slots), and
+# (here 90-98 blocks of 64 tokens x 8 heads: groups of 5 and 1 layers over two slots), and
 # layer by layer.
 PATHS = {
     "all_layers": dict(blocks=12, chunk=32, h=4, per_layer=False, n=(1, 8)),

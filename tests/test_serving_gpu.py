@@ -237,6 +237,55 @@ def test_layer_group_restore_equals_per_layer(scb, oracle):
         assert bits_equal(grouped, per_layer)
 
 
+@pytest.mark.parametrize("seed", range(6))
+def test_layer_groups_random_geometries(scb, oracle, seed):
+    # restores just beyond the all-layers buffer, with random layer counts, block lists (runs
+    # and jumps), slot counts, max_restore_blocks and output dtypes: the grouped path must
+    # write the bits of the layer-by-layer path, in fewer launches, and match the oracle
+    import random
+
+    from speccache_b200.cache import KVRestorePipeline
+
+    rng = random.Random(1000 + seed)
+    layers = rng.randint(2, 12)
+    chunk, h, d = rng.choice([(64, 8, 128), (32, 8, 128), (64, 4, 256), (128, 8, 64)])
+    need = (64 << 20) // (2 * chunk * h * d) // layers + 1  # blocks that pass the 64 MiB buffer
+    blocks = need + rng.randint(5, 40)
+    n = rng.randint(need, blocks)
+    ids = rng.sample(range(blocks), n)
+    step = rng.choice([1, 4, 16])
+    ids.sort(key=lambda x: x // step)  # runs of consecutive ids and jumps
+    dps = [rng.randint(-6000, 6000) for _ in ids]
+    dtype = rng.choice([torch.float16, torch.bfloat16])
+    n_slots, max_rb = rng.randint(1, 3), rng.randint(n, blocks)
+    g = torch.Generator().manual_seed(seed)
+    data, outs, launches = None, [], []
+    for per_layer in (False, True):
+        with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV, n_slots=n_slots,
+                               max_restore_blocks=max_rb, per_layer=per_layer) as pipe:
+            slabs = (pipe.k_quant, pipe.k_scale, pipe.v_quant, pipe.v_scale)
+            if data is None:
+                data = [torch.randint(-127, 128, tuple(x.shape), generator=g, dtype=torch.int8)
+                        if x.dtype == torch.int8 else
+                        (torch.rand(tuple(x.shape), generator=g) * 0.05 + 1e-3).half() for x in slabs]
+            for dst, src in zip(slabs, data):
+                dst.copy_(src)
+            ko = torch.empty((layers, n * chunk, h, d), dtype=dtype, device=DEV)
+            vo = torch.empty_like(ko)
+            launches.append(pipe.restore_launches(n))
+            pipe.restore(ids, dps, ko, vo, theta=5e5)
+            pipe.synchronize()
+            assert pipe.status() == 0
+            outs.append((ko.cpu(), vo.cpu()))
+    assert launches[1] == layers and launches[0] <= layers and (layers < 3 or launches[0] < layers)
+    assert bits_equal(outs[0][0], outs[1][0]) and bits_equal(outs[0][1], outs[1][1])
+    layer = rng.randrange(layers)
+    kr, vr = oracle.restore_blocks(data[0][layer], data[1][layer], data[2][layer], data[3][layer],
+                                   ids, dps, 5e5, dtype)
+    assert bits_equal(outs[0][1][layer], vr)
+    torch.testing.assert_close(outs[0][0][layer].float(), kr.float(), rtol=1e-2, atol=1e-2)
+
+
 def test_offload_staging_ring_and_join(scb, oracle):
     # successive offloads alternate two staging slots (the third reuses the first); join makes
     # the current stream wait for their copies on the GPU, after which the slabs hold the

@@ -190,14 +190,26 @@ class ClockSampler:
 
 class Dist:
     """One process per GPU (torchrun env); barrier and max-over-ranks over the process
-    group (NCCL on GPUs; gloo on CPU for the host-side tests)."""
+    group (NCCL on GPUs; gloo on CPU for the host-side tests).
 
-    def __init__(self, backend: str = "nccl") -> None:
+    Placement: with more GPUs visible than local ranks, rank r takes GPU r * (visible // ranks)
+    (``spread``), so the ranks sit on GPUs that do not share a host link where the machine
+    groups its GPUs' links: on these B200 machines GPUs 0-3 share about 115 GB/s of
+    host-to-device bandwidth, while four spread GPUs move 213-217 GB/s.  ``spread=False``
+    keeps rank r on GPU r."""
+
+    def __init__(self, backend: str = "nccl", spread: bool = True) -> None:
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.placement = None
         if backend == "nccl":
-            self.device = torch.device("cuda", self.local)
+            local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(self.world)))
+            visible = torch.cuda.device_count()
+            stride = max(1, visible // max(1, local_world)) if spread else 1
+            self.device = torch.device("cuda", self.local * stride)
+            self.placement = {"visible_gpus": visible, "rank_to_gpu_stride": stride,
+                              "gpus": [r * stride for r in range(local_world)]}
             torch.cuda.set_device(self.device)
         else:
             self.device = torch.device("cpu")
@@ -930,7 +942,7 @@ def bench_llama70b(args, scb, dist: Dist, cfg: dict):
 
 
 def run_ours(args) -> None:
-    dist = Dist()
+    dist = Dist(spread=not args.pack_ranks)
     scb = importlib.import_module("intelligent-bell_b200")
     cfg = WORKLOADS[args.workload]
     fn = {"llama8b": bench_llama8b, "paged": bench_paged, "roundtrip": bench_roundtrip,
@@ -950,6 +962,8 @@ def run_ours(args) -> None:
                          + str(cfg["out"]).replace("torch.", "") + " out",
                 "data": "synthetic: seeded, see config",
                 "config": workload_config(args.workload, cfg, dist.world, args.gather)}
+        if dist.world > 1:
+            line["config"]["placement"] = dist.placement
         line.update(part)
         line["clocks"] = clocks.summary()
         if dist.world == 1 and not args.skip_cpu_baseline:
@@ -974,6 +988,9 @@ def main() -> None:
     ap.add_argument("--skip-cpu-baseline", action="store_true", help="profiling aid")
     ap.add_argument("--write-combined", action="store_true",
                     help="pin the host slabs write-combined (pipeline workloads)")
+    ap.add_argument("--pack-ranks", action="store_true",
+                    help="N > 1: rank r on GPU r even when more GPUs are visible (default: "
+                         "spread the ranks over the visible GPUs)")
     ap.add_argument("--skip-gather-check", action="store_true",
                     help="N > 1: skip the in-run check of the head-shard gather onto GPU 0")
     ap.add_argument("--gather", action="store_true",

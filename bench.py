@@ -188,6 +188,13 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm), "samples_under_load": len(loaded)}
 
 
+def rank_gpus(local_world: int, visible: int, spread: bool = True) -> list[int]:
+    """The GPU of each local rank: with more GPUs visible than ranks and ``spread``, rank r
+    takes GPU r * (visible // ranks); otherwise GPU r."""
+    stride = max(1, visible // max(1, local_world)) if spread else 1
+    return [r * stride for r in range(local_world)]
+
+
 class Dist:
     """One process per GPU (torchrun env); barrier and max-over-ranks over the process
     group (NCCL on GPUs; gloo on CPU for the host-side tests).
@@ -206,10 +213,9 @@ class Dist:
         if backend == "nccl":
             local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(self.world)))
             visible = torch.cuda.device_count()
-            stride = max(1, visible // max(1, local_world)) if spread else 1
-            self.device = torch.device("cuda", self.local * stride)
-            self.placement = {"visible_gpus": visible, "rank_to_gpu_stride": stride,
-                              "gpus": [r * stride for r in range(local_world)]}
+            gpus = rank_gpus(local_world, visible, spread)
+            self.device = torch.device("cuda", gpus[self.local])
+            self.placement = {"visible_gpus": visible, "gpus": gpus}
             torch.cuda.set_device(self.device)
         else:
             self.device = torch.device("cpu")

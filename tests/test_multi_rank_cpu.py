@@ -72,3 +72,18 @@ def test_two_gloo_ranks_shard_heads_without_exchange():
         assert owned == [1] * 8
         assert equal
         assert slowest == 2.0
+
+
+def test_bench_spreads_ranks_over_the_visible_gpus():
+    # GPUs 0-3 of the measured machines share their host link, so ranks are spread
+    import importlib
+
+    bench = importlib.import_module("bench")
+    assert bench.rank_gpus(1, 8) == [0]
+    assert bench.rank_gpus(2, 8) == [0, 4]
+    assert bench.rank_gpus(4, 8) == [0, 2, 4, 6]
+    assert bench.rank_gpus(8, 8) == list(range(8))
+    assert bench.rank_gpus(3, 8) == [0, 2, 4]       # still one rank per GPU
+    assert bench.rank_gpus(4, 4) == [0, 1, 2, 3]    # exactly N visible: no change
+    assert bench.rank_gpus(4, 8, spread=False) == [0, 1, 2, 3]
+

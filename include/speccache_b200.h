@@ -236,21 +236,26 @@ SC_API int32_t sc_restore_paged(int32_t n_requests, int32_t max_pages, int32_t p
  *    k_quant/v_quant  int8 [n_layers, n_blocks, chunk_size, n_heads, head_dim]
  *    k_scale/v_scale  fp16 [n_layers, n_blocks, chunk_size, n_heads]
  * The v_quant slab directly follows the k_quant slab in one allocation, and v_scale follows
- * k_scale.  A restore copies on the pipeline's transfer stream, per run of consecutive block
- * ids, the scales of every layer (one 2-D copy), then for each layer the K and V codes (one
- * 2-D copy of two rows) into one of n_slots device staging slots, and runs the restore kernel
- * for that layer on compute_stream once its copy event has fired, so layer l+1's copy
- * overlaps layer l's kernel.  A small restore (K and V codes of all layers within 64 MiB) is
- * instead copied with one 3-D copy per run and restored by one launch for all layers, which
- * saves the per-layer launches and events (unless SC_PIPE_PER_LAYER is set).
+ * k_scale; the scale slab is mapped pinned memory.  A restore stages the scales of every
+ * layer on the pipeline's transfer stream: one 2-D copy for a run of consecutive block ids,
+ * one gather kernel reading the mapped slab for a list in several runs.  It then cuts its
+ * block list into stages of at most 64 MiB of K and V codes over all layers (the last stage
+ * one block) and, per stage, copies the codes of every layer with one 3-D copy per run of
+ * consecutive block ids within the stage into one of n_slots device staging slots, and runs
+ * one restore kernel for the stage's blocks of every layer on compute_stream once its copy
+ * event has fired, so stage s+1's copy overlaps stage s's kernel.  Every copy command costs a
+ * few microseconds of copy-engine time beyond its bytes, so a block list in r runs costs
+ * about r + stages commands.  A restore that fits one stage is one launch.  With
+ * SC_PIPE_PER_LAYER (or where a copy pitch exceeds the device's limit) it goes layer by
+ * layer instead: per layer and run one 2-D copy of the K and V codes, one launch per layer.
  */
 typedef struct sc_pipeline sc_pipeline;
 
 #define SC_PIPE_NUMA_LOCAL 0x1u /* allocate the slabs from a thread bound to the GPU's NUMA node */
 #define SC_PIPE_WRITE_COMBINED 0x2u /* pin the slabs write-combined: faster DMA reads on some
                                        hosts, very slow host reads (write-only use) */
-#define SC_PIPE_PER_LAYER 0x4u /* always restore layer by layer (no all-layers launch for small
-                                  restores); for comparisons and tests */
+#define SC_PIPE_PER_LAYER 0x4u /* always restore layer by layer (no block stages); for
+                                  comparisons and tests */
 
 SC_API int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t n_blocks,
                            int32_t chunk_size, int32_t n_heads, int32_t head_dim,
@@ -310,9 +315,9 @@ SC_API int32_t sc_pipeline_join(sc_pipeline* p, void* stream);
 SC_API int32_t sc_pipeline_status(sc_pipeline* p, int32_t* status_bits);
 
 /* How sc_pipeline_restore would run a restore of n_blocks blocks: the kernel launches it
- * issues (1 for a restore small enough for the all-layers buffer, one per layer group for
- * larger ones, one per layer when the groups are off) into *launches.  No device work.  No
- * counterpart in the reference (it launches two kernels per chunk and layer). */
+ * issues (one per block stage: 1 for a restore that fits one stage; one per layer when the
+ * stages are off) into *launches.  No device work.  No counterpart in the reference (it
+ * launches two kernels per chunk and layer). */
 SC_API int32_t sc_pipeline_restore_launches(const sc_pipeline* p, int32_t n_blocks,
                                             int32_t* launches);
 

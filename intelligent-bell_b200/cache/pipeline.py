@@ -3,10 +3,10 @@
 Python face of ``sc_pipeline_*``: it owns pinned host slabs laid out like the
 reference's unified multi-layer slabs (speccache/serving/kv_injector.py:171-192,
 ``[L, blocks, chunk, H, D]`` int8 and ``[L, blocks, chunk, H, 1]`` fp16), and restores a
-list of blocks for every layer: per group of layers (or per layer), H2D copies (one per run
-of consecutive block ids) on its own transfer stream into a ring of device slots, joined by
-events to the restore kernel on the caller's current stream, so the next group's copy
-overlaps this group's kernel.  This replaces the Python loops of
+list of blocks for every layer: per stage of the block list (or per layer), H2D copies (one
+per run of consecutive block ids, every layer in one copy) on its own transfer stream into a
+ring of device slots, joined by events to the restore kernel on the caller's current stream,
+so the next stage's copy overlaps this stage's kernel.  This replaces the Python loops of
 ``MultiLayerKVInjector.reconstruct_and_inject_multi_layer`` (kv_injector.py:392-498)
 and ``SpecCacheEngine.execute_async_dma_and_rope`` (speccache/cache/engine.py:441-601).
 """
@@ -41,11 +41,11 @@ class KVRestorePipeline:
         numa_local: allocate the slabs from a thread bound to the GPU's NUMA node.
         write_combined: pin the slabs write-combined (host writes and GPU reads only; host
             reads of the slab views become very slow).
-        per_layer: always restore layer by layer.  By default a small restore (K and V codes
-            of all layers within 64 MiB) is copied with one 3-D copy per run of blocks and
-            restored by one launch for all layers, and a larger one goes in groups of layers
-            (up to 64 MiB of codes each, the last group one layer): one 3-D copy per run and
-            one launch per group.
+        per_layer: always restore layer by layer.  By default a restore goes in stages of
+            its block list (up to 64 MiB of K and V codes over all layers each, the last stage
+            one block): per stage one 3-D copy per run of consecutive block ids and one launch
+            for every layer, so a scattered block list costs one copy per run; a restore that
+            fits one stage is one launch.
     """
 
     def __init__(self, num_layers: int, num_blocks: int, chunk_size: int, num_kv_heads: int,
@@ -218,8 +218,8 @@ class KVRestorePipeline:
         _lib.check(self._lib.sc_pipeline_join(self._h, handle), "sc_pipeline_join")
 
     def restore_launches(self, n_blocks: int) -> int:
-        """Kernel launches a restore of ``n_blocks`` blocks issues: 1 when it fits the
-        all-layers buffer, one per layer group above that, one per layer with ``per_layer``."""
+        """Kernel launches a restore of ``n_blocks`` blocks issues: one per block stage (1
+        when it fits one stage), one per layer with ``per_layer``."""
         count = ctypes.c_int32(0)
         _lib.check(self._lib.sc_pipeline_restore_launches(self._h, int(n_blocks), ctypes.byref(count)),
                    "sc_pipeline_restore_launches")

@@ -50,16 +50,23 @@ struct PagedArgs {
     const int32_t* page_table;
     int64_t page_table_stride;
     const int32_t* seq_lens;
+    int32_t seq_len_shared;  // 1: seq_lens[0] is every request's length
     const float* delta_p;
+    // 0: delta_p[r]; 1: delta_p[r * max_pages + page]; 2: delta_p[page] (shared by requests)
     int32_t delta_p_per_page;
+    // Rows added to request r's scale index per request (r * scale_request_skew): lets the
+    // requests' codes be packed in a staging pool while their scales keep a wider layout.
+    int64_t scale_request_skew;
     double theta_base;
     const float* inv_freq;  // host, may be null
     void* k_out;
     void* v_out;
     // Per-request output buffers (device arrays of n_requests addresses, 32-byte aligned); when
-    // given, request r writes from offset 0 of its own buffers and out_offsets is not read.
+    // given, request r writes from element out_ptr_offset of its own buffers and out_offsets is
+    // not read.
     const uint64_t* k_out_ptrs;
     const uint64_t* v_out_ptrs;
+    int64_t out_ptr_offset;
     const int64_t* out_offsets;
     int64_t out_strides[3];
     int64_t out_numel;
@@ -70,6 +77,14 @@ struct PagedArgs {
 };
 
 int32_t launch_paged(const PagedArgs& a);
+
+// Gather rows x n pieces of piece_bytes (a multiple of 16) from a device-accessible source
+// laid out [rows][src_blocks] pieces into dst [rows][n]: piece (t, i) is piece ids[i] of
+// source row t.  An id outside [0, src_blocks) skips its piece and ORs SC_STATUS_BAD_PAGE_ID
+// into *status.
+int32_t launch_gather_pieces(const void* src, int64_t src_blocks, void* dst, const int32_t* ids,
+                             int32_t n, int32_t rows, int64_t piece_bytes, int32_t* status,
+                             cudaStream_t stream);
 
 // Load the kernels the pipeline launches (paged restore; quantize with fp16 scales) on the
 // current device now.  CUDA loads a kernel's module lazily at its first launch, and that

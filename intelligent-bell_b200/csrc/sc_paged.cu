@@ -105,12 +105,15 @@ struct PagedParams {
     const int32_t* table;
     int64_t table_stride;
     const int32_t* seq_lens;
+    int32_t seq_r;          // request stride of seq_lens (0: one length for every request)
     const float* dp;
-    int32_t dp_per_page;
+    int64_t dp_r, dp_pg;    // shift of (request r, page pg): dp[r * dp_r + pg * dp_pg]
+    int64_t sc_skew;        // scale rows added per request (packed codes, wider scale layout)
     void* ko;
     void* vo;
     const uint64_t* ko_ptrs;  // per-request output buffers (device), or null: ko/vo + out_off
     const uint64_t* vo_ptrs;
+    int64_t ptr_off;          // with ko_ptrs / vo_ptrs: first element written of each buffer
     const int64_t* out_off;
     int64_t o_t, o_h;
     int64_t out_numel;
@@ -150,7 +153,7 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
     const int pg = static_cast<int>(task - static_cast<int64_t>(r) * p.max_pages);
     const bool reporter = chunk == 0 && tid == 0;
     // The length alone first: a block past its request's length exits after one load.
-    const int len = ld_meta(p.seq_lens + r);
+    const int len = ld_meta(p.seq_lens + r * p.seq_r);
     if (len < 0 || static_cast<int64_t>(len) > static_cast<int64_t>(p.max_pages) * p.page) {
         if (reporter && pg == 0) atomicOr(p.status, SC_STATUS_BAD_SEQ_LEN);
         return;
@@ -170,10 +173,11 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
     if constexpr (kPtrs) {
         if (has_k) ko_r = reinterpret_cast<void*>(ld_meta(reinterpret_cast<const int64_t*>(p.ko_ptrs) + r));
         if (has_v) vo_r = reinterpret_cast<void*>(ld_meta(reinterpret_cast<const int64_t*>(p.vo_ptrs) + r));
+        off = p.ptr_off;
     } else {
         off = ld_meta(p.out_off + r);
     }
-    const float dp = has_k ? ld_meta(p.dp + (p.dp_per_page ? task : r)) : 0.0f;
+    const float dp = has_k ? ld_meta(p.dp + r * p.dp_r + pg * p.dp_pg) : 0.0f;
     if (page_id < 0 || page_id >= p.n_pool_pages) {
         if (reporter) atomicOr(p.status, SC_STATUS_BAD_PAGE_ID);
         return;
@@ -195,21 +199,23 @@ __global__ void __launch_bounds__(kPThreads, SC_PAGED_MIN_BLOCKS)
     // Every round's rows in flight at once: codes into this thread's slots, scales into
     // registers.
     const int64_t prow0 = static_cast<int64_t>(page_id) * p.page * p.H + row_begin + rl;
+    const int64_t srow0 = prow0 + r * p.sc_skew;
     __half ksc[kRounds], vsc[kRounds];
 #pragma unroll
     for (int round = 0; round < kRounds; ++round) {
         if (row_begin + static_cast<int64_t>(round) * RB + rl < rows) {
             const int64_t prow = prow0 + static_cast<int64_t>(round) * RB;
+            const int64_t srow = srow0 + static_cast<int64_t>(round) * RB;
             const int64_t src = prow * p.D + j * 16;
             if (has_k) {
                 cp_async16(&s_codes[round][0][tid], p.kq + src);
                 cp_async16(&s_codes[round][1][tid], p.kq + src + half);
-                ksc[round] = p.ks[prow];
+                ksc[round] = p.ks[srow];
             }
             if (has_v) {
                 cp_async16(&s_codes[round][2][tid], p.vq + src);
                 cp_async16(&s_codes[round][3][tid], p.vq + src + half);
-                vsc[round] = p.vs[prow];
+                vsc[round] = p.vs[srow];
             }
         }
     }
@@ -250,11 +256,44 @@ cudaError_t launch(const PagedParams& p, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
+// Scattered pieces from a device-accessible source (the pipeline's mapped pinned scale slab)
+// into a packed staging buffer: piece (t, i) of the output, n pieces per row, is piece
+// ids[i] of source row t (src_blocks pieces per row).  One warp per piece, four 16-byte loads
+// in flight per lane.  Reading pinned host memory from the SMs moves many small pieces at
+// PCIe rate (measured on B200: 8192 scattered 1 KiB pieces in 0.17 ms, 49 GB/s), where one
+// copy-engine command per piece costs about 4 us each.
+__global__ void __launch_bounds__(256)
+    gather_pieces(const uint4* __restrict__ src, int64_t src_blocks, uint4* __restrict__ dst,
+                  const int32_t* __restrict__ ids, int32_t n, int64_t n_pieces, int32_t piece16,
+                  int32_t* status) {
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= n_pieces) return;
+    const int64_t t = warp / n;
+    const int32_t b = ids[warp - t * n];
+    if (b < 0 || b >= src_blocks) {
+        if (lane == 0) atomicOr(status, SC_STATUS_BAD_PAGE_ID);
+        return;
+    }
+    const uint4* s = src + (t * src_blocks + b) * piece16;
+    uint4* d = dst + warp * piece16;
+    for (int o = lane; o < piece16; o += 128) {
+        uint4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (o + 32 * k < piece16) v[k] = s[o + 32 * k];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (o + 32 * k < piece16) d[o + 32 * k] = v[k];
+    }
+}
+
 }  // namespace
 
 cudaError_t preload_paged_kernels() {
     cudaFuncAttributes attr;
-    cudaError_t e = cudaFuncGetAttributes(&attr, paged_restore<__half, true, false>);
+    cudaError_t e = cudaFuncGetAttributes(&attr, gather_pieces);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__half, true, false>);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__half, false, false>);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__nv_bfloat16, true, false>);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, paged_restore<__nv_bfloat16, false, false>);
@@ -286,6 +325,8 @@ int32_t launch_paged(const PagedArgs& a) {
     if (!a.page_table || !a.seq_lens || (!ptrs && !a.out_offsets) || !a.status ||
         (has_k && !a.delta_p))
         return set_error(SC_ERR_INVALID_ARGUMENT, "null page table / lengths / offsets / status");
+    if (a.delta_p_per_page < 0 || a.delta_p_per_page > 2)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "delta_p_per_page %d", a.delta_p_per_page);
     if (a.page_table_stride < a.max_pages)
         return set_error(SC_ERR_INVALID_ARGUMENT, "page_table_stride %lld < max_pages %d",
                          (long long)a.page_table_stride, a.max_pages);
@@ -323,12 +364,16 @@ int32_t launch_paged(const PagedArgs& a) {
     p.table = a.page_table;
     p.table_stride = a.page_table_stride;
     p.seq_lens = a.seq_lens;
+    p.seq_r = a.seq_len_shared ? 0 : 1;
     p.dp = a.delta_p;
-    p.dp_per_page = a.delta_p_per_page;
+    p.dp_r = a.delta_p_per_page == 0 ? 1 : a.delta_p_per_page == 1 ? a.max_pages : 0;
+    p.dp_pg = a.delta_p_per_page == 0 ? 0 : 1;
+    p.sc_skew = a.scale_request_skew;
     p.ko = a.k_out;
     p.vo = a.v_out;
     p.ko_ptrs = a.k_out_ptrs;
     p.vo_ptrs = a.v_out_ptrs;
+    p.ptr_off = a.out_ptr_offset;
     p.out_off = a.out_offsets;
     p.o_t = a.out_strides[0];
     p.o_h = a.out_strides[1];
@@ -349,6 +394,25 @@ int32_t launch_paged(const PagedArgs& a) {
     return ok();
 }
 
+int32_t launch_gather_pieces(const void* src, int64_t src_blocks, void* dst, const int32_t* ids,
+                             int32_t n, int32_t rows, int64_t piece_bytes, int32_t* status,
+                             cudaStream_t stream) {
+    if (!src || !dst || !ids || !status || n < 0 || rows < 0 || src_blocks <= 0 ||
+        piece_bytes <= 0 || piece_bytes % 16 != 0 || piece_bytes / 16 > (int64_t(1) << 30) ||
+        (reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) % 16 != 0)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "invalid piece gather");
+    const int64_t n_pieces = static_cast<int64_t>(rows) * n;
+    if (n_pieces == 0) return ok();
+    const int64_t blocks = (n_pieces * 32 + 255) / 256;
+    if (blocks >= (int64_t(1) << 31)) return set_error(SC_ERR_INVALID_ARGUMENT, "too many pieces");
+    gather_pieces<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        static_cast<const uint4*>(src), src_blocks, static_cast<uint4*>(dst), ids, n, n_pieces,
+        static_cast<int32_t>(piece_bytes / 16), status);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "piece gather launch");
+    return ok();
+}
+
 }  // namespace sc
 
 extern "C" int32_t sc_restore_paged(int32_t n_requests, int32_t max_pages, int32_t page_size,
@@ -363,6 +427,9 @@ extern "C" int32_t sc_restore_paged(int32_t n_requests, int32_t max_pages, int32
                                     int64_t out_numel, int32_t out_dtype, int32_t* status,
                                     uint32_t flags, void* stream) {
     if (!out_strides) return sc::set_error(SC_ERR_INVALID_ARGUMENT, "null out_strides");
+    if (delta_p_per_page != 0 && delta_p_per_page != 1)
+        return sc::set_error(SC_ERR_INVALID_ARGUMENT, "delta_p_per_page must be 0 or 1, got %d",
+                             delta_p_per_page);
     sc::PagedArgs a{};
     a.n_requests = n_requests;
     a.max_pages = max_pages;

@@ -5,21 +5,29 @@
 //   * pinned slabs [L, B, chunk, H, D] int8 and [L, B, chunk, H] fp16 (cudaHostAlloc,
 //     optionally from a thread bound to the GPU's NUMA node);
 //   * K and V code slabs are one pinned allocation (V right after K), and so are the scale
-//     slabs; a restore first copies every layer's scales of each run of consecutive block
-//     ids with one 2-D copy (2 x n_layers rows), then, per layer, K and V codes of each run
-//     with one 2-D copy of two rows, on the pipeline's own transfer stream into a ring of
-//     device staging slots (a copy costs about 4 us of engine time beyond its bytes, so 33
-//     copies instead of 128 for a 32-layer restore);
-//   * an event per slot joins the transfer stream to the caller's compute stream, where
-//     the paged restore kernel (identity page table, one shift per block) writes the
-//     layer's K and V; a second event per slot releases the slot for layer l + n_slots;
-//   * layer groups (the default where the copy pitches allow): the K and V codes of up to
-//     group_cap layers (64 MiB) go with one 3-D copy per run into a slot, and one kernel
-//     launch restores the group, its layers being the requests of the paged kernel; the last
-//     group is one layer, so that one layer's kernel remains after the last copy.  A 32-layer
-//     restore then takes 9 copies and launches instead of 32 (a copy costs a few
-//     microseconds of engine time beyond its bytes).  A restore small enough for one
-//     64 MiB buffer is one group of every layer (the all-layers mode).
+//     slabs (mapped, so kernels can read them); a restore first stages every layer's scales
+//     of its blocks on the pipeline's own transfer stream: one 2-D copy (2 x n_layers rows)
+//     for a list of consecutive block ids, one gather kernel reading the mapped slab for a
+//     list in several runs;
+//   * every copy command costs about 4 us of copy-engine time beyond its bytes, whatever
+//     its size or shape (the rows of a 2-D or 3-D copy cost nothing extra), and spreading
+//     commands over several streams does not overlap that cost (measured on B200: 8192
+//     copies of 64 KiB take 43 ms against 9.7 ms for the same bytes in one 2-D copy).  So the
+//     codes move in as few commands as the block list allows;
+//   * block stages (the default where the copy pitches allow): the restore's block list is
+//     cut into stages of at most 64 MiB of K and V codes over all layers; a stage's codes go
+//     with one 3-D copy per run of consecutive block ids (rows: every layer at the slab's
+//     layer pitch; slices: K then V) into one of a ring of device slots, and one paged-kernel
+//     launch restores the stage, the layers being its requests.  A restore of n blocks in r
+//     runs costs about r + stages copy commands, so a scattered block list costs one copy
+//     per run rather than one per run and layer.  The last stage is one block, so that only
+//     its kernel remains after the last copy; a restore that fits one stage is one copy per
+//     run and one launch;
+//   * an event per slot joins the transfer stream to the caller's compute stream; a second
+//     event per slot releases the slot for stage s + n_slots;
+//   * layer by layer (SC_PIPE_PER_LAYER, or where a pitch exceeds the device's limit): per
+//     layer, K and V codes of each run with one 2-D copy of two rows into a slot, one
+//     paged-kernel launch per layer.
 // The offload runs the other way: the quantize kernel writes a device staging buffer on
 // the compute stream, an event hands it to the transfer stream, D2H copies fill the slabs.
 // Nothing on the host waits during a restore or an offload while fewer than four earlier
@@ -47,13 +55,32 @@ struct Meta {  // one upload per restore: identity-table length and per-block sh
     float delta_p[1];  // [max_restore_blocks]
 };
 
-// Staging for the all-layers mode: a restore whose K and V codes over all layers fit here is
-// copied with one 3-D copy per run of blocks and restored by one kernel launch (per-layer
-// launches and events cost about 8 us of host time per layer, more than the copies of a
-// restore of a few blocks take).
-constexpr size_t kAllLayerBytes = size_t(64) << 20;
-// Largest K + V codes of one layer group in a slot.
-constexpr size_t kGroupBytes = size_t(64) << 20;
+// K and V codes of one block stage (all layers) in a slot.  A restore that fits one stage is
+// one copy per run and one kernel launch (per-layer launches and events cost about 8 us of
+// host time per layer, more than the copies of a restore of a few blocks take).
+constexpr size_t kStageBytes = size_t(64) << 20;
+// Block stages are off where one block's codes over all layers exceed this (a slot holds at
+// least one block).
+constexpr size_t kMaxStageBytes = size_t(256) << 20;
+
+// Blocks per stage of an n-block restore with at most `cap` blocks per stage: one stage if
+// n <= cap; otherwise the last stage is one block (its kernel is the only one left after the
+// last copy; every other stage's kernel runs while the next stage's copy, tens of times
+// longer, is in flight) and the n - 1 blocks before it go in as few stages of at most cap
+// blocks as possible, of nearly equal size.
+void stage_sizes(int64_t n, int64_t cap, std::vector<int32_t>& out) {
+    out.clear();
+    if (n <= 0) return;
+    if (n <= cap) {
+        out.push_back(static_cast<int32_t>(n));
+        return;
+    }
+    const int64_t front = n - 1;
+    const int64_t n_front = (front + cap - 1) / cap;
+    for (int64_t i = 0; i < n_front; ++i)
+        out.push_back(static_cast<int32_t>(front / n_front + (i < front % n_front ? 1 : 0)));
+    out.push_back(1);
+}
 
 size_t meta_bytes(int64_t max_blocks) {
     return sizeof(Meta) + sizeof(float) * static_cast<size_t>(max_blocks > 1 ? max_blocks - 1 : 0);
@@ -137,7 +164,9 @@ struct sc_pipeline {
     uint16_t* h_vs = nullptr;
     uint8_t* h_meta = nullptr;  // kMetaRing buffers of meta_stride bytes
     size_t meta_stride = 0;
-    std::vector<int8_t*> d_kq, d_vq;  // per slot; d_vq[s] = d_kq[s] + stage codes (one allocation)
+    // per slot: block stages use d_kq[s] alone ([2][L][m][block]); layer by layer, d_vq[s] =
+    // d_kq[s] + stage codes in the same allocation
+    std::vector<int8_t*> d_kq, d_vq;
     uint16_t* d_sc = nullptr;         // scales of every layer: [2][L][max_blocks * chunk * H]
     bool codes_2d = false, scales_2d = false;  // pitches within the device's copy limit
     int32_t* d_table = nullptr;
@@ -150,22 +179,23 @@ struct sc_pipeline {
     bool meta_used[kMetaRing] = {};
     int meta_next = 0;
     bool any_restore = false;
-    // all-layers mode (small restores): K and V codes of every layer in one staging buffer
-    // [2][L][n][block], one 3-D copy per run, one kernel launch with one request per layer
-    int8_t* d_all = nullptr;
-    int64_t all_cap_pages = 0;  // capacity in (layer, block) pages; 0 = mode unavailable
-    bool codes_3d = false;
-    // layer-group mode: slots of group_cap layers (0 = mode unavailable), group sizes in order
-    int32_t group_cap = 0;
-    std::vector<int32_t> group_sizes;
-    // kMetaRing host buffers, each seq[L] | dps[meta_pages] | k_out[L] | v_out[L] (both the
-    // all-layers and the layer-group modes; meta_pages = L x the most blocks they take)
-    uint8_t* h_all_meta = nullptr;
-    uint8_t* d_all_meta = nullptr;
-    size_t all_meta_bytes = 0, all_meta_stride = 0, off_dps = 0, off_kp = 0, off_vp = 0;
-    cudaEvent_t all_meta_uploaded[kMetaRing] = {};
-    bool all_meta_used[kMetaRing] = {};
-    int all_meta_next = 0;
+    // block stages: at most stage_cap blocks per stage (0 = mode unavailable); stage_3d: K and
+    // V codes of a run in one 3-D copy (else one 2-D copy each)
+    int64_t stage_cap = 0;
+    bool stage_3d = false;
+    std::vector<int32_t> stages;  // the current restore's stage sizes
+    // The scale slab as the device addresses it (mapped pinned memory), for the scale gather
+    // kernel of restores in more than one run; null where the slab is not mapped.
+    const uint16_t* d_hks = nullptr;
+    // kMetaRing host buffers, each seq[max stages] | dps[max_blocks] | ids[max_blocks] |
+    // k_out[L] | v_out[L]
+    uint8_t* h_stage_meta = nullptr;
+    uint8_t* d_stage_meta = nullptr;
+    size_t stage_meta_bytes = 0, stage_meta_stride = 0, off_dps = 0, off_ids = 0, off_kp = 0,
+           off_vp = 0;
+    cudaEvent_t stage_meta_uploaded[kMetaRing] = {};
+    bool stage_meta_used[kMetaRing] = {};
+    int stage_meta_next = 0;
     // offload: quantize into one of two device staging slots (K then V codes in one
     // allocation, K then V scales in another), then D2H into the slabs
     int8_t* o_codes[2] = {nullptr, nullptr};
@@ -189,11 +219,10 @@ void release(sc_pipeline* p) {
     if (p->any_offload && p->o_free[p->o_last]) cudaEventSynchronize(p->o_free[p->o_last]);
     for (int i = 0; i < kMetaRing; ++i) {
         if (p->meta_uploaded[i]) cudaEventDestroy(p->meta_uploaded[i]);
-        if (p->all_meta_uploaded[i]) cudaEventDestroy(p->all_meta_uploaded[i]);
+        if (p->stage_meta_uploaded[i]) cudaEventDestroy(p->stage_meta_uploaded[i]);
     }
-    cudaFree(p->d_all);
-    cudaFree(p->d_all_meta);
-    cudaFreeHost(p->h_all_meta);
+    cudaFree(p->d_stage_meta);
+    cudaFreeHost(p->h_stage_meta);
     if (p->done) cudaEventDestroy(p->done);
     for (int s = 0; s < 2; ++s) {
         if (p->o_ready[s]) cudaEventDestroy(p->o_ready[s]);
@@ -202,7 +231,7 @@ void release(sc_pipeline* p) {
         cudaFree(p->o_scales[s]);
     }
     if (p->transfer) cudaStreamDestroy(p->transfer);
-    for (auto x : p->d_kq) cudaFree(x);  // d_vq[s] lies in the same allocation
+    for (auto x : p->d_kq) cudaFree(x);  // d_vq[s], where set, lies in the same allocation
     cudaFree(p->d_sc);
     cudaFree(p->d_table);
     cudaFree(p->d_meta);
@@ -278,7 +307,8 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
     };
     halloc(2 * slab_codes, &ptr, slab_flags), p->h_kq = static_cast<int8_t*>(ptr);
     if (e == cudaSuccess) p->h_vq = p->h_kq + slab_codes;
-    halloc(2 * slab_scales * 2, &ptr, slab_flags), p->h_ks = static_cast<uint16_t*>(ptr);
+    halloc(2 * slab_scales * 2, &ptr, slab_flags | cudaHostAllocMapped),
+        p->h_ks = static_cast<uint16_t*>(ptr);
     if (e == cudaSuccess) p->h_vs = p->h_ks + slab_scales;
     p->meta_stride = round_up64(meta_bytes(max_restore_blocks));
     halloc(kMetaRing * p->meta_stride, &ptr, cudaHostAllocPortable), p->h_meta = static_cast<uint8_t*>(ptr);
@@ -295,32 +325,32 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
     int max_pitch = 0;
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&max_pitch, cudaDevAttrMaxPitch, device);
     const size_t mp = static_cast<size_t>(max_pitch);
+    const size_t blk_codes = row * head_dim;
     {
-        // Layer groups need the 3-D copy's pitches (the slab's layer pitch, the staging row) and
-        // the scales' 2-D copy within the device's limit.
-        const size_t blk_codes = row * head_dim;
-        const bool pitches = static_cast<size_t>(n_blocks) * blk_codes <= mp && stage_codes <= mp &&
-                             static_cast<size_t>(n_blocks) * row * 2 <= mp;
-        int64_t cap = static_cast<int64_t>(kGroupBytes / (2 * stage_codes));
-        if (cap > n_layers) cap = n_layers;
-        if (!(flags & SC_PIPE_PER_LAYER) && pitches && cap >= 2) {
-            p->group_cap = static_cast<int32_t>(cap);
-            // The last group is one layer: its kernel is the only one left after the last copy
-            // (every other group's kernels run while the next group's copy, about 40x longer,
-            // is in flight).  The layers before it go in as few groups of at most group_cap as
-            // possible, of nearly equal size.
-            const int32_t front = n_layers - 1;
-            const int32_t n_front = (front + p->group_cap - 1) / p->group_cap;
-            for (int32_t i = 0; i < n_front; ++i)
-                p->group_sizes.push_back(front / n_front + (i < front % n_front ? 1 : 0));
-            p->group_sizes.push_back(1);
-        }
+        // Block stages need the copies' pitches within the device's limit: the slab's layer
+        // pitch and the slot's row (one layer of a stage) for the codes, the slabs' and the
+        // staging's rows for the scales.
+        const size_t per_block = 2 * static_cast<size_t>(n_layers) * blk_codes;
+        int64_t cap = static_cast<int64_t>(kStageBytes / per_block);
+        if (cap < 1) cap = 1;
+        if (cap > max_restore_blocks) cap = max_restore_blocks;
+        const bool pitches = static_cast<size_t>(n_blocks) * blk_codes <= mp &&
+                             static_cast<size_t>(cap) * blk_codes <= mp &&
+                             static_cast<size_t>(n_blocks) * row * 2 <= mp && stage_scales * 2 <= mp;
+        if (!(flags & SC_PIPE_PER_LAYER) && pitches && per_block <= kMaxStageBytes)
+            p->stage_cap = cap;
+        // One 3-D copy per run moves K and V (slices at the K -> V slab distance) where that
+        // distance is within the limit too; otherwise one 2-D copy each.
+        p->stage_3d = slab_codes <= mp;
     }
-    const size_t slot_layers = p->group_cap > 1 ? static_cast<size_t>(p->group_cap) : 1;
+    const size_t slot_bytes = p->stage_cap > 0
+                                  ? static_cast<size_t>(p->stage_cap) * 2 * n_layers * blk_codes
+                                  : 2 * stage_codes;
     for (int s = 0; s < n_slots && e == cudaSuccess; ++s) {
         int8_t* kv = nullptr;
-        e = cudaMalloc(&kv, 2 * slot_layers * stage_codes);
-        p->d_kq.push_back(kv), p->d_vq.push_back(kv ? kv + stage_codes : nullptr);
+        e = cudaMalloc(&kv, slot_bytes);
+        p->d_kq.push_back(kv);
+        p->d_vq.push_back(kv && p->stage_cap == 0 ? kv + stage_codes : nullptr);
     }
     if (e == cudaSuccess)
         e = cudaMalloc(&p->d_sc, 2 * static_cast<size_t>(n_layers) * stage_scales * 2);
@@ -328,39 +358,37 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
         p->codes_2d = slab_codes <= mp && stage_codes <= mp;
         p->scales_2d = static_cast<size_t>(n_blocks) * row * 2 <= mp && stage_scales * 2 <= mp;
         p->offload_scales_2d = slab_scales * 2 <= mp && stage_scales * 2 <= mp;
-        // all-layers mode: up to kAllLayerBytes of K and V codes staged for one launch
-        const size_t blk_codes = row * head_dim;
-        int64_t cap = static_cast<int64_t>(kAllLayerBytes / (2 * blk_codes));
-        if (cap > static_cast<int64_t>(n_layers) * max_restore_blocks)
-            cap = static_cast<int64_t>(n_layers) * max_restore_blocks;
-        const int64_t max_n = cap / n_layers;  // blocks per restore the mode can take
-        p->codes_3d = static_cast<size_t>(n_blocks) * blk_codes <= mp &&
-                      static_cast<size_t>(max_n) * blk_codes <= mp;
-        if (!(flags & SC_PIPE_PER_LAYER) && max_n >= 1 && p->codes_3d &&
-            static_cast<size_t>(n_blocks) * row * 2 <= mp) {
-            p->all_cap_pages = max_n * n_layers;
-            e = cudaMalloc(&p->d_all, 2 * static_cast<size_t>(p->all_cap_pages) * blk_codes);
-        }
-        if (e == cudaSuccess && (p->all_cap_pages > 0 || p->group_cap > 1)) {
-            const int64_t meta_pages = p->group_cap > 1 ? n_layers * max_restore_blocks
-                                                        : p->all_cap_pages;
-            p->off_dps = (static_cast<size_t>(n_layers) * 4 + 7) / 8 * 8;
-            p->off_kp = p->off_dps + (static_cast<size_t>(meta_pages) * 4 + 7) / 8 * 8;
-            p->off_vp = p->off_kp + static_cast<size_t>(n_layers) * 8;
-            p->all_meta_bytes = p->off_vp + static_cast<size_t>(n_layers) * 8;
-            p->all_meta_stride = round_up64(p->all_meta_bytes);
-            e = cudaMalloc(&p->d_all_meta, p->all_meta_bytes);
-            if (e == cudaSuccess)
-                e = cudaHostAlloc(&p->h_all_meta, kMetaRing * p->all_meta_stride,
-                                  cudaHostAllocPortable);
-            for (int i = 0; i < kMetaRing && e == cudaSuccess; ++i)
-                e = cudaEventCreateWithFlags(&p->all_meta_uploaded[i], cudaEventDisableTiming);
+    }
+    if (e == cudaSuccess && p->stage_cap > 0) {
+        // The stage count grows with the block count, so the largest restore has the most.
+        stage_sizes(max_restore_blocks, p->stage_cap, p->stages);
+        const size_t max_stages = p->stages.size();
+        p->off_dps = (max_stages * 4 + 7) / 8 * 8;
+        p->off_ids = p->off_dps + (static_cast<size_t>(max_restore_blocks) * 4 + 7) / 8 * 8;
+        p->off_kp = p->off_ids + (static_cast<size_t>(max_restore_blocks) * 4 + 7) / 8 * 8;
+        p->off_vp = p->off_kp + static_cast<size_t>(n_layers) * 8;
+        p->stage_meta_bytes = p->off_vp + static_cast<size_t>(n_layers) * 8;
+        p->stage_meta_stride = round_up64(p->stage_meta_bytes);
+        e = cudaMalloc(&p->d_stage_meta, p->stage_meta_bytes);
+        if (e == cudaSuccess)
+            e = cudaHostAlloc(&p->h_stage_meta, kMetaRing * p->stage_meta_stride,
+                              cudaHostAllocPortable);
+        for (int i = 0; i < kMetaRing && e == cudaSuccess; ++i)
+            e = cudaEventCreateWithFlags(&p->stage_meta_uploaded[i], cudaEventDisableTiming);
+        // The scale gather reads the slab in 16-byte units: one block's scales of one layer
+        // (chunk x heads fp16) must be a multiple of 16 bytes.
+        void* mapped = nullptr;
+        if (e == cudaSuccess && (row * 2) % 16 == 0) {
+            if (cudaHostGetDevicePointer(&mapped, p->h_ks, 0) == cudaSuccess)
+                p->d_hks = static_cast<const uint16_t*>(mapped);
+            else
+                cudaGetLastError();  // not mapped: the scales go by copies
         }
     }
-    int64_t table_len = p->all_cap_pages > max_restore_blocks ? p->all_cap_pages
-                                                               : max_restore_blocks;
-    if (p->group_cap > 1 && static_cast<int64_t>(p->group_cap) * max_restore_blocks > table_len)
-        table_len = static_cast<int64_t>(p->group_cap) * max_restore_blocks;
+    // Identity page table: a stage's pool holds n_layers x (at most stage_cap) pages.
+    int64_t table_len = max_restore_blocks;
+    if (static_cast<int64_t>(n_layers) * p->stage_cap > table_len)
+        table_len = static_cast<int64_t>(n_layers) * p->stage_cap;
     if (e == cudaSuccess) e = cudaMalloc(&p->d_table, sizeof(int32_t) * table_len);
     if (e == cudaSuccess) e = cudaMalloc(&p->d_meta, meta_bytes(max_restore_blocks));
     if (e == cudaSuccess) e = cudaMalloc(&p->d_status, sizeof(int32_t));
@@ -410,109 +438,140 @@ extern "C" int32_t sc_pipeline_host_slabs(const sc_pipeline* p, int8_t** k_quant
 
 namespace {
 
-// Layer groups: the layers of a group are the requests of one paged restore (request g
-// writes layer l0 + g).  Their K and V codes are staged [2][G][n][block] by one 3-D copy per
-// run of consecutive blocks (rows: layers at the slab's layer pitch; slices: K then V), every
-// layer's scales [2][L][n][chunk * H] by one 2-D copy per run up front.
-//   all_layers: one group of every layer in d_all (restores of at most kAllLayerBytes);
-//   otherwise:  p->group_sizes groups in the slot buffers, the transfer stream filling slot s
-//               while the compute stream restores the groups in the other slots.
-int32_t restore_layer_groups(sc_pipeline* p, bool all_layers, const int32_t* block_ids,
-                             const int32_t* delta_ps, int32_t n, double theta_base,
-                             const float* inv_freq, void* const* k_out, void* const* v_out,
-                             const int64_t* out_strides, int64_t out_numel, int32_t out_dtype,
-                             cudaStream_t cs) {
+// Block stages: stage s holds the blocks at positions [i0, i0 + m) of the restore for every
+// layer; the layers are the requests of one paged restore (request l writes layer l from
+// token i0 * chunk).  The stage's K and V codes are staged [2][L][m][block] in a slot by one
+// 3-D copy per run of consecutive block ids within the stage (rows: layers at the slab's
+// layer pitch; slices: K then V), every layer's scales [2][L][n][chunk * H] up front (one
+// 2-D copy for a single run, else one gather kernel over the mapped slab); the kernel reaches
+// a stage's scales through a per-request skew of (n - m) pages.  The transfer stream fills slot s % n_slots while the compute stream
+// restores the stages in the other slots.
+int32_t restore_block_stages(sc_pipeline* p, const int32_t* block_ids, const int32_t* delta_ps,
+                             int32_t n, double theta_base, const float* inv_freq,
+                             void* const* k_out, void* const* v_out, const int64_t* out_strides,
+                             int64_t out_numel, int32_t out_dtype, cudaStream_t cs) {
     const int L = p->L;
     for (int l = 0; l < L; ++l)
         if (((reinterpret_cast<uintptr_t>(k_out[l]) | reinterpret_cast<uintptr_t>(v_out[l])) & 31) != 0)
             return set_error(SC_ERR_INVALID_ARGUMENT, "outputs must be 32-byte aligned (layer %d)", l);
     const size_t row = static_cast<size_t>(p->chunk) * p->H;
     const size_t blk_codes = row * p->D, blk_scales = row;
+    stage_sizes(n, p->stage_cap, p->stages);
+    const size_t n_stages = p->stages.size();
     cudaError_t e = cudaSuccess;
     // The next host metadata buffer may still feed an upload kMetaRing restores back.
-    const int ms = p->all_meta_next;
-    if (p->all_meta_used[ms]) e = cudaEventSynchronize(p->all_meta_uploaded[ms]);
+    const int ms = p->stage_meta_next;
+    if (p->stage_meta_used[ms]) e = cudaEventSynchronize(p->stage_meta_uploaded[ms]);
     if (e != cudaSuccess) return cuda_error(e, "waiting for an earlier metadata upload");
-    uint8_t* hm = p->h_all_meta + static_cast<size_t>(ms) * p->all_meta_stride;
+    uint8_t* hm = p->h_stage_meta + static_cast<size_t>(ms) * p->stage_meta_stride;
     int32_t* seq = reinterpret_cast<int32_t*>(hm);
     float* dps = reinterpret_cast<float*>(hm + p->off_dps);
+    int32_t* ids = reinterpret_cast<int32_t*>(hm + p->off_ids);
     uint64_t* kp = reinterpret_cast<uint64_t*>(hm + p->off_kp);
     uint64_t* vp = reinterpret_cast<uint64_t*>(hm + p->off_vp);
+    for (size_t s = 0; s < n_stages; ++s) seq[s] = p->stages[s] * p->chunk;
+    int32_t runs = n > 0 ? 1 : 0;
+    for (int32_t i = 0; i < n; ++i) {
+        dps[i] = static_cast<float>(delta_ps[i]);
+        ids[i] = block_ids[i];
+        if (i > 0 && block_ids[i] != block_ids[i - 1] + 1) ++runs;
+    }
     for (int l = 0; l < L; ++l) {
-        seq[l] = n * p->chunk;
         kp[l] = reinterpret_cast<uint64_t>(k_out[l]);
         vp[l] = reinterpret_cast<uint64_t>(v_out[l]);
-        for (int32_t i = 0; i < n; ++i) dps[static_cast<size_t>(l) * n + i] = static_cast<float>(delta_ps[i]);
     }
-    // The staging, the scales and the metadata on the device may still be read by the
-    // previous restore's kernels.
+    // The slots, the scales and the metadata on the device may still be read by the previous
+    // restore's kernels.
     if (p->any_restore) e = cudaStreamWaitEvent(p->transfer, p->done, 0);
     if (e == cudaSuccess)
-        e = cudaMemcpyAsync(p->d_all_meta, hm, p->all_meta_bytes, cudaMemcpyHostToDevice,
+        e = cudaMemcpyAsync(p->d_stage_meta, hm, p->stage_meta_bytes, cudaMemcpyHostToDevice,
                             p->transfer);
-    if (e == cudaSuccess) e = cudaEventRecord(p->all_meta_uploaded[ms], p->transfer);
+    if (e == cudaSuccess) e = cudaEventRecord(p->stage_meta_uploaded[ms], p->transfer);
     if (e != cudaSuccess) return cuda_error(e, "metadata upload");
-    p->all_meta_used[ms] = true;
-    p->all_meta_next = (ms + 1) % kMetaRing;
-    // Runs of consecutive block ids: fn(first block, position in the restore, length).
-    auto for_runs = [&](auto&& fn) {
-        for (int32_t i = 0; i < n && e == cudaSuccess;) {
+    p->stage_meta_used[ms] = true;
+    p->stage_meta_next = (ms + 1) % kMetaRing;
+    // Runs of consecutive block ids among positions [lo, hi): fn(first block, position, length).
+    auto for_runs = [&](int32_t lo, int32_t hi, auto&& fn) {
+        for (int32_t i = lo; i < hi && e == cudaSuccess;) {
             int32_t rn = 1;
-            while (i + rn < n && block_ids[i + rn] == block_ids[i] + rn) ++rn;
+            while (i + rn < hi && block_ids[i + rn] == block_ids[i] + rn) ++rn;
             fn(static_cast<size_t>(block_ids[i]), static_cast<size_t>(i), static_cast<size_t>(rn));
             i += rn;
         }
     };
-    for_runs([&](size_t b0, size_t i, size_t rn) {
-        e = cudaMemcpy2DAsync(p->d_sc + i * blk_scales, static_cast<size_t>(n) * blk_scales * 2,
-                              p->h_ks + b0 * blk_scales, static_cast<size_t>(p->B) * blk_scales * 2,
-                              rn * blk_scales * 2, 2 * static_cast<size_t>(L),
-                              cudaMemcpyHostToDevice, p->transfer);
-    });
-    if (e != cudaSuccess) return cuda_error(e, "scale copies");
+    if (runs > 1 && p->d_hks) {
+        // Every layer's scales of every block by one gather kernel on the transfer stream,
+        // reading the mapped slab: one launch instead of one copy command per run.
+        const int32_t rc = sc::launch_gather_pieces(
+            p->d_hks, p->B, p->d_sc, reinterpret_cast<const int32_t*>(p->d_stage_meta + p->off_ids),
+            n, 2 * L, static_cast<int64_t>(blk_scales) * 2, p->d_status, p->transfer);
+        if (rc != SC_OK) return rc;
+    } else {
+        for_runs(0, n, [&](size_t b0, size_t i, size_t rn) {
+            e = cudaMemcpy2DAsync(p->d_sc + i * blk_scales, static_cast<size_t>(n) * blk_scales * 2,
+                                  p->h_ks + b0 * blk_scales,
+                                  static_cast<size_t>(p->B) * blk_scales * 2, rn * blk_scales * 2,
+                                  2 * static_cast<size_t>(L), cudaMemcpyHostToDevice, p->transfer);
+        });
+        if (e != cudaSuccess) return cuda_error(e, "scale copies");
+    }
     const size_t src_pitch = static_cast<size_t>(p->B) * blk_codes;
-    const size_t n_groups = all_layers ? 1 : p->group_sizes.size();
-    int32_t l0 = 0;
-    for (size_t gi = 0; gi < n_groups; ++gi) {
-        const int32_t G = all_layers ? L : p->group_sizes[gi];
-        const int s = all_layers ? 0 : static_cast<int>(gi % static_cast<size_t>(p->n_slots));
-        if (!all_layers && p->slot_used[s]) e = cudaStreamWaitEvent(p->transfer, p->slot_free[s], 0);
-        int8_t* stage = all_layers ? p->d_all : p->d_kq[s];
-        const size_t pages = static_cast<size_t>(G) * n;
-        for_runs([&](size_t b0, size_t i, size_t rn) {
-            cudaMemcpy3DParms m = {};
-            m.srcPtr = make_cudaPitchedPtr(p->h_kq, src_pitch, src_pitch, static_cast<size_t>(L));
-            m.srcPos = make_cudaPos(b0 * blk_codes, static_cast<size_t>(l0), 0);
-            m.dstPtr = make_cudaPitchedPtr(stage, static_cast<size_t>(n) * blk_codes,
-                                           static_cast<size_t>(n) * blk_codes, static_cast<size_t>(G));
-            m.dstPos = make_cudaPos(i * blk_codes, 0, 0);
-            m.extent = make_cudaExtent(rn * blk_codes, static_cast<size_t>(G), 2);
-            m.kind = cudaMemcpyHostToDevice;
-            e = cudaMemcpy3DAsync(&m, p->transfer);
+    const size_t slab_codes = static_cast<size_t>(L) * src_pitch;
+    int32_t i0 = 0;
+    for (size_t si = 0; si < n_stages; ++si) {
+        const int32_t m = p->stages[si];
+        const int s = static_cast<int>(si % static_cast<size_t>(p->n_slots));
+        if (p->slot_used[s]) e = cudaStreamWaitEvent(p->transfer, p->slot_free[s], 0);
+        int8_t* slot = p->d_kq[s];
+        const size_t dst_pitch = static_cast<size_t>(m) * blk_codes;
+        const size_t v_off = static_cast<size_t>(L) * dst_pitch;  // V codes of the stage
+        for_runs(i0, i0 + m, [&](size_t b0, size_t i, size_t rn) {
+            const size_t j = i - static_cast<size_t>(i0);
+            if (p->stage_3d) {
+                cudaMemcpy3DParms c = {};
+                c.srcPtr = make_cudaPitchedPtr(p->h_kq, src_pitch, src_pitch, static_cast<size_t>(L));
+                c.srcPos = make_cudaPos(b0 * blk_codes, 0, 0);
+                c.dstPtr = make_cudaPitchedPtr(slot, dst_pitch, dst_pitch, static_cast<size_t>(L));
+                c.dstPos = make_cudaPos(j * blk_codes, 0, 0);
+                c.extent = make_cudaExtent(rn * blk_codes, static_cast<size_t>(L), 2);
+                c.kind = cudaMemcpyHostToDevice;
+                e = cudaMemcpy3DAsync(&c, p->transfer);
+            } else {
+                for (int kv = 0; kv < 2 && e == cudaSuccess; ++kv)
+                    e = cudaMemcpy2DAsync(slot + kv * v_off + j * blk_codes, dst_pitch,
+                                          p->h_kq + kv * slab_codes + b0 * blk_codes, src_pitch,
+                                          rn * blk_codes, static_cast<size_t>(L),
+                                          cudaMemcpyHostToDevice, p->transfer);
+            }
         });
         if (e == cudaSuccess) e = cudaEventRecord(p->ready[s], p->transfer);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, p->ready[s], 0);
-        if (e != cudaSuccess) return cuda_error(e, "layer-group copies");
+        if (e != cudaSuccess) return cuda_error(e, "block-stage copies");
         sc::PagedArgs a{};
-        a.n_requests = G;
-        a.max_pages = n;
+        a.n_requests = L;
+        a.max_pages = m;
         a.page_size = p->chunk;
         a.n_heads = p->H;
         a.head_dim = p->D;
-        a.n_pool_pages = static_cast<int64_t>(pages);
-        a.pool_kq = stage;
-        a.pool_vq = stage + pages * blk_codes;
-        a.pool_ks = p->d_sc + static_cast<size_t>(l0) * n * blk_scales;
-        a.pool_vs = p->d_sc + (static_cast<size_t>(L) + l0) * n * blk_scales;
-        a.page_table = p->d_table;  // identity: page i of request g is page g * n + i
-        a.page_table_stride = n;
-        a.seq_lens = reinterpret_cast<const int32_t*>(p->d_all_meta) + l0;
-        a.delta_p = reinterpret_cast<const float*>(p->d_all_meta + p->off_dps) + static_cast<size_t>(l0) * n;
-        a.delta_p_per_page = 1;
+        a.n_pool_pages = static_cast<int64_t>(L) * m;
+        a.pool_kq = slot;
+        a.pool_vq = slot + v_off;
+        // Scales of layer l, stage page j: row (l * n + i0 + j) of d_sc's K half, i.e. pool
+        // page l * m + j plus a skew of l * (n - m) pages.
+        a.pool_ks = p->d_sc + static_cast<size_t>(i0) * blk_scales;
+        a.pool_vs = p->d_sc + (static_cast<size_t>(L) * n + i0) * blk_scales;
+        a.scale_request_skew = static_cast<int64_t>(n - m) * static_cast<int64_t>(blk_scales);
+        a.page_table = p->d_table;  // identity: page j of layer l is pool page l * m + j
+        a.page_table_stride = m;
+        a.seq_lens = reinterpret_cast<const int32_t*>(p->d_stage_meta) + si;
+        a.seq_len_shared = 1;
+        a.delta_p = reinterpret_cast<const float*>(p->d_stage_meta + p->off_dps) + i0;
+        a.delta_p_per_page = 2;  // block i0 + j's shift, the same for every layer
         a.theta_base = theta_base;
         a.inv_freq = inv_freq;
-        a.k_out_ptrs = reinterpret_cast<const uint64_t*>(p->d_all_meta + p->off_kp) + l0;
-        a.v_out_ptrs = reinterpret_cast<const uint64_t*>(p->d_all_meta + p->off_vp) + l0;
+        a.k_out_ptrs = reinterpret_cast<const uint64_t*>(p->d_stage_meta + p->off_kp);
+        a.v_out_ptrs = reinterpret_cast<const uint64_t*>(p->d_stage_meta + p->off_vp);
+        a.out_ptr_offset = static_cast<int64_t>(i0) * p->chunk * out_strides[0];
         for (int i = 0; i < 3; ++i) a.out_strides[i] = out_strides[i];
         a.out_numel = out_numel;
         a.out_dtype = out_dtype;
@@ -520,12 +579,10 @@ int32_t restore_layer_groups(sc_pipeline* p, bool all_layers, const int32_t* blo
         a.stream = cs;
         const int32_t rc = sc::launch_paged(a);
         if (rc != SC_OK) return rc;
-        if (!all_layers) {
-            e = cudaEventRecord(p->slot_free[s], cs);
-            if (e != cudaSuccess) return cuda_error(e, "restore enqueue");
-            p->slot_used[s] = true;
-        }
-        l0 += G;
+        e = cudaEventRecord(p->slot_free[s], cs);
+        if (e != cudaSuccess) return cuda_error(e, "restore enqueue");
+        p->slot_used[s] = true;
+        i0 += m;
     }
     e = cudaEventRecord(p->done, cs);
     if (e != cudaSuccess) return cuda_error(e, "restore enqueue");
@@ -543,10 +600,10 @@ extern "C" int32_t sc_pipeline_restore_launches(const sc_pipeline* p, int32_t n_
                          (long long)p->max_blocks);
     if (n_blocks == 0)
         *launches = 0;
-    else if (static_cast<int64_t>(p->L) * n_blocks <= p->all_cap_pages)
+    else if (p->stage_cap > 0 && n_blocks <= p->stage_cap)
         *launches = 1;
-    else if (p->group_cap > 1)
-        *launches = static_cast<int32_t>(p->group_sizes.size());
+    else if (p->stage_cap > 0)  // the stages of stage_sizes(): the front ones and a last block
+        *launches = static_cast<int32_t>((n_blocks - 1 + p->stage_cap - 1) / p->stage_cap + 1);
     else
         *launches = p->L;
     return sc::ok();
@@ -575,9 +632,8 @@ extern "C" int32_t sc_pipeline_restore(sc_pipeline* p, const int32_t* block_ids,
     DeviceGuard g(p->device);
     if (!g.ok) return set_error(SC_ERR_CUDA, "cudaSetDevice(%d) failed", p->device);
     cudaStream_t cs = static_cast<cudaStream_t>(compute_stream);
-    if (static_cast<int64_t>(p->L) * n_blocks <= p->all_cap_pages || p->group_cap > 1)
-        return restore_layer_groups(p, static_cast<int64_t>(p->L) * n_blocks <= p->all_cap_pages,
-                                    block_ids, delta_ps, n_blocks, theta_base, inv_freq, k_out,
+    if (p->stage_cap > 0)
+        return restore_block_stages(p, block_ids, delta_ps, n_blocks, theta_base, inv_freq, k_out,
                                     v_out, out_strides, out_numel, out_dtype, cs);
     cudaError_t e = cudaSuccess;
 

@@ -10,7 +10,7 @@ the host (nothing here faults, traps or hangs the GPU):
 * ``preload()`` loads every kernel up front, so a fresh process's first calls enqueued behind
   running work do not wait for it;
 * stream hazards: back-to-back restores and offloads that reuse the staging slots (on the
-  all-layers, layer-group and layer-by-layer paths), the shift metadata and the offload slots,
+  single-stage, block-stage and layer-by-layer paths), the shift metadata and the offload slots,
   with random GPU-side delays on the compute stream and random host delays between enqueues,
   all checked against the oracle.
 """
@@ -126,12 +126,12 @@ def test_preloaded_first_calls_do_not_wait_for_the_device(scb):
     assert dt < 0.25, out.stdout
 
 
-# The restore paths: small restores in one all-layers launch, larger ones in layer groups
-# (here 90-98 blocks of 64 tokens x 8 heads: groups of 5 and 1 layers over two slots), and
-# layer by layer.
+# The restore paths: small restores in one stage and one launch, larger ones in block stages
+# (here 90-98 blocks of 64 tokens x 8 heads over 6 layers, 85 blocks per stage: stages of
+# 44-49, 44-48 and 1 blocks over two slots), and layer by layer.
 PATHS = {
-    "all_layers": dict(blocks=12, chunk=32, h=4, per_layer=False, n=(1, 8)),
-    "layer_groups": dict(blocks=100, chunk=64, h=8, per_layer=False, n=(90, 98)),
+    "single_stage": dict(blocks=12, chunk=32, h=4, per_layer=False, n=(1, 8)),
+    "block_stages": dict(blocks=100, chunk=64, h=8, per_layer=False, n=(90, 98)),
     "per_layer": dict(blocks=12, chunk=32, h=4, per_layer=True, n=(1, 8)),
 }
 

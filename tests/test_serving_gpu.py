@@ -146,9 +146,9 @@ def test_offload_then_restore_round_trip(scb, oracle):
 
 
 @pytest.mark.parametrize("n_blocks", [1, 3, 7])
-def test_all_layers_restore_equals_per_layer(scb, oracle, n_blocks):
-    # a small restore takes the all-layers path (one 3-D copy per run, one launch); it must
-    # write exactly what the layer-by-layer path writes, scattered and consecutive blocks alike
+def test_single_stage_restore_equals_per_layer(scb, oracle, n_blocks):
+    # a small restore fits one block stage (one 3-D copy per run, one launch); it must write
+    # exactly what the layer-by-layer path writes, scattered and consecutive blocks alike
     from speccache_b200.cache import KVRestorePipeline
 
     layers, blocks, chunk, h, d = 5, 12, 32, 4, 128
@@ -189,20 +189,25 @@ def test_all_layers_restore_equals_per_layer(scb, oracle, n_blocks):
         assert bits_equal(outs[0][1][layer], outs[1][1][layer])
 
 
-def test_layer_group_restore_equals_per_layer(scb, oracle):
-    # a restore beyond the all-layers buffer (64 MiB of codes) takes the layer-group path:
-    # groups of up to 6 layers (64 MiB of codes each), here 4, 4, 1, one 3-D copy per run of
-    # blocks and group, one launch per group, the groups rotating over two slots.  Two restores back to back (the second reuses the slots and the scales); both
+def test_block_stage_restore_equals_per_layer(scb, oracle):
+    # a restore beyond one stage (64 MiB of codes over all layers: 56 blocks here) goes in
+    # block stages, here 35, 34 and 1 blocks: one 3-D copy per run of blocks within a stage (a
+    # run that crosses a stage boundary is split), one launch per stage, the stages rotating
+    # over two slots.  Three restores back to back (each reuses the slots and the scales), the
+    # last a fully scattered list (every block its own run, in stages of 40, 39 and 1); all
     # must write exactly what the layer-by-layer path writes.
     from speccache_b200.cache import KVRestorePipeline
 
     layers, blocks, chunk, h, d = 9, 80, 64, 8, 128
-    ids_a = list(range(10, 40)) + list(range(0, 10)) + [45, 44, 43] + list(range(50, 77))
-    ids_b = list(range(79, 59, -1)) + list(range(0, 50))
     g = torch.Generator().manual_seed(77)
-    dps_a = torch.randint(-3000, 3000, (len(ids_a),), generator=g).tolist()
-    dps_b = torch.randint(-3000, 3000, (len(ids_b),), generator=g).tolist()
-    n_a, n_b = len(ids_a) * chunk, len(ids_b) * chunk
+    cases = []
+    for ids, theta, dt in (
+            (list(range(10, 40)) + list(range(0, 10)) + [45, 44, 43] + list(range(50, 77)), 5e5,
+             torch.bfloat16),
+            (list(range(79, 59, -1)) + list(range(0, 50)), 1e4, torch.float16),
+            (list(range(0, 80, 2)) + list(range(79, 0, -2)), 5e5, torch.bfloat16)):
+        dps = torch.randint(-3000, 3000, (len(ids),), generator=g).tolist()
+        cases.append((ids, dps, theta, dt))
     outs = []
     for per_layer in (False, True):
         with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV, per_layer=per_layer) as pipe:
@@ -211,37 +216,43 @@ def test_layer_group_restore_equals_per_layer(scb, oracle):
                 t.copy_(torch.randint(-127, 128, tuple(t.shape), generator=g2, dtype=torch.int8))
             for t in (pipe.k_scale, pipe.v_scale):
                 t.copy_((torch.rand(tuple(t.shape), generator=g2) * 0.05 + 1e-3).half())
-            ka = torch.zeros((layers, n_a, h, d), dtype=torch.bfloat16, device=DEV)
-            va = torch.zeros_like(ka)
-            kb = torch.zeros((layers, n_b, h, d), dtype=torch.float16, device=DEV)
-            vb = torch.zeros_like(kb)
-            # groups of 4, 4, 1 layers (6 fit 64 MiB of codes here), or one per layer
-            assert pipe.restore_launches(len(ids_a)) == (layers if per_layer else 3)
-            assert pipe.restore_launches(4) == (layers if per_layer else 1)  # all-layers buffer
-            pipe.restore(ids_a, dps_a, ka, va, theta=5e5)
-            pipe.restore(ids_b, dps_b, kb, vb, theta=1e4)
+            # stages of 35, 34, 1 blocks (56 fit 64 MiB of codes here), or one per layer
+            assert pipe.restore_launches(70) == (layers if per_layer else 3)
+            assert pipe.restore_launches(4) == (layers if per_layer else 1)  # one stage
+            res = []
+            for ids, dps, theta, dt in cases:
+                k = torch.zeros((layers, len(ids) * chunk, h, d), dtype=dt, device=DEV)
+                v = torch.zeros_like(k)
+                pipe.restore(ids, dps, k, v, theta=theta)
+                res.append((k, v))
             pipe.synchronize()
             assert pipe.status() == 0
-            outs.append([x.cpu() for x in (ka, va, kb, vb)])
+            outs.append([x.cpu() for kv in res for x in kv])
             if not per_layer:
                 for layer in (0, 4, 8):
-                    for ids, dps, theta, k, v, dt in ((ids_a, dps_a, 5e5, ka, va, torch.bfloat16),
-                                                      (ids_b, dps_b, 1e4, kb, vb, torch.float16)):
+                    for (ids, dps, theta, dt), (k, v) in zip(cases, res):
                         kr, vr = oracle.restore_blocks(pipe.k_quant[layer], pipe.k_scale[layer],
                                                        pipe.v_quant[layer], pipe.v_scale[layer],
                                                        ids, dps, theta, dt)
                         assert bits_equal(v[layer].cpu(), vr)
                         torch.testing.assert_close(k[layer].cpu().float(), kr.float(), rtol=1e-2,
                                                    atol=1e-2)
-    for grouped, per_layer in zip(outs[0], outs[1]):
-        assert bits_equal(grouped, per_layer)
+    for staged, per_layer in zip(outs[0], outs[1]):
+        assert bits_equal(staged, per_layer)
+
+
+def stage_count(n, cap):
+    """Launches of a block-stage restore of n blocks with at most cap blocks per stage: one
+    stage, or as few front stages of at most cap blocks as hold n - 1 blocks plus a last
+    one-block stage."""
+    return 1 if n <= cap else -(-(n - 1) // cap) + 1
 
 
 @pytest.mark.parametrize("seed", range(6))
-def test_layer_groups_random_geometries(scb, oracle, seed):
-    # restores just beyond the all-layers buffer, with random layer counts, block lists (runs
-    # and jumps), slot counts, max_restore_blocks and output dtypes: the grouped path must
-    # write the bits of the layer-by-layer path, in fewer launches, and match the oracle
+def test_block_stages_random_geometries(scb, oracle, seed):
+    # restores beyond one stage, with random layer counts, block lists (runs and jumps), slot
+    # counts, max_restore_blocks and output dtypes: the staged path must write the bits of the
+    # layer-by-layer path, in the launches the stage rule gives, and match the oracle
     import random
 
     from speccache_b200.cache import KVRestorePipeline
@@ -249,7 +260,8 @@ def test_layer_groups_random_geometries(scb, oracle, seed):
     rng = random.Random(1000 + seed)
     layers = rng.randint(2, 12)
     chunk, h, d = rng.choice([(64, 8, 128), (32, 8, 128), (64, 4, 256), (128, 8, 64)])
-    need = (64 << 20) // (2 * chunk * h * d) // layers + 1  # blocks that pass the 64 MiB buffer
+    cap = (64 << 20) // (2 * layers * chunk * h * d)  # blocks per 64 MiB stage
+    need = cap + 1
     blocks = need + rng.randint(5, 40)
     n = rng.randint(need, blocks)
     ids = rng.sample(range(blocks), n)
@@ -277,7 +289,7 @@ def test_layer_groups_random_geometries(scb, oracle, seed):
             pipe.synchronize()
             assert pipe.status() == 0
             outs.append((ko.cpu(), vo.cpu()))
-    assert launches[1] == layers and launches[0] <= layers and (layers < 3 or launches[0] < layers)
+    assert launches == [stage_count(n, min(cap, max_rb)), layers]
     assert bits_equal(outs[0][0], outs[1][0]) and bits_equal(outs[0][1], outs[1][1])
     layer = rng.randrange(layers)
     kr, vr = oracle.restore_blocks(data[0][layer], data[1][layer], data[2][layer], data[3][layer],

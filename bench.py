@@ -16,7 +16,10 @@ Workloads (synthetic, seeded data with the shapes and value distributions below)
   - ``e2e``: the same metric through the pinned-host restore pipeline
     (``sc_pipeline_restore``, the C ABI): each step copies the 32 layers' codes and
     scales from pinned host slabs (545 MB), restores them, and reads back the last cache
-    row of K and V.  ``restore_ms`` is the T = 8192 restore time.
+    row of K and V.  ``restore_ms`` is the T = 8192 restore time.  ``--block-order
+    scattered`` restores the same 128 blocks from a slab of 256, every other block in a
+    seeded random order (every block its own run: the fragmented pool of a long-running
+    server) instead of consecutive ones.
   - ``e2e.h2d_ceiling_gbs``: the copy-only ceiling at the same N - every rank copies its
     whole pinned slab into HBM with nothing else running, all ranks at once, best of 5 -
     and ``e2e.h2d_vs_ceiling``, the pipeline's host-to-device rate over it.
@@ -52,6 +55,7 @@ import importlib
 import importlib.util
 import json
 import os
+import random
 import statistics
 import subprocess
 import sys
@@ -592,15 +596,22 @@ def bench_llama8b(args, scb, dist: Dist, cfg: dict):
     if args.skip_e2e:
         return line
     n_blocks = t // CHUNK
-    with KVRestorePipeline(layers, n_blocks, CHUNK, h, d, device=dev, n_slots=3,
-                           write_combined=args.write_combined) as pipe:
-        pipe.k_quant.view(layers, t, h, d).copy_(kq.cpu())
-        pipe.v_quant.view(layers, t, h, d).copy_(vq.cpu())
-        pipe.k_scale.view(layers, t, h, 1).copy_(ks.cpu())
-        pipe.v_scale.view(layers, t, h, 1).copy_(vs.cpu())
+    scattered = args.block_order == "scattered"
+    slab_blocks = 2 * n_blocks if scattered else n_blocks
+    if scattered:  # block i of the restore lives at slab block ids[i]: every block its own run
+        ids = [2 * b + 1 for b in range(n_blocks)]
+        random.Random(SEED).shuffle(ids)
+    else:
+        ids = list(range(n_blocks))
+    with KVRestorePipeline(layers, slab_blocks, CHUNK, h, d, device=dev, n_slots=3,
+                           max_restore_blocks=n_blocks, write_combined=args.write_combined) as pipe:
+        where = torch.tensor(ids)
+        for slab, src, last in ((pipe.k_quant, kq, d), (pipe.v_quant, vq, d),
+                                (pipe.k_scale, ks, 1), (pipe.v_scale, vs, 1)):
+            slab[:, where] = src.cpu().view(layers, n_blocks, CHUNK, h, last)
         ko = [k_out[i] for i in range(layers)]
         vo = [v_out[i] for i in range(layers)]
-        ids, shifts = list(range(n_blocks)), [dp] * n_blocks
+        shifts = [dp] * n_blocks
         tail = torch.empty((2, h, d), dtype=cfg["out"]).pin_memory()
 
         def e2e_step():
@@ -610,6 +621,7 @@ def bench_llama8b(args, scb, dist: Dist, cfg: dict):
 
         e2e_ms, _ = time_steps(e2e_step, args.steps, args.warmup, dist)
         launches = pipe.restore_launches(n_blocks)
+        runs = 1 + sum(1 for a, b in zip(ids, ids[1:]) if b != a + 1)
         ceiling = h2d_ceiling(pipe, dist)
         # one restore on its own (latency, nothing overlapping it)
         torch.cuda.synchronize(dev)
@@ -624,7 +636,8 @@ def bench_llama8b(args, scb, dist: Dist, cfg: dict):
                            tail.numel() * tail.element_size(), launches * args.steps,
                            f"sc_pipeline_restore from pinned host slabs, {launches} kernel "
                            f"launches per restore of {layers} layers",
-                           {"restore_ms_single": single_ms, "device_status": status})
+                           {"restore_ms_single": single_ms, "device_status": status,
+                            "block_order": args.block_order, "runs": runs})
     line["e2e"].update(ceiling)
     line["e2e"]["h2d_vs_ceiling"] = line["e2e"]["h2d_gbs"] / ceiling["h2d_ceiling_gbs"]
     return line
@@ -1001,6 +1014,10 @@ def main() -> None:
                     help="N > 1: skip the in-run check of the head-shard gather onto GPU 0")
     ap.add_argument("--gather", action="store_true",
                     help="llama70b: restore every rank's head shard into GPU 0's caches (NVLink)")
+    ap.add_argument("--block-order", choices=["contiguous", "scattered"], default="contiguous",
+                    help="llama8b e2e: restore consecutive blocks (default), or the same number "
+                         "of blocks scattered over a slab twice as large (every other block, in "
+                         "a seeded random order: every block its own run)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

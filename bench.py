@@ -37,7 +37,9 @@ Workloads (synthetic, seeded data with the shapes and value distributions below)
   launch.
 * ``roundtrip``: Qwen-2.5-7B-like - 28 layers, 4 KV heads x 128, T = 16384, theta 1e6,
   fp16 N(0,1) K/V with 2% of channels scaled x10; quantize (bit-exact twin) then restore
-  with shift 2048 into fp16.
+  with shift 2048 into fp16.  ``offload``: every layer quantized on the GPU into the pinned
+  slabs (``sc_pipeline_offload``); with ``--block-order scattered`` into every other block
+  of a slab twice as large, in a seeded random order.
 * ``llama70b``: Llama-3-70B KV geometry - 80 layers, 8 KV heads x 128, T = 32768, shift
   8192, theta 5e5; pinned host slab -> GPU pipeline; with N GPUs each rank restores 8/N
   heads (strong scaling).  ``value`` is end-to-end (H2D-bound).
@@ -836,27 +838,44 @@ def bench_roundtrip(args, scb, dist: Dist, cfg: dict):
 
 
 def offload_line(args, dist: Dist, xk: torch.Tensor, xv: torch.Tensor) -> dict:
-    """The cold-miss direction: every layer's fp16 K/V quantized on the GPU and copied into
+    """The cold-miss direction: every layer's fp16 K/V quantized on the GPU and moved into
     the pinned host slabs (sc_pipeline_offload), timed on the current stream through
-    sc_pipeline_join (no host wait inside the step)."""
+    sc_pipeline_join (no host wait inside the step).  With ``--block-order scattered`` the
+    blocks go to every other block of a slab twice as large, in a seeded random order (every
+    block its own run), as a pool that allocates blocks from a free list would place them."""
     from speccache_b200.cache import KVRestorePipeline
 
     layers, t, h, d = xk.shape
-    ids = list(range(t // CHUNK))
-    with KVRestorePipeline(layers, len(ids), CHUNK, h, d, device=dist.device) as pipe:
+    n_blocks = t // CHUNK
+    scattered = args.block_order == "scattered"
+    if scattered:
+        ids = [2 * b + 1 for b in range(n_blocks)]
+        random.Random(SEED).shuffle(ids)
+    else:
+        ids = list(range(n_blocks))
+    with KVRestorePipeline(layers, 2 * n_blocks if scattered else n_blocks, CHUNK, h, d,
+                           device=dist.device, max_restore_blocks=n_blocks) as pipe:
         def step():
             for layer in range(layers):
                 pipe.offload(layer, ids, xk[layer], xv[layer])
             pipe.join()
 
         ms, _ = time_steps(step, args.steps, args.warmup, dist)
+        status = pipe.status()
     rows = layers * t * h
     d2h = 2 * rows * (d + 2)  # int8 codes and fp16 scales of K and V
+    # per layer: the K and V quantize launches, plus two scatter launches (codes, scales) of at
+    # most 960 blocks each for a scattered list
+    per_layer = 2 + (2 * -(-n_blocks // 960) if scattered else 0)
     return {"ms_per_step": ms / args.steps,
             "d2h_gbs": d2h * dist.world * args.steps / (ms / 1e3) / 1e9,
             "quantize_gbs": quantize_bytes(rows, d) * dist.world * args.steps / (ms / 1e3) / 1e9,
-            "d2h_bytes_per_step": d2h, "gpu_launches": 2 * layers * args.steps,
-            "path": "quantize on the GPU into a staging slot, 2-D D2H copies into the pinned slabs"}
+            "d2h_bytes_per_step": d2h, "gpu_launches": per_layer * layers * args.steps,
+            "block_order": args.block_order, "device_status": status,
+            "path": ("quantize on the GPU into a staging slot, one scatter kernel per layer "
+                     "writing the blocks into the mapped pinned slabs" if scattered else
+                     "quantize on the GPU into a staging slot, 2-D D2H copies into the pinned "
+                     "slabs")}
 
 
 def bench_keyshift(args, scb, dist: Dist, cfg: dict):
@@ -1015,9 +1034,10 @@ def main() -> None:
     ap.add_argument("--gather", action="store_true",
                     help="llama70b: restore every rank's head shard into GPU 0's caches (NVLink)")
     ap.add_argument("--block-order", choices=["contiguous", "scattered"], default="contiguous",
-                    help="llama8b e2e: restore consecutive blocks (default), or the same number "
-                         "of blocks scattered over a slab twice as large (every other block, in "
-                         "a seeded random order: every block its own run)")
+                    help="llama8b e2e restore and roundtrip offload: consecutive blocks "
+                         "(default), or the same number of blocks scattered over a slab twice "
+                         "as large (every other block, in a seeded random order: every block "
+                         "its own run)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

@@ -285,9 +285,12 @@ SC_API int32_t sc_pipeline_restore(sc_pipeline* p, const int32_t* block_ids, con
 /*
  * Enqueue the offload of n_blocks freshly computed K/V blocks of one layer into the slabs:
  * quantize on the GPU (sc_quantize_int8 arithmetic, bit-exact with the reference) into one of
- * two device staging slots on compute_stream, then copy codes and scales to the pinned slabs
- * on the pipeline's transfer stream (K and V as the two rows of one 2-D copy), so the next
- * layer's quantize overlaps this layer's copies.  Replaces the cold-miss offload of the reference runner:
+ * two device staging slots on compute_stream, then move codes and scales to the pinned slabs
+ * on the pipeline's transfer stream, so the next layer's quantize overlaps this layer's
+ * transfer: for consecutive block ids one 2-D copy of the codes (K and V as its two rows) and
+ * one of the scales; for a list in several runs one scatter kernel writing every block into
+ * the mapped slabs (a copy command per run costs about 5 us; SM stores into pinned memory run
+ * at the PCIe rate whatever the block order).  Replaces the cold-miss offload of the reference runner:
  * quantize_kv_int8 + .cpu() + PinnedKVPool.write_block (speccache/serving/pipeline.py:506-524,
  * speccache/cache/pinned_pool.py:275-367).
  *  k, v       device [n_blocks * chunk_size, n_heads, head_dim], dtype x_dtype (F16|BF16|F32),

@@ -183,7 +183,8 @@ class KVRestorePipeline:
         return arr
 
     def offload(self, layer: int, block_ids, k: torch.Tensor, v: torch.Tensor) -> None:
-        """Enqueue quantize-on-GPU + D2H of freshly computed K/V into the slabs.
+        """Enqueue quantize-on-GPU + D2H of freshly computed K/V into the slabs (copies for
+        consecutive block ids, one scatter kernel into the mapped slabs for a scattered list).
 
         ``k`` / ``v``: ``[n * chunk, H, D]`` fp16/bf16/fp32 CUDA tensors; block i's tokens go
         to slab block ``block_ids[i]`` of ``layer``.  The quantisation is bit-exact with the

@@ -86,6 +86,16 @@ int32_t launch_gather_pieces(const void* src, int64_t src_blocks, void* dst, con
                              int32_t n, int32_t rows, int64_t piece_bytes, int32_t* status,
                              cudaStream_t stream);
 
+// Scatter rows x n pieces of piece_bytes (a multiple of 16) from src (row pitch src_pitch
+// pieces) into a device-accessible destination: piece (t, i) goes to piece
+// t * dst_pitch + ids[i].  The ids (host array, each in [0, bound)) are passed in the launch
+// parameters, kMaxScatterIds per launch; an id outside [0, bound) skips its piece and ORs
+// SC_STATUS_BAD_PAGE_ID into *status.
+constexpr int32_t kMaxScatterIds = 960;
+int32_t launch_scatter_pieces(const void* src, int64_t src_pitch, void* dst, int64_t dst_pitch,
+                              int64_t bound, const int32_t* ids, int32_t n, int32_t rows,
+                              int64_t piece_bytes, int32_t* status, cudaStream_t stream);
+
 // Load the kernels the pipeline launches (paged restore; quantize with fp16 scales) on the
 // current device now.  CUDA loads a kernel's module lazily at its first launch, and that
 // load waits for the device to go idle, which would make a first restore or offload enqueued

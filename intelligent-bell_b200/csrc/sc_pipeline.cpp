@@ -29,7 +29,9 @@
 //     layer, K and V codes of each run with one 2-D copy of two rows into a slot, one
 //     paged-kernel launch per layer.
 // The offload runs the other way: the quantize kernel writes a device staging buffer on
-// the compute stream, an event hands it to the transfer stream, D2H copies fill the slabs.
+// the compute stream, an event hands it to the transfer stream, and D2H copies (consecutive
+// block ids) or one scatter kernel writing the mapped slabs (a list in several runs) fill the
+// slabs.
 // Nothing on the host waits during a restore or an offload while fewer than four earlier
 // restores still have their metadata upload queued (each upload follows the previous
 // restore's kernels; the host metadata buffers form a ring of four); sc_pipeline_synchronize
@@ -184,9 +186,12 @@ struct sc_pipeline {
     int64_t stage_cap = 0;
     bool stage_3d = false;
     std::vector<int32_t> stages;  // the current restore's stage sizes
-    // The scale slab as the device addresses it (mapped pinned memory), for the scale gather
-    // kernel of restores in more than one run; null where the slab is not mapped.
-    const uint16_t* d_hks = nullptr;
+    // The slabs as the device addresses them (mapped pinned memory): the scale gather of
+    // restores and the scatter of offloads in more than one run read and write through them;
+    // null where a slab is not mapped (or, for the scales, where one block's scales of a layer
+    // are not a multiple of 16 bytes).
+    int8_t* d_hkq = nullptr;
+    uint16_t* d_hks = nullptr;
     // kMetaRing host buffers, each seq[max stages] | dps[max_blocks] | ids[max_blocks] |
     // k_out[L] | v_out[L]
     uint8_t* h_stage_meta = nullptr;
@@ -305,7 +310,7 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
         e = cudaHostAlloc(dst, bytes, hflags);
         if (e == cudaSuccess) memset(*dst, 0, bytes);  // first touch on the bound thread
     };
-    halloc(2 * slab_codes, &ptr, slab_flags), p->h_kq = static_cast<int8_t*>(ptr);
+    halloc(2 * slab_codes, &ptr, slab_flags | cudaHostAllocMapped), p->h_kq = static_cast<int8_t*>(ptr);
     if (e == cudaSuccess) p->h_vq = p->h_kq + slab_codes;
     halloc(2 * slab_scales * 2, &ptr, slab_flags | cudaHostAllocMapped),
         p->h_ks = static_cast<uint16_t*>(ptr);
@@ -375,15 +380,20 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
                               cudaHostAllocPortable);
         for (int i = 0; i < kMetaRing && e == cudaSuccess; ++i)
             e = cudaEventCreateWithFlags(&p->stage_meta_uploaded[i], cudaEventDisableTiming);
-        // The scale gather reads the slab in 16-byte units: one block's scales of one layer
-        // (chunk x heads fp16) must be a multiple of 16 bytes.
+    }
+    if (e == cudaSuccess) {
+        // The piece kernels move 16-byte units: one block's codes of a layer always are a
+        // multiple of 16 bytes (head_dim is a multiple of 32); its scales (chunk x heads fp16)
+        // must be too.  A slab that is not mapped goes by copies.
         void* mapped = nullptr;
-        if (e == cudaSuccess && (row * 2) % 16 == 0) {
-            if (cudaHostGetDevicePointer(&mapped, p->h_ks, 0) == cudaSuccess)
-                p->d_hks = static_cast<const uint16_t*>(mapped);
-            else
-                cudaGetLastError();  // not mapped: the scales go by copies
-        }
+        if (cudaHostGetDevicePointer(&mapped, p->h_kq, 0) == cudaSuccess)
+            p->d_hkq = static_cast<int8_t*>(mapped);
+        else
+            cudaGetLastError();
+        if ((row * 2) % 16 == 0 && cudaHostGetDevicePointer(&mapped, p->h_ks, 0) == cudaSuccess)
+            p->d_hks = static_cast<uint16_t*>(mapped);
+        else
+            cudaGetLastError();
     }
     // Identity page table: a stage's pool holds n_layers x (at most stage_cap) pages.
     int64_t table_len = max_restore_blocks;
@@ -794,36 +804,55 @@ extern "C" int32_t sc_pipeline_offload(sc_pipeline* p, int32_t layer, const int3
     if (e == cudaSuccess) e = cudaStreamWaitEvent(p->transfer, p->o_ready[s], 0);
     const size_t lay_codes = static_cast<size_t>(layer) * p->B * blk_codes;
     const size_t lay_scales = static_cast<size_t>(layer) * p->B * blk_scales;
-    // Per run: K and V codes as the two rows of one 2-D copy (host pitch slab_codes, device
-    // pitch stage_codes), and the same for the scales.
-    for (int32_t i = 0; i < n_blocks && e == cudaSuccess;) {
-        int32_t n = 1;
-        while (i + n < n_blocks && block_ids[i + n] == block_ids[i] + n) ++n;
-        const size_t b0 = static_cast<size_t>(block_ids[i]);
-        const size_t src = static_cast<size_t>(i);
-        int8_t* hc = p->h_kq + lay_codes + b0 * blk_codes;
-        const int8_t* dc = okq + src * blk_codes;
-        if (p->codes_2d) {
-            e = cudaMemcpy2DAsync(hc, slab_codes, dc, stage_codes, n * blk_codes, 2,
-                                  cudaMemcpyDeviceToHost, p->transfer);
-        } else {
-            e = cudaMemcpyAsync(hc, dc, n * blk_codes, cudaMemcpyDeviceToHost, p->transfer);
-            if (e == cudaSuccess)
-                e = cudaMemcpyAsync(hc + slab_codes, dc + stage_codes, n * blk_codes,
-                                    cudaMemcpyDeviceToHost, p->transfer);
+    int32_t runs = 1;
+    for (int32_t i = 1; i < n_blocks; ++i) runs += block_ids[i] != block_ids[i - 1] + 1;
+    if (e == cudaSuccess && runs > 1 && p->d_hkq && p->d_hks) {
+        // A list in several runs: one scatter kernel writes every block's K and V codes into
+        // the mapped slab (rows: K, V), one its scales, on the transfer stream, instead of two
+        // copy commands per run.
+        const int64_t lb = static_cast<int64_t>(p->L) * p->B;  // K -> V slab distance, blocks
+        rc = sc::launch_scatter_pieces(okq, p->max_blocks, p->d_hkq + lay_codes, lb, p->B,
+                                       block_ids, n_blocks, 2, static_cast<int64_t>(blk_codes),
+                                       p->d_status, p->transfer);
+        if (rc == SC_OK)
+            rc = sc::launch_scatter_pieces(oks, p->max_blocks, p->d_hks + lay_scales, lb, p->B,
+                                           block_ids, n_blocks, 2,
+                                           static_cast<int64_t>(blk_scales) * 2, p->d_status,
+                                           p->transfer);
+        if (rc != SC_OK) return rc;
+    } else {
+        // Per run: K and V codes as the two rows of one 2-D copy (host pitch slab_codes,
+        // device pitch stage_codes), and the same for the scales.
+        for (int32_t i = 0; i < n_blocks && e == cudaSuccess;) {
+            int32_t n = 1;
+            while (i + n < n_blocks && block_ids[i + n] == block_ids[i] + n) ++n;
+            const size_t b0 = static_cast<size_t>(block_ids[i]);
+            const size_t src = static_cast<size_t>(i);
+            int8_t* hc = p->h_kq + lay_codes + b0 * blk_codes;
+            const int8_t* dc = okq + src * blk_codes;
+            if (p->codes_2d) {
+                e = cudaMemcpy2DAsync(hc, slab_codes, dc, stage_codes, n * blk_codes, 2,
+                                      cudaMemcpyDeviceToHost, p->transfer);
+            } else {
+                e = cudaMemcpyAsync(hc, dc, n * blk_codes, cudaMemcpyDeviceToHost, p->transfer);
+                if (e == cudaSuccess)
+                    e = cudaMemcpyAsync(hc + slab_codes, dc + stage_codes, n * blk_codes,
+                                        cudaMemcpyDeviceToHost, p->transfer);
+            }
+            uint16_t* hs = p->h_ks + lay_scales + b0 * blk_scales;
+            const uint16_t* ds = oks + src * blk_scales;
+            if (e == cudaSuccess && p->offload_scales_2d) {
+                e = cudaMemcpy2DAsync(hs, slab_scales * 2, ds, stage_scales * 2,
+                                      n * blk_scales * 2, 2, cudaMemcpyDeviceToHost, p->transfer);
+            } else if (e == cudaSuccess) {
+                e = cudaMemcpyAsync(hs, ds, n * blk_scales * 2, cudaMemcpyDeviceToHost,
+                                    p->transfer);
+                if (e == cudaSuccess)
+                    e = cudaMemcpyAsync(hs + slab_scales, ds + stage_scales, n * blk_scales * 2,
+                                        cudaMemcpyDeviceToHost, p->transfer);
+            }
+            i += n;
         }
-        uint16_t* hs = p->h_ks + lay_scales + b0 * blk_scales;
-        const uint16_t* ds = oks + src * blk_scales;
-        if (e == cudaSuccess && p->offload_scales_2d) {
-            e = cudaMemcpy2DAsync(hs, slab_scales * 2, ds, stage_scales * 2, n * blk_scales * 2, 2,
-                                  cudaMemcpyDeviceToHost, p->transfer);
-        } else if (e == cudaSuccess) {
-            e = cudaMemcpyAsync(hs, ds, n * blk_scales * 2, cudaMemcpyDeviceToHost, p->transfer);
-            if (e == cudaSuccess)
-                e = cudaMemcpyAsync(hs + slab_scales, ds + stage_scales, n * blk_scales * 2,
-                                    cudaMemcpyDeviceToHost, p->transfer);
-        }
-        i += n;
     }
     if (e == cudaSuccess) e = cudaEventRecord(p->o_free[s], p->transfer);
     if (e != cudaSuccess) return cuda_error(e, "offload enqueue");

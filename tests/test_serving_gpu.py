@@ -326,6 +326,54 @@ def test_offload_staging_ring_and_join(scb, oracle):
                 assert bits_equal(got_s.reshape(s_ref.shape), s_ref)
 
 
+@pytest.mark.parametrize("chunk,h,n", [(16, 2, 1500), (3, 1, 40)])
+def test_scattered_offload_writes_only_its_blocks(scb, oracle, chunk, h, n):
+    # an offload of a block list in several runs: the scatter kernel writes each block's codes
+    # and scales into the mapped slabs (1500 blocks: two launches of at most 960 ids); with
+    # 3 tokens x 1 head a block's scales are 6 bytes, not a multiple of 16, so that geometry
+    # goes by copies.  Every other block of the slabs keeps its bytes, and a restore of the
+    # offloaded blocks (its scales gathered from the mapped slab) matches the oracle.
+    import random
+
+    from speccache_b200.cache import KVRestorePipeline
+
+    layers, blocks, d = 2, 2 * n + 5, 32
+    rng = random.Random(n)
+    ids = rng.sample(range(blocks), n)
+    with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV, max_restore_blocks=n) as pipe:
+        pipe.k_quant.fill_(77)
+        pipe.v_quant.fill_(-66)
+        pipe.k_scale.fill_(0.25)
+        pipe.v_scale.fill_(-0.5)
+        g = torch.Generator().manual_seed(n)
+        k = torch.randn((n * chunk, h, d), generator=g).half()
+        v = torch.randn((n * chunk, h, d), generator=g).half()
+        pipe.offload(1, ids, k.to(DEV), v.to(DEV))
+        pipe.synchronize()
+        assert pipe.status() == 0
+        kq, ks = oracle.quantize_kv_int8(k)
+        vq, vs = oracle.quantize_kv_int8(v)
+        where = torch.tensor(ids)
+        assert torch.equal(pipe.k_quant[1, where].reshape(kq.shape), kq)
+        assert torch.equal(pipe.v_quant[1, where].reshape(vq.shape), vq)
+        assert bits_equal(pipe.k_scale[1, where].reshape(ks.shape), ks)
+        assert bits_equal(pipe.v_scale[1, where].reshape(vs.shape), vs)
+        rest = torch.tensor(sorted(set(range(blocks)) - set(ids)))
+        assert (pipe.k_quant[1, rest] == 77).all() and (pipe.v_quant[1, rest] == -66).all()
+        assert (pipe.k_scale[1, rest] == 0.25).all() and (pipe.v_scale[1, rest] == -0.5).all()
+        assert (pipe.k_quant[0] == 77).all() and (pipe.v_scale[0] == -0.5).all()
+        dps = [rng.randint(-4000, 4000) for _ in ids]
+        ko = torch.empty((layers, n * chunk, h, d), dtype=torch.float16, device=DEV)
+        vo = torch.empty_like(ko)
+        pipe.restore(ids, dps, ko, vo)
+        pipe.synchronize()
+        assert pipe.status() == 0
+        kr, vr = oracle.restore_blocks(pipe.k_quant[1], pipe.k_scale[1], pipe.v_quant[1],
+                                       pipe.v_scale[1], ids, dps, 10000.0, torch.float16)
+        assert bits_equal(vo[1].cpu(), vr)
+        torch.testing.assert_close(ko[1].cpu().float(), kr.float(), rtol=1e-2, atol=1e-2)
+
+
 def test_pool_async_dma_multi_chunk_parity(scb, oracle):
     # reference tests/test_phase2_engine.py:297-359: 4 chunks with distinct shifts
     from speccache_b200.cache import PinnedKVPool

@@ -622,7 +622,7 @@ def bench_llama8b(args, scb, dist: Dist, cfg: dict):
             tail[1].copy_(v_out[layers - 1, t - 1], non_blocking=True)
 
         e2e_ms, _ = time_steps(e2e_step, args.steps, args.warmup, dist)
-        launches = pipe.restore_launches(n_blocks)
+        launches, copies = pipe.restore_plan(ids)
         runs = 1 + sum(1 for a, b in zip(ids, ids[1:]) if b != a + 1)
         ceiling = h2d_ceiling(pipe, dist)
         # one restore on its own (latency, nothing overlapping it)
@@ -639,7 +639,8 @@ def bench_llama8b(args, scb, dist: Dist, cfg: dict):
                            f"sc_pipeline_restore from pinned host slabs, {launches} kernel "
                            f"launches per restore of {layers} layers",
                            {"restore_ms_single": single_ms, "device_status": status,
-                            "block_order": args.block_order, "runs": runs})
+                            "block_order": args.block_order, "runs": runs,
+                            "copies_per_restore": copies})
     line["e2e"].update(ceiling)
     line["e2e"]["h2d_vs_ceiling"] = line["e2e"]["h2d_gbs"] / ceiling["h2d_ceiling_gbs"]
     return line
@@ -862,16 +863,15 @@ def offload_line(args, dist: Dist, xk: torch.Tensor, xv: torch.Tensor) -> dict:
 
         ms, _ = time_steps(step, args.steps, args.warmup, dist)
         status = pipe.status()
+        per_layer, copies = pipe.offload_plan(ids)  # launches and copy commands per layer
     rows = layers * t * h
     d2h = 2 * rows * (d + 2)  # int8 codes and fp16 scales of K and V
-    # per layer: the K and V quantize launches, plus two scatter launches (codes, scales) of at
-    # most 960 blocks each for a scattered list
-    per_layer = 2 + (2 * -(-n_blocks // 960) if scattered else 0)
     return {"ms_per_step": ms / args.steps,
             "d2h_gbs": d2h * dist.world * args.steps / (ms / 1e3) / 1e9,
             "quantize_gbs": quantize_bytes(rows, d) * dist.world * args.steps / (ms / 1e3) / 1e9,
             "d2h_bytes_per_step": d2h, "gpu_launches": per_layer * layers * args.steps,
-            "block_order": args.block_order, "device_status": status,
+            "copies_per_step": copies * layers, "block_order": args.block_order,
+            "device_status": status,
             "path": ("quantize on the GPU into a staging slot, one scatter kernel per layer "
                      "writing the blocks into the mapped pinned slabs" if scattered else
                      "quantize on the GPU into a staging slot, 2-D D2H copies into the pinned "
@@ -963,7 +963,7 @@ def bench_llama70b(args, scb, dist: Dist, cfg: dict):
 
         total_ms, _ = time_steps(step, args.steps, args.warmup, dist)
         status = pipe.status()
-        launches = pipe.restore_launches(n_blocks)
+        launches, copies = pipe.restore_plan(ids)
         if gather is not None:
             dist.barrier()  # the owner's buffers stay alive until every writer is done
             gather.close()
@@ -972,7 +972,8 @@ def bench_llama70b(args, scb, dist: Dist, cfg: dict):
             if args.gather else "sc_pipeline_restore from pinned host slabs (bytes of all ranks)")
     e2e = e2e_line(nbytes, total_ms, args.steps, dist.world, h2d,
                    tail.numel() * tail.element_size() if k_out is not None else 0,
-                   launches * args.steps, path, {"device_status": status})
+                   launches * args.steps, path,
+                   {"device_status": status, "copies_per_restore": copies})
     return {"value": e2e["value"], "ms_per_step": total_ms / args.steps, "scaling": "strong",
             "gpu_launches": launches * args.steps, "e2e": e2e,
             "roofline": {"bound": "pcie-h2d", "achieved": e2e["h2d_gbs"] / dist.world,

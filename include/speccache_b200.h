@@ -324,6 +324,14 @@ SC_API int32_t sc_pipeline_status(sc_pipeline* p, int32_t* status_bits);
 SC_API int32_t sc_pipeline_restore_launches(const sc_pipeline* p, int32_t n_blocks,
                                             int32_t* launches);
 
+/* The work a restore (offload = 0) or an offload of one layer (offload = 1) of this block list
+ * would enqueue: the kernel launches (restore: one per block stage, plus the scale gather of a
+ * list in several runs; offload: the K and V quantize, plus the scatter kernels of a list in
+ * several runs) into *launches and the copy commands (metadata upload included) into *copies.
+ * No device work.  No counterpart in the reference. */
+SC_API int32_t sc_pipeline_plan(const sc_pipeline* p, int32_t offload, const int32_t* block_ids,
+                                int32_t n_blocks, int32_t* launches, int32_t* copies);
+
 SC_API int32_t sc_pipeline_destroy(sc_pipeline* p);
 
 /*

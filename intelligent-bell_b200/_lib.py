@@ -87,6 +87,7 @@ _SIGNATURES = {
     "sc_pipeline_join": (_i32, [_vp, _vp]),
     "sc_pipeline_status": (_i32, [_vp, _vp]),
     "sc_pipeline_restore_launches": (_i32, [_vp, _i32, _vp]),
+    "sc_pipeline_plan": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp]),
     "sc_pipeline_destroy": (_i32, [_vp]),
     "sc_ipc_export": (_i32, [_vp, _vp, _vp]),
     "sc_ipc_import": (_i32, [_vp, _i64, _vp, _vp]),

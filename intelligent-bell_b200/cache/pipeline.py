@@ -226,6 +226,26 @@ class KVRestorePipeline:
                    "sc_pipeline_restore_launches")
         return int(count.value)
 
+    def restore_plan(self, block_ids) -> tuple[int, int]:
+        """(kernel launches, copy commands) a restore of ``block_ids`` enqueues: one launch per
+        block stage plus the scale gather of a list in several runs; one copy per run of
+        consecutive ids within a stage, the scales' copies and the metadata upload."""
+        return self._plan(0, block_ids)
+
+    def offload_plan(self, block_ids) -> tuple[int, int]:
+        """(kernel launches, copy commands) an offload of one layer into ``block_ids``
+        enqueues: the K and V quantize, plus the scatter kernels of a list in several runs
+        (else two copies per run)."""
+        return self._plan(1, block_ids)
+
+    def _plan(self, offload: int, block_ids) -> tuple[int, int]:
+        ids = np.ascontiguousarray(np.asarray(block_ids, dtype=np.int32).reshape(-1))
+        launches, copies = ctypes.c_int32(0), ctypes.c_int32(0)
+        _lib.check(self._lib.sc_pipeline_plan(self._h, offload, ids.ctypes.data, int(ids.size),
+                                              ctypes.byref(launches), ctypes.byref(copies)),
+                   "sc_pipeline_plan")
+        return int(launches.value), int(copies.value)
+
     def status(self) -> int:
         """Device status bits of the restore kernels (0 = clean); reading clears them."""
         bits = ctypes.c_int32(0)

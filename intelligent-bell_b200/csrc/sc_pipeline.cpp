@@ -619,6 +619,55 @@ extern "C" int32_t sc_pipeline_restore_launches(const sc_pipeline* p, int32_t n_
     return sc::ok();
 }
 
+extern "C" int32_t sc_pipeline_plan(const sc_pipeline* p, int32_t offload,
+                                    const int32_t* block_ids, int32_t n_blocks,
+                                    int32_t* launches, int32_t* copies) {
+    if (!p || !launches || !copies || (n_blocks > 0 && !block_ids))
+        return set_error(SC_ERR_INVALID_ARGUMENT, "null argument");
+    if (n_blocks < 0 || n_blocks > p->max_blocks)
+        return set_error(SC_ERR_INVALID_ARGUMENT, "n_blocks %d outside [0, %lld]", n_blocks,
+                         (long long)p->max_blocks);
+    for (int32_t i = 0; i < n_blocks; ++i)
+        if (block_ids[i] < 0 || block_ids[i] >= p->B)
+            return set_error(SC_ERR_INVALID_ARGUMENT, "block id %d outside [0, %lld)",
+                             block_ids[i], (long long)p->B);
+    *launches = 0;
+    *copies = 0;
+    if (n_blocks == 0) return sc::ok();
+    // Runs of consecutive block ids among positions [lo, hi).
+    auto runs_in = [&](int32_t lo, int32_t hi) {
+        int32_t r = hi > lo ? 1 : 0;
+        for (int32_t i = lo + 1; i < hi; ++i) r += block_ids[i] != block_ids[i - 1] + 1;
+        return r;
+    };
+    const int32_t runs = runs_in(0, n_blocks);
+    if (offload) {  // sc_pipeline_offload: quantize K and V, then scatter kernels or copies
+        if (runs > 1 && p->d_hkq && p->d_hks) {
+            *launches = 2 + 2 * ((n_blocks + sc::kMaxScatterIds - 1) / sc::kMaxScatterIds);
+        } else {
+            *launches = 2;
+            *copies = runs * ((p->codes_2d ? 1 : 2) + (p->offload_scales_2d ? 1 : 2));
+        }
+        return sc::ok();
+    }
+    if (p->stage_cap > 0) {  // block stages: metadata upload, scales, per stage its runs
+        std::vector<int32_t> st;
+        stage_sizes(n_blocks, p->stage_cap, st);
+        const bool gather = runs > 1 && p->d_hks;
+        *launches = static_cast<int32_t>(st.size()) + (gather ? 1 : 0);
+        *copies = 1 + (gather ? 0 : runs);
+        int32_t i0 = 0;
+        for (const int32_t m : st) {
+            *copies += runs_in(i0, i0 + m) * (p->stage_3d ? 1 : 2);
+            i0 += m;
+        }
+    } else {  // layer by layer
+        *launches = p->L;
+        *copies = 1 + (p->scales_2d ? runs : 2 * p->L * runs) + p->L * runs * (p->codes_2d ? 1 : 2);
+    }
+    return sc::ok();
+}
+
 extern "C" int32_t sc_pipeline_restore(sc_pipeline* p, const int32_t* block_ids,
                                        const int32_t* delta_ps, int32_t n_blocks,
                                        double theta_base, const float* inv_freq,

@@ -219,6 +219,15 @@ def test_block_stage_restore_equals_per_layer(scb, oracle):
             # stages of 35, 34, 1 blocks (56 fit 64 MiB of codes here), or one per layer
             assert pipe.restore_launches(70) == (layers if per_layer else 3)
             assert pipe.restore_launches(4) == (layers if per_layer else 1)  # one stage
+            # the first list is 6 runs; its stages hold 2, 5 and 1 of them.  Staged: 3
+            # launches + the scale gather, the metadata upload + 8 code copies; layer by
+            # layer: 9 launches, the upload + 6 scale copies + 9 x 6 code copies
+            assert pipe.restore_plan(cases[0][0]) == ((9, 61) if per_layer else (4, 9))
+            assert pipe.restore_plan([3, 4, 5, 6]) == ((9, 11) if per_layer else (1, 3))
+            # offloads: K and V quantize + the codes' and scales' scatter for 80 single runs;
+            # one run: two copies (codes; scales)
+            assert pipe.offload_plan(cases[2][0]) == (4, 0)
+            assert pipe.offload_plan([5, 6, 7]) == (2, 2)
             res = []
             for ids, dps, theta, dt in cases:
                 k = torch.zeros((layers, len(ids) * chunk, h, d), dtype=dt, device=DEV)

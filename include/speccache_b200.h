@@ -256,6 +256,9 @@ typedef struct sc_pipeline sc_pipeline;
                                        hosts, very slow host reads (write-only use) */
 #define SC_PIPE_PER_LAYER 0x4u /* always restore layer by layer (no block stages); for
                                   comparisons and tests */
+#define SC_PIPE_SPLIT_KV_COPIES 0x8u /* block stages move a run's K and V codes as two 2-D copies
+                                        (the form a slab beyond the device's copy pitch takes)
+                                        instead of one 3-D copy; for comparisons and tests */
 
 SC_API int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t n_blocks,
                            int32_t chunk_size, int32_t n_heads, int32_t head_dim,

@@ -41,6 +41,7 @@ SC_STATUS_BAD_OUT_OFFSET = 0x4
 SC_PIPE_NUMA_LOCAL = 0x1
 SC_PIPE_WRITE_COMBINED = 0x2
 SC_PIPE_PER_LAYER = 0x4
+SC_PIPE_SPLIT_KV_COPIES = 0x8
 
 SC_IPC_HANDLE_BYTES = 64
 

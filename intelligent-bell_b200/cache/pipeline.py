@@ -46,13 +46,16 @@ class KVRestorePipeline:
             one block): per stage one 3-D copy per run of consecutive block ids and one launch
             for every layer, so a scattered block list costs one copy per run; a restore that
             fits one stage is one launch.
+        split_kv_copies: move a run's K and V codes as two 2-D copies instead of one 3-D copy
+            (what a slab beyond the device's 2 GB copy pitch does anyway); for comparisons and
+            tests.
     """
 
     def __init__(self, num_layers: int, num_blocks: int, chunk_size: int, num_kv_heads: int,
                  head_dim: int, *, device: torch.device | str | int | None = None,
                  max_restore_blocks: int | None = None, n_slots: int = 2,
                  numa_local: bool = True, write_combined: bool = False,
-                 per_layer: bool = False) -> None:
+                 per_layer: bool = False, split_kv_copies: bool = False) -> None:
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device())
         device = torch.device(device if not isinstance(device, int) else f"cuda:{device}")
@@ -69,7 +72,8 @@ class KVRestorePipeline:
         handle = ctypes.c_void_p()
         flags = (_lib.SC_PIPE_NUMA_LOCAL if numa_local else 0) | (
             _lib.SC_PIPE_WRITE_COMBINED if write_combined else 0) | (
-            _lib.SC_PIPE_PER_LAYER if per_layer else 0)
+            _lib.SC_PIPE_PER_LAYER if per_layer else 0) | (
+            _lib.SC_PIPE_SPLIT_KV_COPIES if split_kv_copies else 0)
         rc = self._lib.sc_pipeline_create(device.index, self.num_layers, self.num_blocks,
                                           self.chunk_size, self.num_kv_heads, self.head_dim,
                                           self.max_restore_blocks, int(n_slots), flags,

@@ -346,7 +346,7 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
             p->stage_cap = cap;
         // One 3-D copy per run moves K and V (slices at the K -> V slab distance) where that
         // distance is within the limit too; otherwise one 2-D copy each.
-        p->stage_3d = slab_codes <= mp;
+        p->stage_3d = slab_codes <= mp && !(flags & SC_PIPE_SPLIT_KV_COPIES);
     }
     const size_t slot_bytes = p->stage_cap > 0
                                   ? static_cast<size_t>(p->stage_cap) * 2 * n_layers * blk_codes

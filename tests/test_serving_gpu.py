@@ -189,13 +189,16 @@ def test_single_stage_restore_equals_per_layer(scb, oracle, n_blocks):
         assert bits_equal(outs[0][1][layer], outs[1][1][layer])
 
 
-def test_block_stage_restore_equals_per_layer(scb, oracle):
+@pytest.mark.parametrize("n_slots,split", [(2, False), (1, False), (2, True)])
+def test_block_stage_restore_equals_per_layer(scb, oracle, n_slots, split):
     # a restore beyond one stage (64 MiB of codes over all layers: 56 blocks here) goes in
     # block stages, here 35, 34 and 1 blocks: one 3-D copy per run of blocks within a stage (a
     # run that crosses a stage boundary is split), one launch per stage, the stages rotating
     # over two slots.  Three restores back to back (each reuses the slots and the scales), the
     # last a fully scattered list (every block its own run, in stages of 40, 39 and 1); all
-    # must write exactly what the layer-by-layer path writes.
+    # must write exactly what the layer-by-layer path writes.  Also with one slot (each stage's
+    # copy waits for the kernel of the stage before) and with each run's K and V as two 2-D
+    # copies (the form a slab beyond the device's copy pitch takes).
     from speccache_b200.cache import KVRestorePipeline
 
     layers, blocks, chunk, h, d = 9, 80, 64, 8, 128
@@ -210,7 +213,8 @@ def test_block_stage_restore_equals_per_layer(scb, oracle):
         cases.append((ids, dps, theta, dt))
     outs = []
     for per_layer in (False, True):
-        with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV, per_layer=per_layer) as pipe:
+        with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV, per_layer=per_layer,
+                               n_slots=n_slots, split_kv_copies=split) as pipe:
             g2 = torch.Generator().manual_seed(101)
             for t in (pipe.k_quant, pipe.v_quant):
                 t.copy_(torch.randint(-127, 128, tuple(t.shape), generator=g2, dtype=torch.int8))
@@ -222,8 +226,10 @@ def test_block_stage_restore_equals_per_layer(scb, oracle):
             # the first list is 6 runs; its stages hold 2, 5 and 1 of them.  Staged: 3
             # launches + the scale gather, the metadata upload + 8 code copies; layer by
             # layer: 9 launches, the upload + 6 scale copies + 9 x 6 code copies
-            assert pipe.restore_plan(cases[0][0]) == ((9, 61) if per_layer else (4, 9))
-            assert pipe.restore_plan([3, 4, 5, 6]) == ((9, 11) if per_layer else (1, 3))
+            assert pipe.restore_plan(cases[0][0]) == ((9, 61) if per_layer else
+                                                     (4, 17) if split else (4, 9))
+            assert pipe.restore_plan([3, 4, 5, 6]) == ((9, 11) if per_layer else
+                                                       (1, 4) if split else (1, 3))
             # offloads: K and V quantize + the codes' and scales' scatter for 80 single runs;
             # one run: two copies (codes; scales)
             assert pipe.offload_plan(cases[2][0]) == (4, 0)

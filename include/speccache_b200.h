@@ -245,7 +245,8 @@ SC_API int32_t sc_restore_paged(int32_t n_requests, int32_t max_pages, int32_t p
  * one restore kernel for the stage's blocks of every layer on compute_stream once its copy
  * event has fired, so stage s+1's copy overlaps stage s's kernel.  Every copy command costs a
  * few microseconds of copy-engine time beyond its bytes, so a block list in r runs costs
- * about r + stages commands.  A restore that fits one stage is one launch.  With
+ * about r + stages commands.  A restore of fewer than 8 blocks that fits one stage is one
+ * launch; from 8 blocks on the last block has a stage of its own.  With
  * SC_PIPE_PER_LAYER (or where a copy pitch exceeds the device's limit) it goes layer by
  * layer instead: per layer and run one 2-D copy of the K and V codes, one launch per layer.
  */
@@ -321,8 +322,8 @@ SC_API int32_t sc_pipeline_join(sc_pipeline* p, void* stream);
 SC_API int32_t sc_pipeline_status(sc_pipeline* p, int32_t* status_bits);
 
 /* How sc_pipeline_restore would run a restore of n_blocks blocks: the kernel launches it
- * issues (one per block stage: 1 for a restore that fits one stage; one per layer when the
- * stages are off) into *launches.  No device work.  No counterpart in the reference (it
+ * issues (one per block stage: 1 for a restore of fewer than 8 blocks that fits one stage;
+ * one per layer when the stages are off) into *launches.  No device work.  No counterpart in the reference (it
  * launches two kernels per chunk and layer). */
 SC_API int32_t sc_pipeline_restore_launches(const sc_pipeline* p, int32_t n_blocks,
                                             int32_t* launches);

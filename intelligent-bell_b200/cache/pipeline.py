@@ -44,8 +44,8 @@ class KVRestorePipeline:
         per_layer: always restore layer by layer.  By default a restore goes in stages of
             its block list (up to 64 MiB of K and V codes over all layers each, the last stage
             one block): per stage one 3-D copy per run of consecutive block ids and one launch
-            for every layer, so a scattered block list costs one copy per run; a restore that
-            fits one stage is one launch.
+            for every layer, so a scattered block list costs one copy per run; a restore of
+            fewer than 8 blocks that fits one stage is one launch.
         split_kv_copies: move a run's K and V codes as two 2-D copies instead of one 3-D copy
             (what a slab beyond the device's 2 GB copy pitch does anyway); for comparisons and
             tests.
@@ -224,7 +224,7 @@ class KVRestorePipeline:
 
     def restore_launches(self, n_blocks: int) -> int:
         """Kernel launches a restore of ``n_blocks`` blocks issues: one per block stage (1
-        when it fits one stage), one per layer with ``per_layer``."""
+        below 8 blocks when they fit one stage), one per layer with ``per_layer``."""
         count = ctypes.c_int32(0)
         _lib.check(self._lib.sc_pipeline_restore_launches(self._h, int(n_blocks), ctypes.byref(count)),
                    "sc_pipeline_restore_launches")

@@ -21,8 +21,8 @@
 //     launch restores the stage, the layers being its requests.  A restore of n blocks in r
 //     runs costs about r + stages copy commands, so a scattered block list costs one copy
 //     per run rather than one per run and layer.  The last stage is one block, so that only
-//     its kernel remains after the last copy; a restore that fits one stage is one copy per
-//     run and one launch;
+//     its kernel remains after the last copy; a restore of fewer than 8 blocks that fits one
+//     stage is one copy per run and one launch;
 //   * an event per slot joins the transfer stream to the caller's compute stream; a second
 //     event per slot releases the slot for stage s + n_slots;
 //   * layer by layer (SC_PIPE_PER_LAYER, or where a pitch exceeds the device's limit): per
@@ -38,6 +38,7 @@
 // polls events with a deadline.
 #include <errno.h>
 #include <sched.h>
+#include <sys/prctl.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -57,23 +58,28 @@ struct Meta {  // one upload per restore: identity-table length and per-block sh
     float delta_p[1];  // [max_restore_blocks]
 };
 
-// K and V codes of one block stage (all layers) in a slot.  A restore that fits one stage is
-// one copy per run and one kernel launch (per-layer launches and events cost about 8 us of
-// host time per layer, more than the copies of a restore of a few blocks take).
+// K and V codes of one block stage (all layers) in a slot.  A small restore is one copy per
+// run and one kernel launch (per-layer launches and events cost about 8 us of host time per
+// layer, more than the copies of a restore of a few blocks take).
 constexpr size_t kStageBytes = size_t(64) << 20;
 // Block stages are off where one block's codes over all layers exceed this (a slot holds at
 // least one block).
 constexpr size_t kMaxStageBytes = size_t(256) << 20;
 
-// Blocks per stage of an n-block restore with at most `cap` blocks per stage: one stage if
-// n <= cap; otherwise the last stage is one block (its kernel is the only one left after the
-// last copy; every other stage's kernel runs while the next stage's copy, tens of times
-// longer, is in flight) and the n - 1 blocks before it go in as few stages of at most cap
-// blocks as possible, of nearly equal size.
+// Restores of fewer blocks than this that fit one stage stay one stage; from this many on,
+// the last block gets its own stage.
+constexpr int64_t kSplitLastMin = 8;
+
+// Blocks per stage of an n-block restore with at most `cap` blocks per stage.  The last stage
+// is one block: its kernel is the only one left after the last copy, while every other
+// stage's kernel runs under the next stage's copy (tens of times longer).  The n - 1 blocks
+// before it go in as few stages of at most cap blocks as possible, of nearly equal size.  A
+// restore of fewer than kSplitLastMin blocks that fits one stage is one stage: there the
+// extra copy command and launch cost about what the shorter tail saves.
 void stage_sizes(int64_t n, int64_t cap, std::vector<int32_t>& out) {
     out.clear();
     if (n <= 0) return;
-    if (n <= cap) {
+    if (n <= cap && (n < kSplitLastMin || cap < 2)) {
         out.push_back(static_cast<int32_t>(n));
         return;
     }
@@ -610,7 +616,8 @@ extern "C" int32_t sc_pipeline_restore_launches(const sc_pipeline* p, int32_t n_
                          (long long)p->max_blocks);
     if (n_blocks == 0)
         *launches = 0;
-    else if (p->stage_cap > 0 && n_blocks <= p->stage_cap)
+    else if (p->stage_cap > 0 && n_blocks <= p->stage_cap &&
+             (n_blocks < kSplitLastMin || p->stage_cap < 2))
         *launches = 1;
     else if (p->stage_cap > 0)  // the stages of stage_sizes(): the front ones and a last block
         *launches = static_cast<int32_t>((n_blocks - 1 + p->stage_cap - 1) / p->stage_cap + 1);
@@ -913,10 +920,26 @@ extern "C" int32_t sc_pipeline_offload(sc_pipeline* p, int32_t layer, const int3
 }
 
 namespace {
-// Polls without sleeping for the first millisecond (a sleep of 50 us takes 50-100 us more
-// with the kernel's default timer slack, longer than a small restore), then every 50 us.
+// Holds the calling thread's timer slack at 1 us for the scope: with the default 50 us slack a
+// short sleep returns 50-100 us late, which restores of a few milliseconds would see as
+// latency.  The previous slack is put back on exit.
+struct TightTimerSlack {
+    long prev = -1;
+    TightTimerSlack() {
+        prev = prctl(PR_GET_TIMERSLACK, 0, 0, 0, 0);
+        if (prev > 0) prctl(PR_SET_TIMERSLACK, 1000UL, 0, 0, 0);
+    }
+    ~TightTimerSlack() {
+        if (prev > 0) prctl(PR_SET_TIMERSLACK, static_cast<unsigned long>(prev), 0, 0, 0);
+    }
+};
+
+// Polls without sleeping for the first millisecond, then every 20 us with a 1 us timer slack
+// (measured on the GPU hosts: with 50 us sleeps at the default slack, a 1.3 ms restore's
+// completion was seen 50-110 us late).
 int32_t wait_event(cudaEvent_t ev, double deadline, double timeout_s, const char* what) {
     const double spin_until = now_s() + 1e-3;
+    TightTimerSlack slack;
     for (;;) {
         const cudaError_t e = cudaEventQuery(ev);
         if (e == cudaSuccess) return SC_OK;
@@ -927,7 +950,7 @@ int32_t wait_event(cudaEvent_t ev, double deadline, double timeout_s, const char
         if (t < spin_until)
             sched_yield();
         else
-            usleep(50);
+            usleep(20);
     }
 }
 }  // namespace

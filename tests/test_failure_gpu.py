@@ -130,7 +130,7 @@ def test_preloaded_first_calls_do_not_wait_for_the_device(scb):
 # (here 90-98 blocks of 64 tokens x 8 heads over 6 layers, 85 blocks per stage: stages of
 # 44-49, 44-48 and 1 blocks over two slots), and layer by layer.
 PATHS = {
-    "single_stage": dict(blocks=12, chunk=32, h=4, per_layer=False, n=(1, 8)),
+    "single_stage": dict(blocks=12, chunk=32, h=4, per_layer=False, n=(1, 7)),
     "block_stages": dict(blocks=100, chunk=64, h=8, per_layer=False, n=(90, 98)),
     "per_layer": dict(blocks=12, chunk=32, h=4, per_layer=True, n=(1, 8)),
 }

@@ -145,10 +145,12 @@ def test_offload_then_restore_round_trip(scb, oracle):
     inj.close()
 
 
-@pytest.mark.parametrize("n_blocks", [1, 3, 7])
-def test_single_stage_restore_equals_per_layer(scb, oracle, n_blocks):
-    # a small restore fits one block stage (one 3-D copy per run, one launch); it must write
-    # exactly what the layer-by-layer path writes, scattered and consecutive blocks alike
+@pytest.mark.parametrize("n_blocks", [1, 3, 7, 12])
+def test_small_restore_equals_per_layer(scb, oracle, n_blocks):
+    # a restore that fits one stage: below 8 blocks one stage (one 3-D copy per run, one
+    # launch), from 8 blocks on the last block in a stage of its own (12 blocks: stages of 11
+    # and 1); it must write exactly what the layer-by-layer path writes, scattered and
+    # consecutive blocks alike
     from speccache_b200.cache import KVRestorePipeline
 
     layers, blocks, chunk, h, d = 5, 12, 32, 4, 128
@@ -166,9 +168,11 @@ def test_single_stage_restore_equals_per_layer(scb, oracle, n_blocks):
             for t in (pipe.k_scale, pipe.v_scale):
                 t.copy_((torch.rand(tuple(t.shape), generator=g2) * 0.05 + 1e-3).half())
             # model-layout outputs: [1, H, Tmax, D] per layer, separate allocations
-            kc = [torch.zeros((1, h, 256, d), dtype=torch.bfloat16, device=DEV) for _ in range(layers)]
+            kc = [torch.zeros((1, h, 512, d), dtype=torch.bfloat16, device=DEV) for _ in range(layers)]
             vc = [torch.zeros_like(x) for x in kc]
             n_tok = n_blocks * chunk
+            assert pipe.restore_launches(n_blocks) == (
+                layers if per_layer else 2 if n_blocks >= 8 else 1)
             pipe.restore(ids, dps, [x[0, :, 16:16 + n_tok].permute(1, 0, 2) for x in kc],
                          [x[0, :, 16:16 + n_tok].permute(1, 0, 2) for x in vc], theta=5e5)
             pipe.synchronize()
@@ -258,9 +262,9 @@ def test_block_stage_restore_equals_per_layer(scb, oracle, n_slots, split):
 
 def stage_count(n, cap):
     """Launches of a block-stage restore of n blocks with at most cap blocks per stage: one
-    stage, or as few front stages of at most cap blocks as hold n - 1 blocks plus a last
-    one-block stage."""
-    return 1 if n <= cap else -(-(n - 1) // cap) + 1
+    stage below 8 blocks when they fit, else as few front stages of at most cap blocks as
+    hold n - 1 blocks plus a last one-block stage."""
+    return 1 if n <= cap and (n < 8 or cap < 2) else -(-(n - 1) // cap) + 1
 
 
 @pytest.mark.parametrize("seed", range(6))

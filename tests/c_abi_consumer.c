@@ -4,14 +4,19 @@
  *
  * It quantizes seeded float32 K and V [T, H, D] on the GPU (sc_quantize_int8, fp16 scales),
  * restores them (sc_dequant_rope_kv: K shifted by delta_p with the cos/sin table built by the
- * library, V plain, fp16 out, one launch), checks a rejected call's status and message, and
- * writes inputs and outputs to a file that the Python test compares with the oracle.
+ * library, V plain, fp16 out, one launch), checks a rejected call's status and message, then
+ * drives the pinned-host pipeline the way an engine binding would (sc_pipeline_create, the
+ * slabs filled through sc_pipeline_host_slabs, sc_pipeline_plan, sc_pipeline_restore of a
+ * scattered block list, sc_pipeline_synchronize, sc_pipeline_status), and writes inputs and
+ * outputs to a file that the Python test compares with the oracle.
  *
  *   c_abi_consumer <out.bin> <T> <H> <D> <delta_p> <theta>
  *
  * File layout (little endian): int32 T, H, D; float64 delta_p, theta; then float32 xk[T*H*D],
  * xv[T*H*D]; int8 kq[T*H*D], vq[T*H*D]; uint16 ks[T*H], vs[T*H]; uint16 ko[T*H*D], vo[T*H*D]
- * (fp16 bit patterns).
+ * (fp16 bit patterns).  Then the pipeline: int32 L, B, C, PH, PD, n, launches, copies; int32
+ * ids[n], shifts[n]; int8 K and V code slabs [L*B*C*PH*PD] each; uint16 K and V scale slabs
+ * [L*B*C*PH] each; uint16 K and V outputs [L*n*C*PH*PD] each.
  */
 #include <stdio.h>
 #include <stdlib.h>
@@ -135,7 +140,68 @@ int main(int argc, char** argv) {
               write_all(f, xk, n * 4) | write_all(f, xv, n * 4) | write_all(f, kq, n) |
               write_all(f, vq, n) | write_all(f, ks, rows * 2) | write_all(f, vs, rows * 2) |
               write_all(f, ko, n * 2) | write_all(f, vo, n * 2);
+    if (bad) return 8;
+
+    /* The pipeline: 3 layers x 12 blocks of 16 tokens x 2 heads x 64, fp16 out.  Nine scattered
+     * blocks in six runs: the scales come by the gather kernel, and from eight blocks on the
+     * last block has a stage of its own (two launches). */
+    enum { PL = 3, PB = 12, PC = 16, PH = 2, PD = 64, PN = 9 };
+    const int32_t ids[PN] = {4, 0, 1, 5, 9, 10, 11, 2, 7};
+    const int32_t shifts[PN] = {-300, 12, 12, 4000, -7, 0, 65000, 1, -4096};
+    const size_t slab = (size_t)PL * PB * PC * PH * PD, slab_s = (size_t)PL * PB * PC * PH;
+    const size_t per_layer = (size_t)PN * PC * PH * PD;
+    sc_pipeline* pipe = NULL;
+    CHECK_SC(sc_pipeline_create(0, PL, PB, PC, PH, PD, PB, 2, 0, &pipe));
+    int8_t *h_kq, *h_vq;
+    void *h_ks, *h_vs;
+    CHECK_SC(sc_pipeline_host_slabs(pipe, &h_kq, &h_ks, &h_vq, &h_vs));
+    for (size_t i = 0; i < slab; ++i) h_kq[i] = (int8_t)((int)(next_value(&state) * 31.75f));
+    for (size_t i = 0; i < slab; ++i) h_vq[i] = (int8_t)((int)(next_value(&state) * 31.75f));
+    /* fp16 scales (1 + m/1024) * 2^-8: exponent field 7, mantissa m */
+    for (size_t i = 0; i < slab_s; ++i)
+        ((uint16_t*)h_ks)[i] = (uint16_t)(0x1C00u | ((unsigned)((next_value(&state) + 4.0f) * 128.0f) & 1023u));
+    for (size_t i = 0; i < slab_s; ++i)
+        ((uint16_t*)h_vs)[i] = (uint16_t)(0x1C00u | ((unsigned)((next_value(&state) + 4.0f) * 128.0f) & 1023u));
+    int32_t launches = 0, copies = 0;
+    CHECK_SC(sc_pipeline_plan(pipe, 0, ids, PN, &launches, &copies));
+    void* d_pk[PL];
+    void* d_pv[PL];
+    for (int l = 0; l < PL; ++l) {
+        CHECK_CUDA(cudaMalloc(&d_pk[l], per_layer * 2));
+        CHECK_CUDA(cudaMalloc(&d_pv[l], per_layer * 2));
+    }
+    const int64_t out_st[3] = {(int64_t)PH * PD, PD, 1};
+    CHECK_SC(sc_pipeline_restore(pipe, ids, shifts, PN, theta, NULL, d_pk, d_pv, out_st,
+                                 (int64_t)per_layer, SC_DTYPE_F16, stream));
+    CHECK_SC(sc_pipeline_synchronize(pipe, 30.0));
+    CHECK_CUDA(cudaStreamSynchronize(stream));
+    int32_t status = -1;
+    CHECK_SC(sc_pipeline_status(pipe, &status));
+    if (status != 0) {
+        fprintf(stderr, "pipeline status %d\n", status);
+        return 9;
+    }
+    uint16_t* pko = malloc(PL * per_layer * 2);
+    uint16_t* pvo = malloc(PL * per_layer * 2);
+    if (!pko || !pvo) return 5;
+    for (int l = 0; l < PL; ++l) {
+        CHECK_CUDA(cudaMemcpy(pko + l * per_layer, d_pk[l], per_layer * 2, cudaMemcpyDeviceToHost));
+        CHECK_CUDA(cudaMemcpy(pvo + l * per_layer, d_pv[l], per_layer * 2, cudaMemcpyDeviceToHost));
+    }
+    const int32_t pgeo[8] = {PL, PB, PC, PH, PD, PN, launches, copies};
+    bad = write_all(f, pgeo, sizeof pgeo) | write_all(f, ids, sizeof ids) |
+          write_all(f, shifts, sizeof shifts) | write_all(f, h_kq, slab) | write_all(f, h_vq, slab) |
+          write_all(f, h_ks, slab_s * 2) | write_all(f, h_vs, slab_s * 2) |
+          write_all(f, pko, PL * per_layer * 2) | write_all(f, pvo, PL * per_layer * 2);
     bad |= fclose(f) != 0;
+    printf("pipeline: %d launches, %d copies\n", launches, copies);
+    for (int l = 0; l < PL; ++l) {
+        cudaFree(d_pk[l]);
+        cudaFree(d_pv[l]);
+    }
+    free(pko);
+    free(pvo);
+    CHECK_SC(sc_pipeline_destroy(pipe));
 
     CHECK_CUDA(cudaStreamDestroy(stream));
     cudaFree(d_xk);

@@ -5,7 +5,10 @@ in its process, built with gcc against include/speccache_b200.h and the in-tree 
   exported symbols.
 * GPU: the consumer quantizes seeded fp32 K/V, restores them with an in-library shift table
   and writes everything to a file; codes and scales must equal the oracle's bit for bit, V
-  too, and K must lie within the reference tolerance (rtol = atol = 1e-2).
+  too, and K must lie within the reference tolerance (rtol = atol = 1e-2).  It then restores 9
+  scattered blocks of a 3-layer pinned-host pipeline whose slabs it filled from C; every layer
+  is checked against the oracle the same way, and the plan it read must be 3 launches (two
+  block stages and the scale gather) and 7 copy commands.
 """
 
 from __future__ import annotations
@@ -57,7 +60,26 @@ def _read(path):
         a = np.frombuffer(raw, dtype, count, off).copy()
         off += a.nbytes
         out[name] = torch.from_numpy(a)
+    # the pipeline section
+    pl, pb, pc, ph, pd, pn, launches, copies = (int(x) for x in np.frombuffer(raw, np.int32, 8, off))
+    off += 32
+    pipe = {"geo": (pl, pb, pc, ph, pd), "launches": launches, "copies": copies}
+    slab, slab_s, outs = pl * pb * pc * ph * pd, pl * pb * pc * ph, pl * pn * pc * ph * pd
+    for name, dtype, count in (("ids", np.int32, pn), ("shifts", np.int32, pn),
+                               ("kq", np.int8, slab), ("vq", np.int8, slab),
+                               ("ks", np.int16, slab_s), ("vs", np.int16, slab_s),
+                               ("ko", np.int16, outs), ("vo", np.int16, outs)):
+        a = np.frombuffer(raw, dtype, count, off).copy()
+        off += a.nbytes
+        pipe[name] = torch.from_numpy(a)
     assert off == len(raw)
+    for k in ("kq", "vq"):
+        pipe[k] = pipe[k].view(pl, pb, pc, ph, pd)
+    for k in ("ks", "vs"):
+        pipe[k] = pipe[k].view(torch.float16).view(pl, pb, pc, ph, 1)
+    for k in ("ko", "vo"):
+        pipe[k] = pipe[k].view(torch.float16).view(pl, pn * pc, ph, pd)
+    out["pipeline"] = pipe
     shape, sshape = (int(t), int(h), int(d)), (int(t), int(h), 1)
     for k in ("xk", "xv", "kq", "vq", "ko", "vo"):
         out[k] = out[k].view(shape)
@@ -89,3 +111,11 @@ def test_consumer_restores_like_the_oracle(scb, oracle, tmp_path, geo):
     k_ref = oracle.dequant_rope_shift(r["kq"], r["ks"], cos, sin)
     torch.testing.assert_close(r["ko"], k_ref, rtol=1e-2, atol=1e-2)
     assert bits_equal(r["vo"], oracle.dequant_value(r["vq"], r["vs"]))
+    pipe = r["pipeline"]
+    assert (pipe["launches"], pipe["copies"]) == (3, 7)
+    ids, shifts = pipe["ids"].tolist(), pipe["shifts"].tolist()
+    for layer in range(pipe["geo"][0]):
+        kr, vr = oracle.restore_blocks(pipe["kq"][layer], pipe["ks"][layer], pipe["vq"][layer],
+                                       pipe["vs"][layer], ids, shifts, theta, torch.float16)
+        assert bits_equal(pipe["vo"][layer], vr), layer
+        torch.testing.assert_close(pipe["ko"][layer], kr, rtol=1e-2, atol=1e-2)

@@ -39,6 +39,14 @@ void host_cos_sin_table(int head_dim, float dp, double theta, const float* inv_f
 // kernel parameter of head_dim/2 floats).
 constexpr int kMaxHeadDim = 1024;
 
+// a * b * c of non-negative sizes, or INT64_MAX when the product does not fit: a caller's
+// absurd sizes then fail the size limits instead of wrapping past them.
+inline int64_t size_product(int64_t a, int64_t b, int64_t c = 1) {
+    int64_t ab = 0, abc = 0;
+    if (__builtin_mul_overflow(a, b, &ab) || __builtin_mul_overflow(ab, c, &abc)) return INT64_MAX;
+    return abc;
+}
+
 // Paged restore launch shared by sc_restore_paged and the host pipeline.
 struct PagedArgs {
     int32_t n_requests, max_pages, page_size, n_heads, head_dim;

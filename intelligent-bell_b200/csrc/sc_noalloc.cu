@@ -75,7 +75,9 @@ extern "C" int32_t sc_dequant_rope_kv_token_shifts_noalloc(
     if (scale_dtype != SC_DTYPE_F16 && scale_dtype != SC_DTYPE_F32)
         return sc::set_error(SC_ERR_INVALID_DTYPE, "scale dtype code %d: float16 or float32 only",
                              scale_dtype);
-    const int64_t entries = n_tokens * (head_dim / 2);
+    // An entry count is at least n_tokens (head_dim >= 2), so this bound comes first and the
+    // product below cannot overflow.
+    const int64_t entries = n_tokens > kMaxEntries ? kMaxEntries + 1 : n_tokens * (head_dim / 2);
     if (entries > kMaxEntries)
         return sc::set_error(SC_ERR_INVALID_ARGUMENT,
                              "n_tokens * head_dim / 2 = %lld exceeds the fixed table capacity of "
@@ -90,7 +92,7 @@ extern "C" int32_t sc_dequant_rope_kv_token_shifts_noalloc(
         return sc::set_error(SC_ERR_INVALID_ARGUMENT, "K given without its scale/output/strides");
     if (v_quant && (!v_scale || !v_out || !vq_strides || !vs_strides || !vo_strides))
         return sc::set_error(SC_ERR_INVALID_ARGUMENT, "V given without its scale/output/strides");
-    if (static_cast<int64_t>(n_layers) * n_tokens * n_heads >= (int64_t(1) << 31))
+    if (sc::size_product(n_layers, n_tokens, n_heads) >= (int64_t(1) << 31))
         return sc::set_error(SC_ERR_INVALID_ARGUMENT, "too many rows in one call; split it below 2^31");
     if (n_layers == 0 || n_tokens == 0 || n_heads == 0) return sc::ok();
     void* tables = nullptr;

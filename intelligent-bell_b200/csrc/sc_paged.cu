@@ -385,7 +385,7 @@ int32_t launch_paged(const PagedArgs& a) {
     const int64_t rows_per_block = static_cast<int64_t>(kPThreads / (a.head_dim / 32)) * SC_PAGED_ROUNDS;
     const int64_t chunks = (static_cast<int64_t>(a.page_size) * a.n_heads + rows_per_block - 1) /
                            rows_per_block;
-    if (static_cast<int64_t>(a.n_requests) * a.max_pages * chunks >= (int64_t(1) << 31))
+    if (size_product(a.n_requests, a.max_pages, chunks) >= (int64_t(1) << 31))
         return set_error(SC_ERR_INVALID_ARGUMENT, "too many (request, page) blocks in one call");
 
     PagedParams p{};

@@ -276,6 +276,15 @@ extern "C" int32_t sc_pipeline_create(int32_t device, int32_t n_layers, int64_t 
                          sc::kMaxHeadDim);
     if (max_restore_blocks >= (int64_t(1) << 31) / chunk_size)
         return set_error(SC_ERR_INVALID_ARGUMENT, "max_restore_blocks too large");
+    // Block ids are int32, and the slabs' codes must stay well inside size_t: sizes off by
+    // orders of magnitude fail here instead of wrapping into a small allocation.
+    if (n_blocks >= (int64_t(1) << 31) || n_slots > 64 ||
+        sc::size_product(sc::size_product(n_layers, n_blocks, chunk_size), n_heads, head_dim) >=
+            (int64_t(1) << 44))
+        return set_error(SC_ERR_INVALID_ARGUMENT,
+                         "pipeline too large (layers=%d blocks=%lld chunk=%d heads=%d "
+                         "head_dim=%d slots=%d)",
+                         n_layers, (long long)n_blocks, chunk_size, n_heads, head_dim, n_slots);
     auto* p = new sc_pipeline();
     p->device = device;
     p->L = n_layers;

@@ -423,7 +423,7 @@ extern "C" int32_t sc_quantize_int8(int64_t n_tokens, int32_t n_heads, int32_t h
     if (scale_dtype != SC_DTYPE_F16 && scale_dtype != SC_DTYPE_F32)
         return set_error(SC_ERR_INVALID_DTYPE, "scale dtype code %d: float16 or float32",
                          scale_dtype);
-    const int64_t rows = n_tokens * n_heads;
+    const int64_t rows = size_product(n_tokens, n_heads);
     if (rows >= (int64_t(1) << 31))
         return set_error(SC_ERR_INVALID_ARGUMENT, "%lld rows; split the call below 2^31",
                          (long long)rows);

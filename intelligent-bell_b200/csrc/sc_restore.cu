@@ -546,7 +546,9 @@ extern "C" int32_t sc_rope_cos_sin_delta(const float* delta_pos, int64_t n, int3
     p.D = head_dim;
     fill_inv_freq(p, head_dim, theta_base, inv_freq);
     const int half = head_dim / 2;
-    const int64_t total = n * half;
+    const int64_t total = size_product(n, half);
+    if (total >= (int64_t(1) << 40))
+        return set_error(SC_ERR_INVALID_ARGUMENT, "n = %lld table rows is too many", (long long)n);
     const int64_t need = (total + kThreads - 1) / kThreads;
     const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
     const int grid = static_cast<int>(need < cap ? need : cap);
@@ -595,7 +597,7 @@ extern "C" int32_t sc_dequant_rope_kv(
     if (scale_dtype != SC_DTYPE_F16 && scale_dtype != SC_DTYPE_F32)
         return set_error(SC_ERR_INVALID_DTYPE, "scale dtype code %d: float16 or float32 only",
                          scale_dtype);
-    const int64_t rows = static_cast<int64_t>(n_layers) * n_tokens * n_heads;
+    const int64_t rows = size_product(n_layers, n_tokens, n_heads);
     if (rows == 0) return ok();  // empty tensors may carry null pointers
     const bool has_k = k_quant != nullptr, has_v = v_quant != nullptr;
     if (!has_k && !has_v) return set_error(SC_ERR_INVALID_ARGUMENT, "neither K nor V given");

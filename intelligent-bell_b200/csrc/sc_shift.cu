@@ -245,7 +245,7 @@ extern "C" int32_t sc_rope_shift_keys(int64_t n_tokens, int32_t n_heads, int32_t
     for (int32_t dt : {x_dtype, out_dtype})
         if (dt != SC_DTYPE_F16 && dt != SC_DTYPE_BF16)
             return set_error(SC_ERR_INVALID_DTYPE, "key dtype code %d: float16 or bfloat16", dt);
-    const int64_t rows = n_tokens * n_heads;
+    const int64_t rows = size_product(n_tokens, n_heads);
     if (rows >= (int64_t(1) << 31) / (head_dim > 2 ? head_dim / 2 : 1))
         return set_error(SC_ERR_INVALID_ARGUMENT, "%lld rows in one call; split it",
                          (long long)rows);

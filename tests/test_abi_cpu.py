@@ -104,6 +104,38 @@ def test_paged_rejects_bad_arguments(scb):
     assert call(table_stride=3) == scb._lib.SC_ERR_INVALID_ARGUMENT
 
 
+def test_sizes_whose_products_overflow_are_rejected_before_cuda(scb):
+    # sizes whose products do not fit in 64 bits are refused, not wrapped: 8 x 2^61 rows once
+    # wrapped to 0 rows and the call returned success without doing anything
+    lib = scb._lib.load()
+    st = scb._lib.strides
+    bad = scb._lib.SC_ERR_INVALID_ARGUMENT
+    s4, s3 = st(0, 8 * 64, 64, 1), st(0, 8, 1)
+    rc = lib.sc_dequant_rope_kv(8, 2 ** 61, 1, 64, 16, s4, 16, s3, None, None, None, None, 0,
+                                None, None, None, 0.0, None, 1e4, None, 16, s4, None, None,
+                                0, 0, None)
+    assert rc == bad and "rows" in _err(lib)
+    rc = lib.sc_quantize_int8(2 ** 62, 8, 64, 16, 0, st(512, 64, 1), 1e-5, 16, st(512, 64, 1),
+                              16, 0, st(8, 1), 0, None)
+    assert rc == bad and "rows" in _err(lib)
+    rc = lib.sc_rope_shift_keys(2 ** 62, 8, 64, 16, 0, st(512, 64, 1), None, None, None, 5.0,
+                                1e4, None, 16, 0, st(512, 64, 1), None)
+    assert rc == bad
+    rc = lib.sc_rope_cos_sin_delta(16, 2 ** 62, 64, 1e4, None, 16, 16, 0, None)
+    assert rc == bad
+    rc = lib.sc_restore_paged(2 ** 31 - 1, 2 ** 31 - 1, 64, 8, 128, 10, 16, 16, 16, 16, 16,
+                              2 ** 31 - 1, 16, 16, 0, 1e4, None, 16, 16, 16, st(1024, 128, 1),
+                              1 << 20, 0, 16, 0, None)
+    assert rc == bad
+    rc = lib.sc_dequant_rope_kv_token_shifts_noalloc(1, 2 ** 62, 8, 128, 16, s4, 16, s3, None,
+                                                     None, None, None, 0, 16, 1e4, None, 16, s4,
+                                                     None, None, 0, 0, None)
+    assert rc == bad and "capacity" in _err(lib)
+    h = ctypes.c_void_p()
+    rc = lib.sc_pipeline_create(0, 2, 2 ** 40, 64, 8, 128, 8, 2, 0, ctypes.byref(h))
+    assert rc == bad and "too large" in _err(lib) and h.value is None
+
+
 def test_pipeline_rejects_bad_geometry(scb):
     lib = scb._lib.load()
     h = ctypes.c_void_p()

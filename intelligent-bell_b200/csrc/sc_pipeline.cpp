@@ -45,6 +45,7 @@
 #include <time.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "sc_internal.h"
@@ -88,6 +89,15 @@ void stage_sizes(int64_t n, int64_t cap, std::vector<int32_t>& out) {
     for (int64_t i = 0; i < n_front; ++i)
         out.push_back(static_cast<int32_t>(front / n_front + (i < front % n_front ? 1 : 0)));
     out.push_back(1);
+}
+
+// Whether a block list names a block twice.  An offload of such a list goes by copies, in
+// list order, so the last of the duplicates wins as with the reference's block-by-block
+// writes (pinned_pool.py:275-367); the scatter kernel would write them at once.
+bool has_duplicates(const int32_t* ids, int32_t n) {
+    std::vector<int32_t> v(ids, ids + n);
+    std::sort(v.begin(), v.end());
+    return std::adjacent_find(v.begin(), v.end()) != v.end();
 }
 
 size_t meta_bytes(int64_t max_blocks) {
@@ -658,7 +668,7 @@ extern "C" int32_t sc_pipeline_plan(const sc_pipeline* p, int32_t offload,
     };
     const int32_t runs = runs_in(0, n_blocks);
     if (offload) {  // sc_pipeline_offload: quantize K and V, then scatter kernels or copies
-        if (runs > 1 && p->d_hkq && p->d_hks) {
+        if (runs > 1 && p->d_hkq && p->d_hks && !has_duplicates(block_ids, n_blocks)) {
             *launches = 2 + 2 * ((n_blocks + sc::kMaxScatterIds - 1) / sc::kMaxScatterIds);
         } else {
             *launches = 2;
@@ -871,7 +881,8 @@ extern "C" int32_t sc_pipeline_offload(sc_pipeline* p, int32_t layer, const int3
     const size_t lay_scales = static_cast<size_t>(layer) * p->B * blk_scales;
     int32_t runs = 1;
     for (int32_t i = 1; i < n_blocks; ++i) runs += block_ids[i] != block_ids[i - 1] + 1;
-    if (e == cudaSuccess && runs > 1 && p->d_hkq && p->d_hks) {
+    if (e == cudaSuccess && runs > 1 && p->d_hkq && p->d_hks &&
+        !has_duplicates(block_ids, n_blocks)) {
         // A list in several runs: one scatter kernel writes every block's K and V codes into
         // the mapped slab (rows: K, V), one its scales, on the transfer stream, instead of two
         // copy commands per run.

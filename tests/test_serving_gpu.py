@@ -393,6 +393,30 @@ def test_scattered_offload_writes_only_its_blocks(scb, oracle, chunk, h, n):
         torch.testing.assert_close(ko[1].cpu().float(), kr.float(), rtol=1e-2, atol=1e-2)
 
 
+def test_offload_of_a_repeated_block_keeps_the_last(scb, oracle):
+    # a block named twice in one offload ends with the later chunk, as the reference's
+    # block-by-block writes leave it (such a list goes by copies in list order, not by the
+    # scatter kernel, which would write both at once)
+    from speccache_b200.cache import KVRestorePipeline
+
+    layers, blocks, chunk, h, d = 2, 8, 16, 2, 64
+    ids = [3, 5, 3]
+    with KVRestorePipeline(layers, blocks, chunk, h, d, device=DEV) as pipe:
+        assert pipe.offload_plan(ids) == (2, 6)  # quantize K, V; codes + scales per run
+        assert pipe.offload_plan([3, 5, 1]) == (4, 0)  # no repeat: the scatter kernels
+        g = torch.Generator().manual_seed(5)
+        k = torch.randn((len(ids) * chunk, h, d), generator=g).half()
+        v = torch.randn((len(ids) * chunk, h, d), generator=g).half()
+        pipe.offload(0, ids, k.to(DEV), v.to(DEV))
+        pipe.synchronize()
+        assert pipe.status() == 0
+        for x, q_slab, s_slab in ((k, pipe.k_quant, pipe.k_scale), (v, pipe.v_quant, pipe.v_scale)):
+            q_ref, s_ref = oracle.quantize_kv_int8(x)
+            q_ref, s_ref = q_ref.view(3, chunk, h, d), s_ref.view(3, chunk, h, 1)
+            assert torch.equal(q_slab[0, 3], q_ref[2]) and torch.equal(q_slab[0, 5], q_ref[1])
+            assert bits_equal(s_slab[0, 3], s_ref[2]) and bits_equal(s_slab[0, 5], s_ref[1])
+
+
 def test_pool_async_dma_multi_chunk_parity(scb, oracle):
     # reference tests/test_phase2_engine.py:297-359: 4 chunks with distinct shifts
     from speccache_b200.cache import PinnedKVPool
